@@ -1,0 +1,385 @@
+"""Benchmark: FP4 MoE layer tokens/s (dispatch + FP4 GMM + combine) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE layer forward over one batch of synthetic tokens:
+route (top-8 sigmoid) -> permute -> gather -> gmm1 (SwiGLU) -> gmm2 ->
+combine. At N=1 the workload is BASELINE config 1 (T=64 tokens, H=4096,
+I=2048, E=256 FP4 experts with E8M0 scales); N>1 runs the same per-rank batch
+(weak scaling). The weights (3.3 GB) exceed L2, so every step streams them
+from HBM.
+
+Printed (rank 0, one JSON line): value (device-timed, inputs resident), e2e
+(public API with pinned host buffers, copies inside the timed region),
+roofline of the dominant kernel (dw_moe gmm_fp4, timed with CUDA events on its
+stream), the CPU baseline (the NumPy oracle on the host cores, bounded
+sample), clocks sampled during the timed region and the kernel launch count.
+
+``--impl reference`` times the reference semantics on the host instead (the
+reference's JAX/Pallas path cannot run here; its NumPy restatement in
+oracle/ is the CPU reference) and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE layer tokens/s (dispatch+FP4 GMM+combine)"
+UNIT = "tokens/s"
+T_RANK, H, I, E, TOPK = 64, 4096, 2048, 256, 8
+WORKLOAD = "cfg1 decode MoE layer: T=64/rank, H=4096, I=2048, E=256 FP4 experts, top-8 sigmoid"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-experts", type=int, default=6,
+                   help="experts whose GEMMs the CPU baseline times (then scaled)")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the oracle on the host cores (bounded sample)
+# ----------------------------------------------------------------------------
+
+def cpu_baseline(seed: int, n_experts_sample: int):
+    """Time the reference semantics on the host for the cfg1 layer: routing,
+    permute, gather and combine for all 64 tokens, and both GEMMs (FP4
+    dequant + f64 matmul + SwiGLU) for ``n_experts_sample`` of the active
+    experts, scaled to all active experts."""
+    import torch
+    from oracle import moe_oracle as O
+    from dw_tpu_b200 import synthetic
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, router = synthetic.layer_inputs(T_RANK, H, E, seed=seed)
+    xs = O.bf16_bits_to_f32(x.view(torch.int16).numpy().view(np.uint16))
+    logits = O.round_bf16((xs @ O.bf16_bits_to_f32(
+        router.view(torch.int16).numpy().view(np.uint16))).astype(np.float32))
+    rng = np.random.default_rng(seed)
+    t0 = time.perf_counter()
+    ids, w = O.route_topk(logits, TOPK, "sigmoid", True)
+    _, tok, revert, gs = O.permute(ids, E)
+    xg = O.dispatch_gather(xs, tok)
+    t_route = time.perf_counter() - t0
+    active = np.nonzero(gs)[0]
+    sample = active[:n_experts_sample]
+    starts = np.concatenate([[0], np.cumsum(gs)[:-1]])
+    y = np.zeros((xg.shape[0], H), np.float32)
+    t0 = time.perf_counter()
+    for ex in sample:
+        w13 = rng.integers(0, 256, (H, I), dtype=np.uint8)
+        s13 = rng.integers(123, 130, (H // 32, 2 * I), dtype=np.uint8)
+        w2 = rng.integers(0, 256, (I, H // 2), dtype=np.uint8)
+        s2 = rng.integers(123, 130, (I // 32, H), dtype=np.uint8)
+        r0, r1 = starts[ex], starts[ex] + gs[ex]
+        h1 = (xg[r0:r1] @ O.dequant_fp4_block(w13, s13)).astype(np.float32)
+        a = O.round_bf16(O.silu_and_mul(h1[:, :I], h1[:, I:]))
+        y[r0:r1] = O.round_bf16((a @ O.dequant_fp4_block(w2, s2)).astype(np.float32))
+    t_gemm = (time.perf_counter() - t0) / max(1, len(sample)) * len(active)
+    t0 = time.perf_counter()
+    O.combine(y, revert, O.round_bf16(w), TOPK)
+    t_comb = time.perf_counter() - t0
+    step = t_route + t_gemm + t_comb
+    return {
+        "value": T_RANK / step,
+        "unit": UNIT,
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": (f"routing/permute/gather/combine of all {T_RANK} tokens + FP4 dequant and "
+                   f"GEMMs of {len(sample)} of {len(active)} active experts, GEMM time scaled "
+                   f"to all active experts (NumPy oracle, reference JAX path unavailable)"),
+        "seconds_per_step": step,
+    }
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def read_traffic():
+    """Per-launch DRAM bytes of gmm_fp4 from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gmm_fp4_cfg1_decode.md")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    return float(m.group(1)) if m else None
+
+
+def measured_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import ops, synthetic
+    from dw_tpu_b200 import _lib as L
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    weights = synthetic.moe_weights(E, H, I, seed=args.seed, device=dev)
+    x_cpu, router = synthetic.layer_inputs(T_RANK, H, E, seed=args.seed + 100 * rank)
+    x = x_cpu.to(dev)
+    logits = (x.float() @ router.to(dev).float()).to(torch.bfloat16)
+    layer = dw.MoELayer(weights, TOPK, T_RANK)
+    out = torch.empty((T_RANK, H), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # Warm-up (also checks the device status word once).
+    for _ in range(max(3, args.warmup)):
+        layer(x, logits, out=out)
+    torch.cuda.synchronize(dev)
+    L.raise_on_device_error()
+
+    # Timed region: K steps, events around every gmm launch for the roofline.
+    gmm_ev = []
+    orig = ops.gmm_fp4_out
+
+    def timed_gmm(*a, **kw):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r = orig(*a, **kw)
+        e1.record(stream)
+        gmm_ev.append((e0, e1, kw.get("act", L.ACT_NONE)))
+        return r
+
+    import dw_tpu_b200.fused_moe as fm
+    fm.ops.gmm_fp4_out = timed_gmm
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        start.record(stream)
+        for _ in range(args.steps):
+            layer(x, logits, out=out)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    fm.ops.gmm_fp4_out = orig
+    ms = start.elapsed_time(end)
+    gmm_ms = [(a.elapsed_time(b), act) for a, b, act in gmm_ev]
+
+    # e2e through the public API with pinned host buffers.
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hout = torch.empty((T_RANK, H), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+    dl = torch.empty_like(logits)
+    for _ in range(3):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        layer(dx, dl, out=out)
+        hout.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        layer(dx, dl, out=out)
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    L.raise_on_device_error()
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+
+    # Roofline of the dominant kernel (gmm_fp4): algorithmic bytes per launch.
+    gs = layer.group_sizes.cpu().numpy()
+    active = int((gs > 0).sum())
+    rows = T_RANK * TOPK
+    w13_bytes = H * I + (H // 32) * 2 * I          # codes + e8m0 scales per expert
+    w2_bytes = I * (H // 2) + (I // 32) * H
+    gmm1_bytes = active * w13_bytes + rows * H * 2 + rows * I * 2
+    gmm2_bytes = active * w2_bytes + rows * I * 2 + rows * H * 2
+    g1 = [d for d, act in gmm_ms if act != L.ACT_NONE]
+    g2 = [d for d, act in gmm_ms if act == L.ACT_NONE]
+    avg_ms = (sum(g1) + sum(g2)) / max(1, len(g1) + len(g2))
+    bytes_per_launch = (gmm1_bytes + gmm2_bytes) / 2
+    achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
+    peaks = measured_peaks()
+    peak = peaks["hbm_gbs"] if peaks else 6650.0
+    traffic = read_traffic()
+    res = {
+        "ms": ms, "e2e_ms": e2e_ms, "active": active,
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "kernel": "dw_moe gmm_fp4 (gmm1+gmm2 average)",
+            "peak_source": "measured" if peaks else "fallback",
+            "algorithmic_bytes_per_launch": bytes_per_launch,
+            "gmm1_ms": round(statistics.mean(g1), 4) if g1 else None,
+            "gmm2_ms": round(statistics.mean(g2), 4) if g2 else None,
+            "gmm1_GBps": round(gmm1_bytes / (statistics.mean(g1) * 1e-3) / 1e9, 1) if g1 else None,
+            "gmm2_GBps": round(gmm2_bytes / (statistics.mean(g2) * 1e-3) / 1e9, 1) if g2 else None,
+            "gmm_share_of_step": round((sum(g1) + sum(g2)) / ms, 3),
+        },
+        "clocks": clk.summary(),
+        "h2d": hx.numel() * 2 + hl.numel() * 2,
+        "d2h": hout.numel() * 2,
+    }
+    return res
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.gpus != world and world > 1:
+        print(f"--gpus {args.gpus} != WORLD_SIZE {world}", file=sys.stderr)
+    config = {"workload": WORKLOAD, "tokens_per_rank": T_RANK, "hidden": H, "intermediate": I,
+              "experts": E, "top_k": TOPK, "global_batch": T_RANK * world,
+              "parallelism": f"replicas{world}" if world > 1 else "single",
+              "l2": "inputs larger than L2 (3.3 GB of FP4 weights streamed per step)"}
+
+    if args.impl == "reference":
+        if rank == 0:
+            cb = cpu_baseline(args.seed, args.cpu_experts)
+            print(json.dumps({
+                "impl": "reference", "metric": METRIC, "value": round(cb["value"], 3),
+                "unit": UNIT, "n_gpus": args.gpus, "steps": 1, "warmup": 0,
+                "ms_per_step": cb["seconds_per_step"] * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config,
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 3), "unit": UNIT,
+                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            }), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+    finally:
+        pass
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.seed, args.cpu_experts)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = T_RANK * world * args.steps
+    value = tokens / (res["ms"] * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(res["ms"] / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; FP4 weights and E8M0 scales as BASELINE config 0/1)",
+        "config": config,
+        "e2e": {"value": round(tokens / (res["e2e_ms"] * 1e-3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+        "roofline": res["roofline"],
+        "cpu_baseline": None if cb is None else
+        {k: (round(cb[k], 3) if k == "value" else cb[k])
+         for k in ("value", "unit", "cores", "kind", "sample")},
+        "clocks": res["clocks"],
+        "gpu_launches": 6 * args.steps,
+        "active_experts": res["active"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

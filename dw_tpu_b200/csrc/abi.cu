@@ -1,0 +1,120 @@
+// Library plumbing behind the C ABI: error messages, the per-device status
+// word, tensor-map encoding and SM counts.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+// Device status word: kernels OR DWM_DEV_* bits into it.
+__device__ int g_status;
+
+constexpr int kMaxDevices = 64;
+int* g_status_addr[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
+std::mutex g_mu;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+}  // namespace
+
+namespace dwm {
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return DWM_OK;
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(e));
+  return (int)e;
+}
+
+int* status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (g_status_addr[dev]) return g_status_addr[dev];
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_status_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+    g_status_addr[dev] = static_cast<int*>(p);
+  }
+  return g_status_addr[dev];
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && g_num_sms[dev]) return g_num_sms[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (n <= 0) n = 148;
+  if (dev >= 0 && dev < kMaxDevices) g_num_sms[dev] = n;
+  return n;
+}
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                   uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_outer, CUtensorMapSwizzle swz) {
+  if (!g_encode) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e =
+          cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return set_error(DWM_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(DWM_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu",
+                     (int)r, (unsigned long long)inner, (unsigned long long)outer);
+  return DWM_OK;
+}
+
+}  // namespace dwm
+
+extern "C" {
+
+const char* dwm_version(void) { return "dw_moe 0.1.0 sm_100a"; }
+
+const char* dwm_last_error(void) { return g_last_error; }
+
+int dwm_device_status(void* stream, int* bits) {
+  if (!bits) return dwm::set_error(DWM_ERR_INVALID, "bits is NULL");
+  int* p = dwm::status_ptr();
+  if (!p) return dwm::set_error(DWM_ERR_STATE, "no device status word");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  int rc = dwm::check_cuda(cudaMemcpyAsync(&host, p, sizeof(int), cudaMemcpyDeviceToHost, s),
+                           "status read");
+  if (rc) return rc;
+  rc = dwm::check_cuda(cudaMemsetAsync(p, 0, sizeof(int), s), "status clear");
+  if (rc) return rc;
+  rc = dwm::check_cuda(cudaStreamSynchronize(s), "status sync");
+  if (rc) return rc;
+  *bits = host;
+  return DWM_OK;
+}
+
+}  // extern "C"

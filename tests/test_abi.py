@@ -1,0 +1,105 @@
+"""The C ABI library loads and exports every symbol include/*.h declares, and
+argument validation runs on the host (no GPU compute in this file)."""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"\b(dwm_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from dw_tpu_b200 import _lib
+    return _lib.load()
+
+
+def test_headers_declare_entry_points():
+    syms = declared_symbols()
+    assert "dwm_gmm_fp4" in syms and "dwm_combine" in syms and "dwm_permute" in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_signatures_cover_header():
+    from dw_tpu_b200 import _lib
+    missing = [s for s in declared_symbols() if s not in _lib.SIGNATURES]
+    assert not missing, missing
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.dwm_version()
+
+
+def _gmm(lib, **kw):
+    args = dict(lhs=None, codes=None, fmt=0, scales=None, sd=2, gs=None, ng=8, m=16, k=64,
+                n=256, go=0, nl=8, act=0, lim=0.0, od=0, zi=0, out=None, stream=None)
+    args.update(kw)
+    return lib.dwm_gmm_fp4(*args.values())
+
+
+def test_gmm_rejects_bad_shapes_on_host(lib):
+    from dw_tpu_b200 import _lib
+    fake = 1 << 20  # never dereferenced: validation fails first
+    assert _gmm(lib, k=63, lhs=fake, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert "multiple of 64" in _lib.last_error()
+    assert _gmm(lib, n=128, lhs=fake, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert _gmm(lib, fmt=1, lhs=fake, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert "tokamax" in _lib.last_error()
+    assert _gmm(lib, go=4, nl=8, lhs=fake, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert _gmm(lib, sd=7, lhs=fake, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert _gmm(lib, lhs=fake + 8, codes=fake, scales=fake, gs=fake, out=fake) == -1
+    assert "aligned" in _lib.last_error()
+
+
+def test_other_entry_points_validate(lib):
+    fake = 1 << 20
+    assert lib.dwm_permute(fake, 4, 0, 8, None, None, None, fake, None) == -1
+    assert lib.dwm_permute(fake, 4, 2, 2000, None, None, None, fake, None) == -1
+    assert lib.dwm_combine(fake, 5, 4, fake, fake, 0, 1, 64, 2, fake, 0, None) == -1
+    assert lib.dwm_combine(fake, 0, 4, fake, fake, 0, 1, 60, 2, fake, 0, None) == -1
+    assert lib.dwm_dispatch_gather(fake, 4, 12, fake, 4, fake, None) == -1
+    assert lib.dwm_route_topk(fake, 0, 4, 8, 9, 1, 1, None, -1, fake, None, None, None) == -1
+    assert lib.dwm_route_topk(fake, 0, 4, 8, 2, 7, 1, None, -1, fake, None, None, None) == -1
+    assert lib.dwm_fp4_codes_convert(fake, fake, 16, 0, 5, None) == -1
+    assert lib.dwm_fp4_dequant(fake, fake, 2, 1, 48, 64, fake, None) == -1
+    assert lib.dwm_device_status(None, None) == -1
+
+
+def test_python_shims_raise_value_error_without_gpu():
+    import torch
+    import dw_tpu_b200 as dw
+    lhs = torch.zeros((4, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        dw.gmm_v2(lhs, torch.zeros((1, 64, 128), dtype=torch.uint8),
+                  torch.zeros(1, dtype=torch.int32),
+                  torch.zeros((1, 2, 256), dtype=torch.uint8))
+    with pytest.raises(ValueError):
+        dw.fast_combine(torch.zeros((4, 8)), torch.zeros(4, dtype=torch.int32),
+                        torch.zeros((2, 2)), 2, mode=3)
+    with pytest.raises(ValueError):
+        dw.gmm_v2(lhs.float(), torch.zeros((1, 64, 128), dtype=torch.uint8),
+                  torch.zeros(1, dtype=torch.int32), torch.zeros((1, 2, 256), dtype=torch.uint8))
+
+
+def test_build_writes_library_in_tree():
+    from dw_tpu_b200 import _lib
+    assert os.path.dirname(_lib.LIB_PATH) == os.path.join(ROOT, "dw_tpu_b200")
+    assert os.path.exists(_lib.LIB_PATH)

@@ -1,0 +1,158 @@
+"""Routing, permute, gather, combine and e8m0 on the GPU vs the oracle:
+bit-exact for the integer/data-movement ops and the k-order combine."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests.gpu_util import bf16_to_np, np_to_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dw():
+    import dw_tpu_b200
+    return dw_tpu_b200
+
+
+def _ids(t, e, k, seed, dist="uniform"):
+    from dw_tpu_b200 import synthetic
+    ids, w = synthetic.route_ids(t, e, k, seed=seed, dist=dist)
+    return ids, w
+
+
+def test_permute_golden(dw, golden):
+    d = golden("permute_small")
+    argsort, tok, revert, gs = dw.moe_permute(torch.from_numpy(d["ids"]).cuda(), 16)
+    assert np.array_equal(argsort.cpu().numpy(), d["argsort"])
+    assert np.array_equal(tok.cpu().numpy(), d["tok"])
+    assert np.array_equal(revert.cpu().numpy(), d["revert"])
+    assert np.array_equal(gs.cpu().numpy(), d["group_sizes"])
+    x = dw.dispatch_gather(np_to_bf16(O.bf16_bits_to_f32(d["hidden_bits"])), tok)
+    assert np.array_equal(x.cpu().view(torch.int16).numpy().view(np.uint16), d["x_bits"])
+
+
+@pytest.mark.parametrize("t,e,k,dist", [
+    (1, 256, 8, "uniform"), (64, 256, 8, "uniform"), (512, 256, 8, "zipf"),
+    (8192, 256, 8, "uniform"), (3000, 32, 6, "zipf"), (0, 16, 4, "uniform"),
+    (100, 1024, 8, "uniform"),
+])
+def test_permute_bit_exact(dw, t, e, k, dist):
+    if t:
+        ids, _ = _ids(t, e, k, seed=t + e, dist=dist)
+    else:
+        ids = np.zeros((0, k), np.int32)
+    argsort, tok, revert, gs = dw.moe_permute(torch.from_numpy(ids).cuda(), e)
+    ra, rt, rr, rg = O.permute(ids, e)
+    assert np.array_equal(argsort.cpu().numpy(), ra)
+    assert np.array_equal(tok.cpu().numpy(), rt)
+    assert np.array_equal(revert.cpu().numpy(), rr)
+    assert np.array_equal(gs.cpu().numpy(), rg)
+
+
+def test_permute_repeated_ids_stable(dw):
+    """Repeated expert ids inside a token (no dedupe) keep flat order."""
+    rng = np.random.default_rng(9)
+    ids = rng.integers(0, 4, (700, 8)).astype(np.int32)
+    argsort, tok, revert, gs = dw.moe_permute(torch.from_numpy(ids).cuda(), 4)
+    ra, rt, rr, rg = O.permute(ids, 4)
+    assert np.array_equal(argsort.cpu().numpy(), ra)
+    assert np.array_equal(gs.cpu().numpy(), rg)
+
+
+def test_permute_bad_id_reported(dw):
+    from dw_tpu_b200 import _lib
+    ids = np.array([[0, 1], [2, 99]], np.int32)
+    _, _, _, gs = dw.moe_permute(torch.from_numpy(ids).cuda(), 4)
+    assert _lib.device_status() & _lib.DEV_BAD_INDEX
+    assert gs.cpu().tolist() == [1, 1, 1, 0]
+
+
+def test_sorted_token_indices_and_fast_dispatch(dw):
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 64, (333, 8)).astype(np.int32)
+    argsort = np.argsort(ids.reshape(-1), kind="stable").astype(np.int32)
+    got = dw.sorted_token_indices(torch.from_numpy(argsort).cuda(), 8)
+    assert np.array_equal(got.cpu().numpy(), np.repeat(np.arange(333), 8)[argsort])
+    hidden = O.round_bf16(rng.standard_normal((333, 4096)).astype(np.float32))
+    for mode in (0, 1, 2):
+        x = dw.fast_dispatch_gather(np_to_bf16(hidden), torch.from_numpy(argsort).cuda(), 8,
+                                    mode)
+        assert np.array_equal(bf16_to_np(x), hidden[np.repeat(np.arange(333), 8)[argsort]])
+
+
+def test_combine_golden(dw, golden):
+    d = golden("combine_small")
+    y = np_to_bf16(O.bf16_bits_to_f32(d["y_bits"]))
+    idx = torch.from_numpy(d["idx"]).cuda()
+    w = torch.from_numpy(d["w"]).cuda()
+    out = dw.fast_combine(y, idx, w, 6, mode=2, out_dtype=torch.bfloat16)
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), d["out_bits"])
+    out32 = dw.combine_xla(y, idx, w, 6, out_dtype=torch.float32)
+    assert np.array_equal(out32.cpu().numpy(), d["out_f32"])
+
+
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+@pytest.mark.parametrize("wdt", ["bf16", "f32"])
+def test_combine_bit_exact(dw, xdt, wdt):
+    rng = np.random.default_rng(2)
+    t, k, h = 257, 8, 4096
+    y = rng.standard_normal((t * k, h)).astype(np.float32)
+    if xdt == "bf16":
+        y = O.round_bf16(y)
+        y_t = np_to_bf16(y)
+    else:
+        y_t = torch.from_numpy(y).cuda()
+    w = rng.dirichlet(np.ones(k), size=t).astype(np.float32)
+    if wdt == "bf16":
+        w = O.round_bf16(w)
+        w_t = np_to_bf16(w)
+    else:
+        w_t = torch.from_numpy(w).cuda()
+    idx = rng.permutation(t * k).astype(np.int32)
+    out = dw.fast_combine(y_t, torch.from_numpy(idx).cuda(), w_t, k, mode=1,
+                          out_dtype=torch.bfloat16)
+    assert np.array_equal(bf16_to_np(out), O.combine(y, idx, w, k))
+
+
+@pytest.mark.parametrize("fn", ["sigmoid", "softmax", "sqrtsoftplus"])
+def test_route_topk_golden(dw, golden, fn):
+    d = golden("route_small")
+    logits = np_to_bf16(O.bf16_bits_to_f32(d["logits_bits"]))
+    w, ids = dw.route_topk(logits, 8, renormalize=True, scoring_fn=fn, dtype=torch.float32)
+    assert np.array_equal(ids.cpu().numpy(), d[f"{fn}_ids"])
+    np.testing.assert_allclose(w.cpu().numpy(), d[f"{fn}_w"], rtol=2e-6, atol=1e-7)
+
+
+def test_route_topk_bias_and_padding(dw):
+    rng = np.random.default_rng(3)
+    logits = O.round_bf16(rng.standard_normal((40, 256)).astype(np.float32))
+    bias = (rng.standard_normal(256) * 0.1).astype(np.float32)
+    w, ids = dw.route_topk(np_to_bf16(logits), 8, scoring_fn="sigmoid",
+                           bias=torch.from_numpy(bias).cuda(), num_valid_tokens=33,
+                           dtype=torch.float32)
+    rid, rw = O.route_topk(logits, 8, "sigmoid", True, bias=bias, num_valid_tokens=33)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    assert np.all(ids.cpu().numpy()[33:] == 0) and np.all(w.cpu().numpy()[33:] == 0)
+
+
+def test_route_ties_go_to_lower_index(dw):
+    logits = torch.zeros((2, 64), dtype=torch.float32, device="cuda")
+    w, ids = dw.route_topk(logits, 4, scoring_fn="softmax", dtype=torch.float32)
+    assert ids.cpu().tolist() == [[0, 1, 2, 3], [0, 1, 2, 3]]
+
+
+def test_e8m0_roundtrip(dw):
+    e = np.arange(-126, 128)
+    s = np.ldexp(np.ones(e.shape, np.float32), e).astype(np.float32)
+    codes, lossless = dw.e8m0_encode(torch.from_numpy(s).cuda())
+    assert bool(lossless)
+    rc, _ = O.e8m0_encode(s)
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    back = dw.e8m0_decode(codes)
+    assert np.array_equal(back.cpu().numpy().view(np.uint32), s.view(np.uint32))
+    _, lossless = dw.e8m0_encode(torch.tensor([1.0, 3.0], device="cuda"))
+    assert not bool(lossless)

@@ -1,0 +1,93 @@
+"""The single-device MoE layer on the GPU vs the oracle: a reduced layer in
+full, and the BASELINE config-1 layer (T=64, H=4096, I=2048, E=256, top-8) on
+a sample of tokens."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests.gpu_util import bf16_to_np, gemm_rel_tol, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dw():
+    import dw_tpu_b200
+    return dw_tpu_b200
+
+
+def _layer(dw, t, e, h, i, k, seed, lo=118, hi=121, f32_reduce=False):
+    from dw_tpu_b200 import synthetic
+    w = synthetic.moe_weights(e, h, i, seed=seed, device="cuda")
+    for name in ("s13", "s2"):  # keep activations O(1): scales 2^-9..2^-6
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, seed + 5, "cuda",
+                                               lo=lo, hi=hi))
+    x, router = synthetic.layer_inputs(t, h, e, seed=seed)
+    logits = (x.float() @ router.float()).to(torch.bfloat16)
+    layer = dw.MoELayer(w, k, t, f32_reduce=f32_reduce)
+    out = layer(x.cuda(), logits.cuda())
+    torch.cuda.synchronize()
+    from dw_tpu_b200 import _lib
+    _lib.raise_on_device_error()
+    return w, x, logits, layer, out
+
+
+@pytest.mark.parametrize("f32_reduce", [False, True])
+def test_layer_small_matches_oracle(dw, f32_reduce):
+    t, e, h, i, k = 24, 16, 512, 256, 4
+    w, x, logits, layer, out = _layer(dw, t, e, h, i, k, seed=1, f32_reduce=f32_reduce)
+    ref = O.fused_moe(bf16_to_np(x), bf16_to_np(logits), w.w13.cpu().numpy(),
+                      w.s13.cpu().numpy(), w.w2.cpu().numpy(), w.s2.cpu().numpy(), k,
+                      f32_reduce=f32_reduce)
+    ids, _ = O.route_topk(bf16_to_np(logits), k, "sigmoid", True)
+    assert np.array_equal(layer.ids[:t].cpu().numpy(), ids)
+    got = bf16_to_np(out)
+    rf = rel_fro(got, ref)
+    assert rf < 2 * gemm_rel_tol(i), rf
+
+
+def test_layer_cfg1_sampled_tokens(dw):
+    """Full-size decode layer; tokens 0 and 37 checked against the oracle
+    restricted to their 8 experts (weights dequantised per expert)."""
+    t, e, h, i, k = 64, 256, 4096, 2048, 8
+    w, x, logits, layer, out = _layer(dw, t, e, h, i, k, seed=2)
+    lg = bf16_to_np(logits)
+    ids, wts = O.route_topk(lg, k, "sigmoid", True)
+    assert np.array_equal(layer.ids.cpu().numpy(), ids)
+    xs = bf16_to_np(x)
+    got = bf16_to_np(out)
+    for tok in (0, 37):
+        acc = np.zeros(h, np.float32)
+        for kk in range(k):
+            ex = int(ids[tok, kk])
+            w13 = O.dequant_fp4_block(w.w13[ex].cpu().numpy(), w.s13[ex].cpu().numpy())
+            w2 = O.dequant_fp4_block(w.w2[ex].cpu().numpy(), w.s2[ex].cpu().numpy())
+            h1 = (xs[tok].astype(np.float64) @ w13.astype(np.float64)).astype(np.float32)
+            a = O.round_bf16(O.silu_and_mul(h1[:i], h1[i:]))
+            y = O.round_bf16((a.astype(np.float64) @ w2.astype(np.float64)).astype(np.float32))
+            acc = (acc + (y * O.round_bf16(wts[tok, kk:kk + 1])).astype(np.float32)).astype(
+                np.float32)
+        ref = O.round_bf16(acc)
+        rf = rel_fro(got[tok], ref)
+        assert rf < 2 * gemm_rel_tol(i), (tok, rf)
+
+
+def test_layer_graph_capture_replays_bitwise(dw):
+    t, e, h, i, k = 32, 16, 512, 256, 4
+    w, x, logits, layer, out = _layer(dw, t, e, h, i, k, seed=3)
+    xc, lc = x.cuda(), logits.cuda()
+    res = torch.empty_like(out)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer(xc, lc, out=res)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        layer(xc, lc, out=res)
+    res.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(res.view(torch.int16), out.view(torch.int16))
