@@ -49,8 +49,10 @@ constexpr int T_STAGE = BT * BK * 2;         // 16 KiB, K-major SW128
 constexpr int T_BOX_ROWS = 16;
 constexpr int T_BOX_BYTES = T_BOX_ROWS * BK * 2;  // 2 KiB
 constexpr int C_SUB_BYTES = BK * (BW / 2);        // 4 KiB of packed nibbles
-constexpr int C_SUB1_OFF = C_SUB_BYTES + 64;      // shifts sub 1 by 16 banks
-constexpr int C_STAGE = 8320;
+// TMA writes shared memory at 128-byte aligned addresses only.
+constexpr int C_SUB1_OFF = C_SUB_BYTES;
+constexpr int C_STAGE = NSUB * C_SUB_BYTES;
+static_assert(C_SUB1_OFF % 128 == 0 && C_STAGE % 128 == 0, "TMA needs 128 B alignment");
 
 template <int SD>
 struct ScaleTraits;
@@ -516,8 +518,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp >= DEC_WARP0) {
     // ---------------- decode ----------------
-    const int dw = warp - DEC_WARP0;  // rows dw, dw+8, ..., dw+56 of each stage
-    const int sub = lane >> 4;        // lanes 0-15 sub 0, 16-31 sub 1
+    // Warps 0-3 of the decode group take sub-tile 0, warps 4-7 sub-tile 1.
+    // A warp decodes two adjacent 64-byte code rows per step (lanes 0-15 row
+    // r, lanes 16-31 row r+1: 128 contiguous bytes, conflict-free), rows
+    // r = 2*(dw%4) + 8j (+1), j = 0..7, covering all 64 rows of the stage.
+    const int dw = warp - DEC_WARP0;
+    const int sub = dw >> 2;
+    const int half = lane >> 4;
     const int g = lane & 15;          // 8-column group inside the sub-tile
     int cs = 0, as = 0;
     uint32_t cs_ph = 0, as_ph = 0;
@@ -546,7 +553,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
-            const int r = kb * 32 + jj * 8 + dw;
+            const int r = kb * 32 + jj * 8 + 2 * (dw & 3) + half;
             const uint32_t w = *reinterpret_cast<const uint32_t*>(csrc + r * (BW / 2) + g * 4);
             const uint4 v = decode8(w, m1, m2, two);
             const int chunk = (g & 7) ^ (r & 7);
