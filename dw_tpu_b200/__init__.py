@@ -20,7 +20,7 @@ _lib.load()
 
 from .e8m0_scale import e8m0_decode, e8m0_encode  # noqa: E402
 from .fused_moe import FP4MoEWeights, MoELayer, fused_moe_func  # noqa: E402
-from .gmm_v2 import (codes_to_e2m1, decode_codes, e2m1_to_codes,  # noqa: E402
+from .gmm_v2 import (b200_to_e2m1, codes_to_e2m1, decode_codes, e2m1_to_codes,  # noqa: E402
                      fp4_weight_to_codes, gmm, gmm_v2, gmm_wrapper, needs_fp4_emulation)
 from .moe_fast_combine import combine_pallas, combine_xla, fast_combine  # noqa: E402
 from .moe_fast_dispatch import (dispatch_gather, dispatch_gather_pallas,  # noqa: E402
@@ -29,7 +29,7 @@ from .routing import route_topk  # noqa: E402
 
 __all__ = [
     "gmm_v2", "gmm", "gmm_wrapper", "e2m1_to_codes", "codes_to_e2m1", "decode_codes",
-    "fp4_weight_to_codes", "needs_fp4_emulation", "fast_dispatch_gather",
+    "fp4_weight_to_codes", "b200_to_e2m1", "needs_fp4_emulation", "fast_dispatch_gather",
     "sorted_token_indices", "moe_permute", "dispatch_gather", "dispatch_gather_pallas",
     "fast_combine", "combine_xla", "combine_pallas", "e8m0_encode", "e8m0_decode",
     "route_topk", "MoELayer", "FP4MoEWeights", "fused_moe_func",

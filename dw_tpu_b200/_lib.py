@@ -14,7 +14,9 @@ import threading
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libdw_moe.so")
+# DWM_LIB_PATH selects another build of the same C ABI (e.g. one compiled with
+# different pipeline depths); default: the in-tree library.
+LIB_PATH = os.environ.get("DWM_LIB_PATH") or os.path.join(_HERE, "libdw_moe.so")
 
 # include/dw_moe.h constants
 OK = 0
@@ -32,9 +34,18 @@ ACT_SWIGLU = 1
 ACT_SWIGLU_CLAMP = 2
 FP4_E2M1 = 0
 FP4_TOKAMAX = 1
+FP4_B200 = 2
+LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200}
 SCORE_SOFTMAX = 0
 SCORE_SIGMOID = 1
 SCORE_SQRTSOFTPLUS = 2
+EP_HANDLE_BYTES = 64
+EP_COUNTS = 1
+EP_ROWS = 2
+EP_WAIT = 4
+EP_ALL = 7
+EP_PUSH = 1
+EP_REDUCE = 2
 
 _c = ctypes
 _P = _c.c_void_p
@@ -50,7 +61,10 @@ SIGNATURES = {
     "dwm_device_status": ([_P, _c.POINTER(_I)], _I),
     "dwm_gmm_fp4": ([_P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P, _P],
                     _I),
-    "dwm_fp4_dequant": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
+    "dwm_fp4_dequant": ([_P, _I, _P, _I, _I, _I, _I, _P, _P], _I),
+    "dwm_fp4_to_b200": ([_P, _P, _I, _I, _I, _I, _P], _I),
+    "dwm_gmm_fp4_variant": ([_P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P,
+                             _I, _P], _I),
     "dwm_fp4_codes_convert": ([_P, _P, _SZ, _I, _I, _P], _I),
     "dwm_e8m0_encode": ([_P, _SZ, _P, _P, _P], _I),
     "dwm_e8m0_decode": ([_P, _SZ, _P, _P], _I),
@@ -59,6 +73,14 @@ SIGNATURES = {
     "dwm_permute": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "dwm_dispatch_gather": ([_P, _I, _I, _P, _I64, _P, _P], _I),
     "dwm_combine": ([_P, _I, _I64, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
+    "dwm_ep_create": ([_I, _I, _I, _I, _I, _I, _c.POINTER(_P)], _I),
+    "dwm_ep_ipc_handle": ([_P, _P], _I),
+    "dwm_ep_connect": ([_P, _P], _I),
+    "dwm_ep_connect_local": ([_P, _c.POINTER(_P)], _I),
+    "dwm_ep_recv_buffer": ([_P, _c.POINTER(_P), _c.POINTER(_I64)], _I),
+    "dwm_ep_dispatch": ([_P, _P, _P, _I, _P, _I, _P], _I),
+    "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
+    "dwm_ep_destroy": ([_P], _I),
 }
 
 _lib = None

@@ -84,8 +84,25 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Polls the phase; a thread whose phase is not complete is suspended in
+// hardware until it completes or the hint (ns) runs out, so waiting warps do
+// not take issue slots from the working ones.
+// Build-time tunable; 0 uses the hardware's default suspend window.
+#ifndef DWM_SUSPEND_HINT_NS
+#define DWM_SUSPEND_HINT_NS 4000
+#endif
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#if DWM_SUSPEND_HINT_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(DWM_SUSPEND_HINT_NS)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -93,6 +110,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
@@ -101,11 +119,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // false so the kernel can wind down instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// kBackoff: sleep between polls (for waits that span a whole tile, so the
+// waiting warps leave issue slots to the decode warps).
+template <bool kBackoff = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
+    if (kBackoff) __nanosleep(256);
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;

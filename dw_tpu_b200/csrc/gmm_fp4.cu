@@ -1,79 +1,89 @@
 // FP4 grouped matmul for sm_100a: tokamax gmm_v2 with rhs_fp4_codes
-// (TK:107-153), decoded in shared memory and multiplied on tcgen05 tensor
-// cores with the accumulator in TMEM.
-//
-// Design (one persistent CTA per SM, 16 warps):
-//   warps 0-3   epilogue: TMEM -> registers -> (SwiGLU) -> global
-//   warp  4     TMA producer: e2m1 codes + scales ring, token-row ring
-//   warp  5     TMEM allocator and single-thread UMMA issuer
-//   warps 8-15  decode: e2m1 nibbles x scale -> bf16 tiles in swizzled SMEM
+// (TK:107-153), decoded on the SM and multiplied on tcgen05 tensor cores with
+// f32 accumulators in TMEM. Decode-sized groups go to the mma.sync kernel in
+// gmv_fp4.cu instead (see the dispatcher at the end of this file).
 //
 // The product is computed transposed ("swap AB"): the decoded weight tile
-// W[k, n0:n0+128] is UMMA operand A (M = 128 weight columns, MN-major, 128B
-// swizzle) and the token rows X[r0:r0+rows, k] are operand B (N = rows
-// rounded up to 16, K-major, 128B swizzle, loaded by TMA). A decode-sized
-// group of 2 rows then costs an N = 16 MMA instead of wasting a 128-row
-// tile, and prefill-sized groups run N = 128. Each tile carries two 128-column
+// W[k, n0:n0+128] is UMMA operand A (M = 128 weight columns) and the token
+// rows X[r0:r0+rows, k] are operand B (N = rows rounded up to 16, K-major,
+// 128-byte swizzled, loaded by TMA). Each tile carries two 128-column
 // sub-tiles (two accumulators): adjacent columns for a plain GEMM, or the
-// matching gate and up columns for the fused SwiGLU.
+// matching gate and up columns for the fused SwiGLU. Two variants share the
+// producers, the tile scheduler and the epilogue:
+//   kMN  raw e2m1 weights [g, k, n/2] decoded into a 128-byte swizzled,
+//        MN-major A tile in shared memory.
+//   kKS  B200-layout weights (fp4_decode.cuh) decoded into a K-major,
+//        128-byte swizzled A tile in shared memory.
+//
+// One persistent CTA per SM, 24 warps:
+//   warps 0-3   epilogue: TMEM -> registers -> (SwiGLU) -> global
+//   warp  4     TMA producer: FP4 codes + scales ring (the HBM stream)
+//   warp  5     TMEM allocator and single-thread UMMA issuer
+//   warp  6     TMA producer: token-row ring (L2-resident rows)
+//   warps 8-23  decode, two groups of 8 on alternate stages
 //
 // Numerics follow the reference order (E0901:84-95): each e2m1 value is
 // decoded exactly to bf16, multiplied by the bf16 scale in one bf16 multiply
 // (round to nearest even), then the MMA accumulates bf16 x bf16 products in
 // f32; the epilogue applies SwiGLU in f32 and rounds once to the output type.
-#include "common.cuh"
+#include <algorithm>
+#include <type_traits>
+
+#include "fp4_decode.cuh"
 
 namespace dwm {
+
+int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+               const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
+               int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
+               cudaStream_t stream);
+
 namespace gmm {
+
+using namespace fp4;
+
+enum Variant { kMN = 0, kKS = 1 };
 
 constexpr int NSUB = 2;    // sub-tiles (accumulators) per tile
 constexpr int BW = 128;    // weight columns per sub-tile (UMMA M)
 constexpr int BK = 64;     // K per pipeline stage (128 bytes of bf16)
 constexpr int BT = 128;    // max token rows per tile (UMMA N)
-constexpr int CS = 6;      // codes+scales stages
-constexpr int TS = 3;      // token-row stages
-constexpr int AS = 3;      // decoded-weight stages
-constexpr int NUM_THREADS = 512;
+constexpr int NUM_THREADS = 768;
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
+constexpr int TOKEN_WARP = 6;
 constexpr int DEC_WARP0 = 8;
-constexpr int NUM_DEC_WARPS = 8;
+constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
 constexpr int MAX_GROUPS = 1024;
-constexpr int TMEM_COLS = 512;  // 2 buffers x NSUB x BT f32 columns
+constexpr int TMEM_COLS = 512;    // 2 buffers x NSUB x BT f32 columns
 
-constexpr int A_SUB_BYTES = BW * BK * 2;     // 16 KiB, MN-major SW128
+constexpr int A_SUB_BYTES = BW * BK * 2;     // 16 KiB bf16 sub-tile
 constexpr int A_STAGE = NSUB * A_SUB_BYTES;  // 32 KiB
-constexpr int A_LBO = 8192;                  // MN-atom (64 columns) stride
-constexpr int A_SBO = 1024;                  // K-atom (8 rows) stride
-constexpr int T_STAGE = BT * BK * 2;         // 16 KiB, K-major SW128
+constexpr int A_LBO_MN = 8192;               // MN-major: MN-atom (64 columns) stride
+constexpr int A_SBO_MN = 1024;               // MN-major: K-atom (8 rows) stride
+constexpr int T_STAGE = 16384;               // token stage: 8 boxes of 16 rows x 64 k
 constexpr int T_BOX_ROWS = 16;
 constexpr int T_BOX_BYTES = T_BOX_ROWS * BK * 2;  // 2 KiB
-constexpr int C_SUB_BYTES = BK * (BW / 2);        // 4 KiB of packed nibbles
-// TMA writes shared memory at 128-byte aligned addresses only.
-constexpr int C_SUB1_OFF = C_SUB_BYTES;
-constexpr int C_STAGE = NSUB * C_SUB_BYTES;
-static_assert(C_SUB1_OFF % 128 == 0 && C_STAGE % 128 == 0, "TMA needs 128 B alignment");
+constexpr int C_SUB_BYTES = BK * (BW / 2);        // 4 KiB of packed nibbles per sub-tile
+constexpr int C_STAGE = NSUB * C_SUB_BYTES;       // TMA writes 128-byte aligned addresses
+static_assert(C_SUB_BYTES % 128 == 0, "TMA needs 128 B alignment");
 
-template <int SD>
-struct ScaleTraits;
-template <>
-struct ScaleTraits<DWM_U8> {
-  static constexpr int bytes = 1;
-  static constexpr CUtensorMapDataType tma = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-};
-template <>
-struct ScaleTraits<DWM_BF16> {
-  static constexpr int bytes = 2;
-  static constexpr CUtensorMapDataType tma = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-};
-template <>
-struct ScaleTraits<DWM_F32> {
-  static constexpr int bytes = 4;
-  static constexpr CUtensorMapDataType tma = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-};
+// Pipeline depths (build-time tunables).
+#ifndef DWM_GMM_TS
+#define DWM_GMM_TS 3
+#endif
+#ifndef DWM_GMM_AS
+#define DWM_GMM_AS 3
+#endif
+#ifndef DWM_GMM_CS
+#define DWM_GMM_CS 8
+#endif
+constexpr int TS = DWM_GMM_TS;
+constexpr int AS = DWM_GMM_AS;
 
 template <int SD>
 struct Smem {
+  static constexpr int CS = ScaleTraits<SD>::bytes == 4 ? (DWM_GMM_CS * 3) / 4 : DWM_GMM_CS;
   static constexpr int S_STAGE = NSUB * 2 * BW * ScaleTraits<SD>::bytes;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_T = OFF_A + AS * A_STAGE;
@@ -86,6 +96,8 @@ struct Smem {
   static constexpr int OFF_TILES = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int BYTES = OFF_TILES + (MAX_GROUPS + 1) * 4;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment
+  static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
+  static_assert(CS <= 32 && TS <= 32, "ring masks are 32-bit");
 };
 
 struct Args {
@@ -97,96 +109,13 @@ struct Args {
   int out_f32;
   int zero_init;
   void* out;
-  int ldo;  // output row length (n, or n/2 with SwiGLU)
+  int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // column tiles per group
   int* status;
 };
 
-// Column permutation inside each 8-column group produced by decode8: SMEM
-// position p holds column (p >> 1) + 4 * (p & 1).
+// SMEM slot p of an 8-column group holds column perm8(p) (kMN).
 __device__ __forceinline__ int perm8(int p) { return (p >> 1) + ((p & 1) << 2); }
-
-// Decode one 32-bit word of 8 e2m1 nibbles (columns c..c+7, column c+j in
-// bits 4j..4j+3) into 8 bf16 values. Output word i holds columns (c+i,
-// c+i+4) in its low/high halves.
-//
-// (w << s) & 0x01C001C0 drops the 3 magnitude bits into the bf16 exponent
-// LSBs and top mantissa bit, and (w << s') & 0x80008000 moves the sign: the
-// result is the e2m1 value times 2^-126 exactly (the e2m1 subnormal 0.5 lands
-// on the bf16 subnormal 2^-127). One bf16 multiply by 2^126 * scale (m1)
-// then gives value * scale rounded once; when that factor would overflow
-// bf16 the caller passes m1 = 2^126 and the scale in m2 (two_step).
-__device__ __forceinline__ uint4 decode8(uint32_t w, const uint32_t (&m1)[4],
-                                         const uint32_t (&m2)[4], bool two_step) {
-  uint32_t t0 = ((w << 6) & 0x01C001C0u) | ((w << 12) & 0x80008000u);
-  uint32_t t1 = ((w << 2) & 0x01C001C0u) | ((w << 8) & 0x80008000u);
-  uint32_t t2 = ((w >> 2) & 0x01C001C0u) | ((w << 4) & 0x80008000u);
-  uint32_t t3 = ((w >> 6) & 0x01C001C0u) | (w & 0x80008000u);
-  uint4 v;
-  v.x = hmul2_bf16(t0, m1[0]);
-  v.y = hmul2_bf16(t1, m1[1]);
-  v.z = hmul2_bf16(t2, m1[2]);
-  v.w = hmul2_bf16(t3, m1[3]);
-  if (two_step) {
-    v.x = hmul2_bf16(v.x, m2[0]);
-    v.y = hmul2_bf16(v.y, m2[1]);
-    v.z = hmul2_bf16(v.z, m2[2]);
-    v.w = hmul2_bf16(v.w, m2[3]);
-  }
-  return v;
-}
-
-constexpr uint32_t kBf16Pow2_126x2 = 0x7E807E80u;  // bf16 2^126, twice
-
-// Multipliers for the 8 scales s[0..7] of columns c..c+7 (pairs (i, i+4)).
-// Returns true if the two-step form is needed for this thread.
-template <int SD>
-__device__ __forceinline__ bool scale_mults(const uint8_t* sp, uint32_t (&m1)[4],
-                                            uint32_t (&m2)[4]) {
-  if constexpr (SD == DWM_U8) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(sp);
-    uint32_t c[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      c[i] = (raw.x >> (8 * i)) & 0xFFu;
-      c[i + 4] = (raw.y >> (8 * i)) & 0xFFu;
-    }
-    bool two = false;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) two |= c[i] > 128u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      // 2^(c-127) has bf16 bits c << 7 (c = 0 -> +0); 2^126 * 2^(c-127) =
-      // 2^(c-1) has bits (c + 126) << 7 and is finite for c <= 128.
-      uint32_t lo1 = c[i] ? ((c[i] + 126u) << 7) : 0u;
-      uint32_t hi1 = c[i + 4] ? ((c[i + 4] + 126u) << 7) : 0u;
-      m1[i] = lo1 | (hi1 << 16);
-      m2[i] = (c[i] << 7) | (c[i + 4] << 23);
-    }
-    return two;
-  } else if constexpr (SD == DWM_BF16) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(sp);
-    const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};  // (s0,s1),(s2,s3),..
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t lo = (r[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu;
-      uint32_t hi = (r[(i + 4) >> 1] >> (((i + 4) & 1) * 16)) & 0xFFFFu;
-      m1[i] = kBf16Pow2_126x2;
-      m2[i] = lo | (hi << 16);
-    }
-    return true;
-  } else {
-    const float4 a = *reinterpret_cast<const float4*>(sp);
-    const float4 b = *reinterpret_cast<const float4*>(sp + 16);
-    const float s[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      m1[i] = kBf16Pow2_126x2;
-      m2[i] = f32_to_bf16_bits(s[i]) | (f32_to_bf16_bits(s[i + 4]) << 16);
-    }
-    return true;
-  }
-}
 
 struct Tile {
   int g;      // local group
@@ -214,12 +143,20 @@ __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const in
   return t;
 }
 
-template <int SD>
+// Token-stage geometry: a tile needs nb 16-row boxes per k-step; rounded up
+// to a power of two (nbp) a stage of 8 boxes covers 8 / nbp k-steps.
+__device__ __forceinline__ int token_span(int nb, int& nbp) {
+  nbp = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;
+  return 8 / nbp;
+}
+
+template <int SD, int VAR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
   using L = Smem<SD>;
+  constexpr int CS = L::CS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -292,8 +229,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int g = lane * per + i;
       if (g < G) {
         int v = max(a.group_sizes[g], 0);
-        int s = min(run, a.m);
-        row_start[g] = s;
+        row_start[g] = min(run, a.m);
         run += v;
       }
     }
@@ -347,9 +283,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Rows outside the local groups: [0, lo) and [hi, m).
       const int lo = row_start[a.group_offset];
       const int hi = row_start[a.group_offset + a.n_local];
-      const int64_t row_bytes = (int64_t)a.ldo * es;
-      const int64_t n16 = row_bytes / 16;
-      uint4 z = make_uint4(0, 0, 0, 0);
+      const int64_t n16 = (int64_t)a.ldo * es / 16;
+      const uint4 z = make_uint4(0, 0, 0, 0);
       const int64_t tid = (int64_t)blockIdx.x * 128 + threadIdx.x;
       const int64_t stride = (int64_t)gridDim.x * 128;
       uint4* o = reinterpret_cast<uint4*>(a.out);
@@ -357,13 +292,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int64_t i = (int64_t)hi * n16 + tid; i < (int64_t)a.m * n16; i += stride) o[i] = z;
     }
     const int mrow = warp * 32 + lane;  // TMEM lane = A row = weight column slot
-    const int col = (mrow & ~7) + perm8(mrow & 7);
+    const int col = VAR == kMN ? (mrow & ~7) + perm8(mrow & 7) : mrow;
+    constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
     int it = 0;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++it) {
       const Tile t = get_tile(idx, row_start, tile_prefix, a);
       const int buf = it & 1;
       const uint32_t ph = (it >> 1) & 1;
-      const bool got = mbar_wait(&acc_full[buf], ph, abort_flag, a.status);
+      const bool got = mbar_wait<true>(&acc_full[buf], ph, abort_flag, a.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NSUB * BT);
@@ -378,8 +314,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int r = c * 16 + e;
           if (r < t.rows) {
             const int64_t row = t.row0 + r;
-            const float v0 = __uint_as_float(r0[e]);
-            const float v1 = __uint_as_float(r1[e]);
+            const float v0 = __uint_as_float(r0[e]) * acc_scale;
+            const float v1 = __uint_as_float(r1[e]) * acc_scale;
             if (a.act == DWM_ACT_NONE) {
               const int64_t base = row * a.ldo + (int64_t)t.n_idx * (NSUB * BW) + col;
               if (a.out_f32) {
@@ -414,16 +350,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   } else if (warp == PRODUCER_WARP) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: codes + scales (HBM stream) ----------------
     if (lane == 0) {
       const uint64_t pol_stream = policy_evict_first();
-      const uint64_t pol_keep = policy_evict_last();
       constexpr uint32_t cs_bytes = NSUB * C_SUB_BYTES + L::S_STAGE;
-      int cs = 0, ts = 0;
-      uint32_t cs_ph = 0, ts_ph = 0;
-      uint32_t cs_armed = 0, cs_par = 0, ts_armed = 0, ts_par = 0;
+      int cs = 0;
+      uint32_t cs_ph = 0, cs_armed = 0, cs_par = 0;
       const int half = a.n / 2;
-      for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         const Tile t = get_tile(idx, row_start, tile_prefix, a);
         int col[NSUB];
         if (a.act == DWM_ACT_NONE) {
@@ -433,9 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           col[0] = t.n_idx * BW;
           col[1] = half + t.n_idx * BW;
         }
-        const int nb = (t.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
-        bool ok = true;
-        for (int kk = 0; kk < KT && ok; ++kk) {
+        for (int kk = 0; kk < KT; ++kk) {
           if (!mbar_wait(&cs_empty[cs], cs_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
           mbar_arrive_expect_tx(&cs_full[cs], cs_bytes);
           cs_armed |= 1u << cs;
@@ -444,28 +377,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sdst = smem + L::OFF_S + cs * L::S_STAGE;
 #pragma unroll
           for (int s = 0; s < NSUB; ++s) {
-            tma_load_2d(cdst + s * C_SUB1_OFF, &tm_codes, &cs_full[cs], col[s] / 2,
-                        t.g * a.k + kk * BK, pol_stream);
+            if constexpr (VAR == kMN)  // [g*k + kk, n/2 bytes]: 64 rows x 64 bytes
+              tma_load_2d(cdst + s * C_SUB_BYTES, &tm_codes, &cs_full[cs], col[s] / 2,
+                          t.g * a.k + kk * BK, pol_stream);
+            else  // [g*n/16 + block, (k/16)*32 words]: 8 column blocks x 4 k-blocks
+              tma_load_2d(cdst + s * C_SUB_BYTES, &tm_codes, &cs_full[cs], kk * 4 * 32,
+                          t.g * (a.n / 16) + col[s] / 16, pol_stream);
             tma_load_2d(sdst + s * (L::S_STAGE / NSUB), &tm_scales, &cs_full[cs], col[s],
                         t.g * (a.k / 32) + kk * 2, pol_stream);
           }
           if (++cs == CS) { cs = 0; cs_ph ^= 1; }
-
-          if (!mbar_wait(&tk_empty[ts], ts_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&tk_full[ts], nb * T_BOX_BYTES);
-          ts_armed |= 1u << ts;
-          ts_par = (ts_par & ~(1u << ts)) | (ts_ph << ts);
-          uint8_t* tdst = smem + L::OFF_T + ts * T_STAGE;
-          for (int b = 0; b < nb; ++b)
-            tma_load_2d(tdst + b * T_BOX_BYTES, &tm_lhs, &tk_full[ts], kk * BK,
-                        t.row0 + b * T_BOX_ROWS, pol_keep);
-          if (++ts == TS) { ts = 0; ts_ph ^= 1; }
         }
-        if (!ok) break;
       }
       // Let every issued copy land before the CTA can exit.
       for (int s = 0; s < CS; ++s)
         if (cs_armed & (1u << s)) mbar_wait(&cs_full[s], (cs_par >> s) & 1, nullptr, a.status);
+    }
+  } else if (warp == TOKEN_WARP) {
+    // ---------------- TMA producer: token rows (L2-resident) ----------------
+    // A token stage holds 8 boxes of 16 rows x 64 k: one k-step of a 128-row
+    // tile, or up to 8 k-steps of a small tile (see token_span).
+    if (lane == 0) {
+      const uint64_t pol_keep = policy_evict_last();
+      int ts = 0;
+      uint32_t ts_ph = 0, ts_armed = 0, ts_par = 0;
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const int nb = (t.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
+        int nbp;
+        const int kspan = token_span(nb, nbp);
+        for (int k0 = 0; k0 < KT; k0 += kspan) {
+          const int kn = min(kspan, KT - k0);
+          if (!mbar_wait(&tk_empty[ts], ts_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&tk_full[ts], kn * nb * T_BOX_BYTES);
+          ts_armed |= 1u << ts;
+          ts_par = (ts_par & ~(1u << ts)) | (ts_ph << ts);
+          uint8_t* tdst = smem + L::OFF_T + ts * T_STAGE;
+          for (int kl = 0; kl < kn; ++kl)
+            for (int b = 0; b < nb; ++b)
+              tma_load_2d(tdst + (kl * nbp + b) * T_BOX_BYTES, &tm_lhs, &tk_full[ts],
+                          (k0 + kl) * BK, t.row0 + b * T_BOX_ROWS, pol_keep);
+          if (++ts == TS) { ts = 0; ts_ph ^= 1; }
+        }
+      }
       for (int s = 0; s < TS; ++s)
         if (ts_armed & (1u << s)) mbar_wait(&tk_full[s], (ts_par >> s) & 1, nullptr, a.status);
     }
@@ -479,35 +434,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
         const Tile t = get_tile(idx, row_start, tile_prefix, a);
         const int nmma = (t.rows + 15) & ~15;
-        const uint32_t idesc = idesc_bf16(128, nmma, /*a_mn=*/true, /*b_mn=*/false);
+        const int nb = nmma / T_BOX_ROWS;
+        int nbp;
+        const int kspan = token_span(nb, nbp);
+        const uint32_t idesc = idesc_bf16(128, nmma, /*a_mn=*/VAR == kMN, /*b_mn=*/false);
         const int buf = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], ph ^ 1, abort_flag, a.status)) break;
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * NSUB * BT);
         for (int kk = 0; kk < KT; ++kk) {
-          if (!mbar_wait(&a_full[as], as_ph, abort_flag, a.status) ||
-              !mbar_wait(&tk_full[ts], ts_ph, abort_flag, a.status)) {
+          const int kl = kk % kspan;
+          if (kl == 0 && !mbar_wait(&tk_full[ts], ts_ph, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&a_full[as], as_ph, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + L::OFF_A + as * A_STAGE);
-          const uint32_t t_base = smem_u32(smem + L::OFF_T + ts * T_STAGE);
+          const uint32_t t_base =
+              smem_u32(smem + L::OFF_T + ts * T_STAGE) + (uint32_t)(kl * nbp * T_BOX_BYTES);
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bdesc = smem_desc_sw128(t_base + j * 32, 16, 1024);
 #pragma unroll
             for (int s = 0; s < NSUB; ++s) {
               const uint64_t adesc =
-                  smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 2048, A_LBO, A_SBO);
+                  VAR == kMN
+                      ? smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 2048, A_LBO_MN, A_SBO_MN)
+                      : smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 32, 16, 1024);
               umma_bf16(d0 + s * BT, adesc, bdesc, idesc, (kk | j) != 0);
             }
           }
           umma_commit(&a_empty[as]);
-          umma_commit(&tk_empty[ts]);
           if (++as == AS) { as = 0; as_ph ^= 1; }
-          if (++ts == TS) { ts = 0; ts_ph ^= 1; }
+          if (kl == kspan - 1 || kk == KT - 1) {
+            umma_commit(&tk_empty[ts]);
+            if (++ts == TS) { ts = 0; ts_ph ^= 1; }
+          }
         }
         if (!ok) break;
         umma_commit(&acc_full[buf]);
@@ -518,56 +485,161 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp >= DEC_WARP0) {
     // ---------------- decode ----------------
-    // Warps 0-3 of the decode group take sub-tile 0, warps 4-7 sub-tile 1.
-    // A warp decodes two adjacent 64-byte code rows per step (lanes 0-15 row
-    // r, lanes 16-31 row r+1: 128 contiguous bytes, conflict-free), rows
-    // r = 2*(dw%4) + 8j (+1), j = 0..7, covering all 64 rows of the stage.
-    const int dw = warp - DEC_WARP0;
-    const int sub = dw >> 2;
-    const int half = lane >> 4;
-    const int g = lane & 15;          // 8-column group inside the sub-tile
-    int cs = 0, as = 0;
-    uint32_t cs_ph = 0, as_ph = 0;
+    // Two groups of 8 decode warps take alternate stages (group = stage
+    // counter % 2), so two stages are decoded concurrently.
+    const int grp = (warp - DEC_WARP0) / NUM_DEC_WARPS;
+    const int dw = (warp - DEC_WARP0) % NUM_DEC_WARPS;
+    constexpr int es = ScaleTraits<SD>::bytes;
+    constexpr int DELTA = decode_delta<SD>();
+    uint32_t step = 0;  // stage counter over all k-steps of all tiles
     bool ok = true;
-    for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-      for (int kk = 0; kk < KT; ++kk) {
-        bool got = mbar_wait(&cs_full[cs], cs_ph, abort_flag, a.status);
-        got = got && mbar_wait(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* csrc = smem + L::OFF_C + cs * C_STAGE + sub * C_SUB1_OFF;
-        const uint8_t* ssrc = smem + L::OFF_S + cs * L::S_STAGE +
-                              sub * (L::S_STAGE / NSUB) + g * 8 * ScaleTraits<SD>::bytes;
-        uint8_t* adst = smem + L::OFF_A + as * A_STAGE + sub * A_SUB_BYTES + (g >> 3) * A_LBO;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
+    if constexpr (VAR == kMN) {
+      // Warp dw owns sub-tile dw/4 and k-block (dw/2)%2 of every stage; lane
+      // (half, g) decodes the 8-column group g of 8 rows kb*32 + q*8 +
+      // (i ^ half), q = 2*(dw%2) + half, i = 0..7: one scale set per thread
+      // per stage. Lanes 0-15 and 16-31 read 64-byte rows 512 +- 64 bytes
+      // apart (disjoint banks); each quarter-warp stores one 128-byte
+      // swizzled row.
+      const int sub = dw >> 2;
+      const int kb = (dw >> 1) & 1;
+      const int half = lane >> 4;
+      const int g = lane & 15;
+      const int q = 2 * (dw & 1) + half;
+      const int row0 = kb * 32 + q * 8;
+      const int c_even = sub * C_SUB_BYTES + (row0 + half) * (BW / 2) + g * 4;
+      const int c_odd = sub * C_SUB_BYTES + (row0 - half) * (BW / 2) + g * 4;
+      const int a_rows = sub * A_SUB_BYTES + (g >> 3) * A_LBO_MN + (row0 >> 3) * A_SBO_MN;
+      const int a_even = a_rows + half * 128;
+      const int a_odd = a_rows - half * 128;
+      const uint32_t gh = (uint32_t)((g & 7) ^ half) << 4;
+      const int s_off = sub * (L::S_STAGE / NSUB) + (kb * BW + g * 8) * es;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        for (int kk = 0; kk < KT; ++kk, ++step) {
+          if ((int)(step & 1) != grp) continue;
+          const int cs = (int)(step % CS);
+          const uint32_t cs_ph = (step / CS) & 1;
+          const int as = (int)(step % AS);
+          const uint32_t as_ph = (step / AS) & 1;
+          bool got = mbar_wait(&cs_full[cs], cs_ph, abort_flag, a.status);
+          got = got && mbar_wait(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE;
+          uint8_t* astage = smem + L::OFF_A + as * A_STAGE;
           uint32_t m1[4], m2[4];
-          bool two = scale_mults<SD>(ssrc + kb * BW * ScaleTraits<SD>::bytes, m1, m2);
-          two = __any_sync(0xffffffffu, two);
-          if (two) {
+          const bool two =
+              raw_mults<SD, DELTA>(smem + L::OFF_S + cs * L::S_STAGE + s_off, m1, m2);
+          auto run = [&](auto two_tag) {
+            constexpr bool TWO = decltype(two_tag)::value;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (SD == DWM_U8) m1[i] = kBf16Pow2_126x2;
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(
+                  cstage + ((i & 1) ? c_odd : c_even) + i * 64);
+              const uint4 v = decode8<false, TWO>(w, m1, m2);
+              *reinterpret_cast<uint4*>(astage + ((i & 1) ? a_odd : a_even) + i * 128 +
+                                        (gh ^ (uint32_t)(i << 4))) = v;
+            }
+          };
+          if (__any_sync(0xffffffffu, two)) {
+            if (!two) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) m1[i] = pow2_126_minus_delta_x2<DELTA>();
+            }
+            run(std::true_type{});
+          } else {
+            run(std::false_type{});
           }
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const int r = kb * 32 + jj * 8 + 2 * (dw & 3) + half;
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(csrc + r * (BW / 2) + g * 4);
-            const uint4 v = decode8(w, m1, m2, two);
-            const int chunk = (g & 7) ^ (r & 7);
-            *reinterpret_cast<uint4*>(adst + (r >> 3) * A_SBO + (r & 7) * 128 + chunk * 16) = v;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&cs_empty[cs]);
+            mbar_arrive(&a_full[as]);
           }
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&cs_empty[cs]);
-          mbar_arrive(&a_full[as]);
+      }
+    } else {
+      // B200 layout: a stage holds, per sub-tile, 8 column blocks x 4 k-blocks
+      // of 32 words. Warp dw owns sub-tile dw/4 and column blocks
+      // 2*(dw%4), 2*(dw%4)+1; its lane l decodes word l of each of the 8
+      // blocks (the A fragment of an m16n8k16 MMA: columns gid, gid+8, k
+      // pairs t, t+4) and scatters the four bf16x2 pairs into the K-major,
+      // 128-byte swizzled A tile with 32-bit stores (conflict-free: the
+      // eight gid rows land on eight different 16-byte chunks).
+      const int sub = dw >> 2;
+      const int gid = lane >> 2, tig = lane & 3;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        for (int kk = 0; kk < KT; ++kk, ++step) {
+          if ((int)(step & 1) != grp) continue;
+          const int cs = (int)(step % CS);
+          const uint32_t cs_ph = (step / CS) & 1;
+          const int as = (int)(step % AS);
+          const uint32_t as_ph = (step / AS) & 1;
+          bool got = mbar_wait(&cs_full[cs], cs_ph, abort_flag, a.status);
+          got = got && mbar_wait(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + sub * C_SUB_BYTES;
+          const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE + sub * (L::S_STAGE / NSUB);
+          uint8_t* asub = smem + L::OFF_A + as * A_STAGE + sub * A_SUB_BYTES;
+#pragma unroll
+          for (int bi = 0; bi < 2; ++bi) {
+            const int cbl = 2 * (dw & 3) + bi;  // column block inside the sub-tile
+            uint32_t m1[2][2], m2[2][2];         // [k32 half][column gid / gid+8]
+            bool two = false;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              two |= col_mult<SD, DELTA>(sstage + (h * BW + 16 * cbl + gid) * es, m1[h][0],
+                                         m2[h][0]);
+              two |= col_mult<SD, DELTA>(sstage + (h * BW + 16 * cbl + gid + 8) * es, m1[h][1],
+                                         m2[h][1]);
+            }
+            const bool two_any = __any_sync(0xffffffffu, two);
+            if (two_any && SD == DWM_U8) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
+            }
+            const int r0 = 16 * cbl + gid;  // A rows r0 and r0 + 8
+            uint8_t* row_a = asub + (r0 >> 3) * 1024 + (r0 & 7) * 128;
+            uint8_t* row_b = asub + ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(cstage + cbl * 512 +
+                                                                    kb * 128 + lane * 4);
+              uint32_t tv[4];
+              tvals<true>(w, tv);
+              const int h = kb >> 1;
+              uint32_t v0 = hmul2_bf16(tv[0], m1[h][0]);
+              uint32_t v1 = hmul2_bf16(tv[1], m1[h][1]);
+              uint32_t v2 = hmul2_bf16(tv[2], m1[h][0]);
+              uint32_t v3 = hmul2_bf16(tv[3], m1[h][1]);
+              if (two_any) {
+                v0 = hmul2_bf16(v0, m2[h][0]);
+                v1 = hmul2_bf16(v1, m2[h][1]);
+                v2 = hmul2_bf16(v2, m2[h][0]);
+                v3 = hmul2_bf16(v3, m2[h][1]);
+              }
+              // k pair (16 kb + 2 tig) sits in 16-byte chunk 2 kb, k pair
+              // (16 kb + 2 tig + 8) in chunk 2 kb + 1, both at byte 4 tig.
+              const int c0 = 2 * kb, c1 = 2 * kb + 1;
+              *reinterpret_cast<uint32_t*>(row_a + ((c0 ^ (r0 & 7)) << 4) + 4 * tig) = v0;
+              *reinterpret_cast<uint32_t*>(row_b + ((c0 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v1;
+              *reinterpret_cast<uint32_t*>(row_a + ((c1 ^ (r0 & 7)) << 4) + 4 * tig) = v2;
+              *reinterpret_cast<uint32_t*>(row_b + ((c1 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v3;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&cs_empty[cs]);
+            mbar_arrive(&a_full[as]);
+          }
         }
-        if (++cs == CS) { cs = 0; cs_ph ^= 1; }
-        if (++as == AS) { as = 0; as_ph ^= 1; }
       }
     }
   }
@@ -580,11 +652,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// Elementwise dequantisation with the same decode (natural column order).
+// ---------------------------------------------------------------------------
+// Elementwise kernels: dequantisation, layout conversion, tokamax codes.
+// ---------------------------------------------------------------------------
+
+// Raw e2m1 dequantisation with the GEMM's decode (delta = 0: value * scale
+// exactly as the reference's bf16 multiply), natural column order.
 template <int SD>
-__global__ void fp4_dequant_kernel(const uint8_t* __restrict__ codes,
-                                   const uint8_t* __restrict__ scales, int groups, int k, int n,
-                                   uint4* __restrict__ out) {
+__global__ void fp4_dequant_raw_kernel(const uint8_t* __restrict__ codes,
+                                       const uint8_t* __restrict__ scales, int groups, int k,
+                                       int n, uint4* __restrict__ out) {
   const int64_t words_per_row = n / 8;
   const int64_t total = (int64_t)groups * k * words_per_row;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -594,21 +671,106 @@ __global__ void fp4_dequant_kernel(const uint8_t* __restrict__ codes,
     const int64_t g = row / k;
     const int kk = (int)(row - g * k);
     const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[i];
-    const uint8_t* sp =
-        scales + ((g * (k / 32) + kk / 32) * (int64_t)n + (int64_t)c8 * 8) * ScaleTraits<SD>::bytes;
+    const uint8_t* sp = scales + ((g * (k / 32) + kk / 32) * (int64_t)n + (int64_t)c8 * 8) *
+                                     ScaleTraits<SD>::bytes;
     uint32_t m1[4], m2[4];
-    bool two = scale_mults<SD>(sp, m1, m2);
-    if (SD == DWM_U8 && two) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) m1[q] = kBf16Pow2_126x2;
-    }
-    const uint4 v = decode8(w, m1, m2, two);
+    const bool two = raw_mults<SD, 0>(sp, m1, m2);
+    const uint4 v = two ? decode8<false, true>(w, m1, m2) : decode8<false, false>(w, m1, m2);
     uint4 o;
     o.x = __byte_perm(v.x, v.y, 0x5410);  // columns 0,1
     o.y = __byte_perm(v.z, v.w, 0x5410);  // columns 2,3
     o.z = __byte_perm(v.x, v.y, 0x7632);  // columns 4,5
     o.w = __byte_perm(v.z, v.w, 0x7632);  // columns 6,7
     out[i] = o;
+  }
+}
+
+// B200-layout dequantisation: one word = one lane's A fragment of a block.
+template <int SD>
+__global__ void fp4_dequant_b200_kernel(const uint32_t* __restrict__ codes,
+                                        const uint8_t* __restrict__ scales, int groups, int k,
+                                        int n, uint16_t* __restrict__ out) {
+  const int64_t total = (int64_t)groups * k * n / 8;
+  const int kb16 = k / 16, cb16 = n / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int l = (int)(i & 31);
+    const int64_t blk = i >> 5;
+    const int kb = (int)(blk % kb16);
+    const int64_t gc = blk / kb16;
+    const int cb = (int)(gc % cb16);
+    const int64_t g = gc / cb16;
+    uint32_t tv[4];
+    tvals<true>(codes[i], tv);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        int dk, dc;
+        b200_nibble_coord(l, 2 * p + hh, dk, dc);
+        const int kk = 16 * kb + dk, col = 16 * cb + dc;
+        uint32_t m1, m2;
+        const bool two = col_mult<SD, 0>(
+            scales + ((g * (k / 32) + kk / 32) * (int64_t)n + col) * ScaleTraits<SD>::bytes, m1,
+            m2);
+        uint32_t v = hmul2_bf16(tv[p], m1);
+        if (two) v = hmul2_bf16(v, m2);
+        out[(g * k + kk) * (int64_t)n + col] = (uint16_t)(hh ? (v >> 16) : (v & 0xFFFFu));
+      }
+    }
+  }
+}
+
+// raw [g, k, n/2] (column-pair bytes) -> B200 words.
+__global__ void fp4_to_b200_kernel(const uint8_t* __restrict__ raw, uint32_t* __restrict__ out,
+                                   int groups, int k, int n) {
+  const int64_t total = (int64_t)groups * k * n / 8;
+  const int kb16 = k / 16, cb16 = n / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int l = (int)(i & 31);
+    const int64_t blk = i >> 5;
+    const int kb = (int)(blk % kb16);
+    const int64_t gc = blk / kb16;
+    const int cb = (int)(gc % cb16);
+    const int64_t g = gc / cb16;
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int dk, dc;
+      b200_nibble_coord(l, j, dk, dc);
+      const int col = 16 * cb + dc;
+      const uint8_t b = raw[(g * k + 16 * kb + dk) * (int64_t)(n / 2) + col / 2];
+      word |= (uint32_t)((col & 1) ? (b >> 4) : (b & 0xF)) << (4 * j);
+    }
+    out[i] = b200_swizzle_word(word);
+  }
+}
+
+// B200 words -> raw [g, k, n/2] bytes (one raw byte = columns 2c, 2c+1).
+__global__ void fp4_from_b200_kernel(const uint32_t* __restrict__ b200, uint8_t* __restrict__ raw,
+                                     int groups, int k, int n) {
+  const int64_t total = (int64_t)groups * k * (n / 2);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int cp = (int)(i % (n / 2));
+    const int64_t gk = i / (n / 2);
+    const int kk = (int)(gk % k);
+    const int64_t g = gk / k;
+    uint32_t byte = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int col = 2 * cp + h;
+      const int dk = kk & 15, dc = col & 15;
+      // Invert b200_nibble_coord: dc = gid + 8*bit1(j), dk = 2t + bit0(j) + 8*bit2(j).
+      const int gid = dc & 7, t = (dk & 7) >> 1;
+      const int j = (dk & 1) | ((dc >> 3) << 1) | ((dk >> 3) << 2);
+      const int l = gid * 4 + t;
+      const uint32_t w =
+          b200_unswizzle_word(b200[b200_word_index(g, col / 16, kk / 16, l, n, k)]);
+      byte |= ((w >> (4 * j)) & 0xFu) << (4 * h);
+    }
+    raw[i] = (uint8_t)byte;
   }
 }
 
@@ -630,7 +792,11 @@ __global__ void fp4_codes_convert_kernel(const uint8_t* __restrict__ in, uint8_t
   }
 }
 
-template <int SD>
+// ---------------------------------------------------------------------------
+// Host launch
+// ---------------------------------------------------------------------------
+
+template <int SD, int VAR>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
@@ -640,9 +806,14 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
                           (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)n / 2,
-                      (uint64_t)n_local * k, (uint64_t)n / 2, BW / 2, BK,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (VAR == kMN)
+    rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)n / 2,
+                        (uint64_t)n_local * k, (uint64_t)n / 2, BW / 2, BK,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+  else  // rows = column blocks, each (k/16) blocks x 32 words
+    rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes,
+                        (uint64_t)(k / 16) * 32, (uint64_t)n_local * (n / 16),
+                        (uint64_t)(k / 16) * 128, 4 * 32, BW / 16, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   rc = encode_tmap_2d(&tm_scales, ScaleTraits<SD>::tma, scales, (uint64_t)n,
                       (uint64_t)n_local * (k / 32), (uint64_t)n * ScaleTraits<SD>::bytes, BW, 2,
@@ -653,7 +824,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmm_fp4_kernel<SD>,
+    rc = check_cuda(cudaFuncSetAttribute(gmm_fp4_kernel<SD, VAR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC),
                     "gmm smem attribute");
     if (rc) return rc;
@@ -675,12 +846,86 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.n_tiles = n / (NSUB * BW);
   a.status = status_ptr();
-  gmm_fp4_kernel<SD><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes, tm_scales,
-                                                                   a);
+  gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
+                                                                       tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmm_fp4 launch");
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline unsigned grid_for(int64_t work, int threads, int per_sm = 16) {
+  int64_t b = (work + threads - 1) / threads;
+  int64_t cap = (int64_t)num_sms() * per_sm;
+  return (unsigned)std::max<int64_t>(1, std::min(b, cap));
+}
+
+// Argument checks shared by the GEMM entry points.
+static int validate(const void* lhs, const void* codes, int codes_format, const void* scales,
+                    int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k,
+                    int n, int group_offset, int num_local_groups, int act, int out_dtype,
+                    void* out) {
+  DWM_CHECK_ARG(codes_format == DWM_FP4_E2M1 || codes_format == DWM_FP4_B200,
+                "gmm_fp4 takes e2m1 nibbles (raw or B200 layout); convert tokamax codes once "
+                "with dwm_fp4_codes_convert");
+  DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
+                "scale dtype must be u8 (e8m0), bf16 or f32");
+  DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
+  DWM_CHECK_ARG(act == DWM_ACT_NONE || act == DWM_ACT_SWIGLU || act == DWM_ACT_SWIGLU_CLAMP,
+                "unknown activation %d", act);
+  DWM_CHECK_ARG(m >= 0 && k > 0 && n > 0, "bad shape m=%d k=%d n=%d", m, k, n);
+  DWM_CHECK_ARG(k % BK == 0, "k=%d must be a multiple of %d", k, BK);
+  DWM_CHECK_ARG(n % (NSUB * BW) == 0, "n=%d must be a multiple of 256", n);
+  DWM_CHECK_ARG(num_groups >= 1 && num_groups <= MAX_GROUPS, "num_groups=%d out of [1, %d]",
+                num_groups, MAX_GROUPS);
+  DWM_CHECK_ARG(group_offset >= 0 && num_local_groups >= 0 &&
+                    group_offset + num_local_groups <= num_groups,
+                "group_offset=%d + num_local_groups=%d exceeds num_groups=%d", group_offset,
+                num_local_groups, num_groups);
+  DWM_CHECK_ARG(group_sizes && out && (m == 0 || lhs), "NULL pointer");
+  DWM_CHECK_ARG(num_local_groups == 0 || (codes && scales), "NULL weights");
+  DWM_CHECK_ARG(aligned16(lhs) && aligned16(codes) && aligned16(scales) && aligned16(out),
+                "pointers must be 16-byte aligned");
+  return DWM_OK;
+}
+
+// variant: 0 = choose, 1 = tcgen05 (shared-memory decode), 2 = mma.sync
+// decode kernel (B200 layout only) with 8- or 16-row token tiles by the
+// average rows per local group, 3 / 4 = the same with 8 / 16-row tiles. The
+// automatic choice sends the B200 layout to mma.sync when the local groups
+// average at most 16 rows.
+static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
+               int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
+               int group_offset, int num_local_groups, int act, float act_limit, int out_dtype,
+               int zero_init, void* out, int variant, cudaStream_t s) {
+  const int n_out = act == DWM_ACT_NONE ? n : n / 2;
+  const size_t es = out_dtype == DWM_F32 ? 4 : 2;
+  if (m == 0) return DWM_OK;
+  if (num_local_groups == 0) {
+    if (zero_init)
+      return check_cuda(cudaMemsetAsync(out, 0, (size_t)m * n_out * es, s), "gmm zero");
+    return DWM_OK;
+  }
+  const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
+  if (variant == 0 && codes_format == DWM_FP4_B200) variant = avg <= 16 ? 2 : 1;
+  if (variant >= 2)
+    return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                      group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
+                      variant == 3 ? 1 : variant == 4 ? 2 : (avg <= 8 ? 1 : 2), s);
+#define DWM_GMM_LAUNCH(SD, VAR)                                                          \
+  return launch<SD, VAR>(lhs, codes, scales, group_sizes, num_groups, m, k, n,          \
+                         group_offset, num_local_groups, act, act_limit, out_dtype,      \
+                         zero_init, out, s)
+#define DWM_GMM_BY_SCALE(VAR)                                   \
+  do {                                                          \
+    if (scale_dtype == DWM_U8) DWM_GMM_LAUNCH(DWM_U8, VAR);     \
+    if (scale_dtype == DWM_BF16) DWM_GMM_LAUNCH(DWM_BF16, VAR); \
+    DWM_GMM_LAUNCH(DWM_F32, VAR);                               \
+  } while (0)
+  if (codes_format == DWM_FP4_B200) DWM_GMM_BY_SCALE(kKS);
+  DWM_GMM_BY_SCALE(kMN);
+#undef DWM_GMM_BY_SCALE
+#undef DWM_GMM_LAUNCH
+}
 
 }  // namespace gmm
 }  // namespace dwm
@@ -692,58 +937,40 @@ extern "C" int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format,
                            int num_groups, int m, int k, int n, int group_offset,
                            int num_local_groups, int act, float act_limit, int out_dtype,
                            int zero_init, void* out, void* stream) {
-  DWM_CHECK_ARG(codes_format == DWM_FP4_E2M1,
-                "gmm_fp4 takes e2m1 nibbles; convert tokamax codes once with "
-                "dwm_fp4_codes_convert");
-  DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
-                "scale dtype must be u8 (e8m0), bf16 or f32");
-  DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
-  DWM_CHECK_ARG(act == DWM_ACT_NONE || act == DWM_ACT_SWIGLU || act == DWM_ACT_SWIGLU_CLAMP,
-                "unknown activation %d", act);
-  DWM_CHECK_ARG(m >= 0 && k > 0 && n > 0, "bad shape m=%d k=%d n=%d", m, k, n);
-  DWM_CHECK_ARG(k % gmm::BK == 0, "k=%d must be a multiple of %d", k, gmm::BK);
-  DWM_CHECK_ARG(n % (gmm::NSUB * gmm::BW) == 0, "n=%d must be a multiple of 256", n);
-  DWM_CHECK_ARG(num_groups >= 1 && num_groups <= gmm::MAX_GROUPS,
-                "num_groups=%d out of [1, %d]", num_groups, gmm::MAX_GROUPS);
-  DWM_CHECK_ARG(group_offset >= 0 && num_local_groups >= 0 &&
-                    group_offset + num_local_groups <= num_groups,
-                "group_offset=%d + num_local_groups=%d exceeds num_groups=%d", group_offset,
-                num_local_groups, num_groups);
-  DWM_CHECK_ARG(group_sizes && out && (m == 0 || lhs), "NULL pointer");
-  DWM_CHECK_ARG(num_local_groups == 0 || (codes && scales), "NULL weights");
-  DWM_CHECK_ARG(gmm::aligned16(lhs) && gmm::aligned16(codes) && gmm::aligned16(scales) &&
-                    gmm::aligned16(out),
-                "pointers must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int n_out = act == DWM_ACT_NONE ? n : n / 2;
-  const size_t es = out_dtype == DWM_F32 ? 4 : 2;
-  if (m == 0) return DWM_OK;
-  if (num_local_groups == 0) {
-    if (zero_init)
-      return check_cuda(cudaMemsetAsync(out, 0, (size_t)m * n_out * es, s), "gmm zero");
-    return DWM_OK;
-  }
-  switch (scale_dtype) {
-    case DWM_U8:
-      return gmm::launch<DWM_U8>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                 group_offset, num_local_groups, act, act_limit, out_dtype,
-                                 zero_init, out, s);
-    case DWM_BF16:
-      return gmm::launch<DWM_BF16>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                   group_offset, num_local_groups, act, act_limit, out_dtype,
-                                   zero_init, out, s);
-    default:
-      return gmm::launch<DWM_F32>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                  group_offset, num_local_groups, act, act_limit, out_dtype,
-                                  zero_init, out, s);
-  }
+  int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
+                         m, k, n, group_offset, num_local_groups, act, out_dtype, out);
+  if (rc) return rc;
+  return gmm::run(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups, m, k,
+                  n, group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
+                  0, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int dwm_fp4_dequant(const void* codes, const void* scales, int scale_dtype,
-                               int groups, int k, int n, void* out, void* stream) {
+extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format,
+                                   const void* scales, int scale_dtype,
+                                   const int32_t* group_sizes, int num_groups, int m, int k,
+                                   int n, int group_offset, int num_local_groups, int act,
+                                   float act_limit, int out_dtype, int zero_init, void* out,
+                                   int variant, void* stream) {
+  DWM_CHECK_ARG(variant >= 0 && variant <= 4,
+                "variant must be 0 (auto), 1 (tcgen05) or 2-4 (mma.sync decode kernel)");
+  DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
+                "explicit variants need the B200 layout");
+  int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
+                         m, k, n, group_offset, num_local_groups, act, out_dtype, out);
+  if (rc) return rc;
+  return gmm::run(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups, m, k,
+                  n, group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
+                  variant, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dwm_fp4_dequant(const void* codes, int codes_format, const void* scales,
+                               int scale_dtype, int groups, int k, int n, void* out,
+                               void* stream) {
   DWM_CHECK_ARG(codes && scales && out, "NULL pointer");
-  DWM_CHECK_ARG(groups >= 0 && k > 0 && n > 0 && k % 32 == 0 && n % 8 == 0,
-                "bad shape groups=%d k=%d n=%d (k %% 32, n %% 8)", groups, k, n);
+  DWM_CHECK_ARG(codes_format == DWM_FP4_E2M1 || codes_format == DWM_FP4_B200,
+                "codes_format must be DWM_FP4_E2M1 or DWM_FP4_B200");
+  DWM_CHECK_ARG(groups >= 0 && k > 0 && n > 0 && k % 32 == 0 && n % 16 == 0,
+                "bad shape groups=%d k=%d n=%d (k %% 32, n %% 16)", groups, k, n);
   DWM_CHECK_ARG(gmm::aligned16(out) && (reinterpret_cast<uintptr_t>(codes) & 3) == 0,
                 "misaligned pointer");
   DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
@@ -752,17 +979,47 @@ extern "C" int dwm_fp4_dequant(const void* codes, const void* scales, int scale_
   if (total == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int threads = 256;
-  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148LL * 16);
-  auto c = static_cast<const uint8_t*>(codes);
+  const unsigned blocks = gmm::grid_for(total, threads);
   auto sc = static_cast<const uint8_t*>(scales);
-  auto o = static_cast<uint4*>(out);
-  if (scale_dtype == DWM_U8)
-    gmm::fp4_dequant_kernel<DWM_U8><<<(int)blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
-  else if (scale_dtype == DWM_BF16)
-    gmm::fp4_dequant_kernel<DWM_BF16><<<(int)blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
-  else
-    gmm::fp4_dequant_kernel<DWM_F32><<<(int)blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
+  if (codes_format == DWM_FP4_B200) {
+    auto cw = static_cast<const uint32_t*>(codes);
+    auto o = static_cast<uint16_t*>(out);
+    if (scale_dtype == DWM_U8)
+      gmm::fp4_dequant_b200_kernel<DWM_U8><<<blocks, threads, 0, s>>>(cw, sc, groups, k, n, o);
+    else if (scale_dtype == DWM_BF16)
+      gmm::fp4_dequant_b200_kernel<DWM_BF16><<<blocks, threads, 0, s>>>(cw, sc, groups, k, n, o);
+    else
+      gmm::fp4_dequant_b200_kernel<DWM_F32><<<blocks, threads, 0, s>>>(cw, sc, groups, k, n, o);
+  } else {
+    auto c = static_cast<const uint8_t*>(codes);
+    auto o = static_cast<uint4*>(out);
+    if (scale_dtype == DWM_U8)
+      gmm::fp4_dequant_raw_kernel<DWM_U8><<<blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
+    else if (scale_dtype == DWM_BF16)
+      gmm::fp4_dequant_raw_kernel<DWM_BF16><<<blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
+    else
+      gmm::fp4_dequant_raw_kernel<DWM_F32><<<blocks, threads, 0, s>>>(c, sc, groups, k, n, o);
+  }
   return check_cuda(cudaGetLastError(), "fp4_dequant launch");
+}
+
+extern "C" int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int n, int inverse,
+                               void* stream) {
+  DWM_CHECK_ARG(in && out && in != out, "NULL or aliased pointers (out-of-place only)");
+  DWM_CHECK_ARG(groups >= 0 && k > 0 && n > 0 && k % 16 == 0 && n % 16 == 0,
+                "bad shape groups=%d k=%d n=%d (k %% 16, n %% 16)", groups, k, n);
+  DWM_CHECK_ARG(((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 3) == 0,
+                "pointers must be 4-byte aligned");
+  const int64_t words = (int64_t)groups * k * n / 8;
+  if (words == 0) return DWM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!inverse)
+    gmm::fp4_to_b200_kernel<<<gmm::grid_for(words, 256), 256, 0, s>>>(
+        static_cast<const uint8_t*>(in), static_cast<uint32_t*>(out), groups, k, n);
+  else
+    gmm::fp4_from_b200_kernel<<<gmm::grid_for(words * 4, 256), 256, 0, s>>>(
+        static_cast<const uint32_t*>(in), static_cast<uint8_t*>(out), groups, k, n);
+  return check_cuda(cudaGetLastError(), "fp4_to_b200 launch");
 }
 
 extern "C" int dwm_fp4_codes_convert(const void* in, void* out, size_t nbytes, int from_format,
@@ -778,9 +1035,7 @@ extern "C" int dwm_fp4_codes_convert(const void* in, void* out, size_t nbytes, i
     return check_cuda(cudaMemcpyAsync(out, in, nbytes, cudaMemcpyDeviceToDevice, s),
                       "codes copy");
   }
-  const int threads = 256;
-  const size_t blocks = std::min<size_t>((nbytes + threads - 1) / threads, 148 * 32);
-  gmm::fp4_codes_convert_kernel<<<(unsigned)blocks, threads, 0, s>>>(
+  gmm::fp4_codes_convert_kernel<<<gmm::grid_for((int64_t)nbytes, 256), 256, 0, s>>>(
       static_cast<const uint8_t*>(in), static_cast<uint8_t*>(out), nbytes,
       to_format == DWM_FP4_TOKAMAX);
   return check_cuda(cudaGetLastError(), "codes_convert launch");

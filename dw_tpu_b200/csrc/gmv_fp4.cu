@@ -1,0 +1,574 @@
+// FP4 grouped matmul for decode-sized groups (a few token rows per expert).
+//
+// At decode, a tcgen05 UMMA of M = 128 weight columns x K = 16 costs about
+// 138 cycles whatever its N (measured on B200 for N = 16..256), so with N =
+// the 2-16 token rows of an expert it consumes only 1 KiB of FP4 codes per
+// 138 cycles: about 2 TB/s across the chip, a third of HBM. This kernel runs
+// the same math on mma.sync.m16n8k16 (bf16 in, f32 accumulate): weights are
+// decoded straight from the B200 layout into A-fragment registers (one 32-bit
+// word per lane per 16x16 block, one PRMT per bf16 pair), token rows are the
+// n8 tiles, and nothing decoded touches shared or tensor memory.
+//
+// The kernel is bound by instruction issue, not by the MMA: at the HBM
+// roofline an SM must retire one 32-bit code word (8 weights) per lane every
+// ~23 issue slots. So the per-word work is kept to the load, the 4-PRMT
+// decode and the MMA:
+//   * E8M0 scales (the common case) are applied after the MMA, to the f32
+//     partial of each 32-deep k block (partial * 2^(c-127)), instead of to
+//     every decoded weight. The decode yields value * 2^-126 (fp4_decode.cuh);
+//     token fragments are pre-scaled by 2^64 and the k-block factor is
+//     2^(c-65), all exact powers of two, so the result equals the reference's
+//     bf16(value * scale) x bf16 token products (E0901:84-95) up to the f32
+//     summation order. Codes 0 (scale +0) and 1..192 take this path; a k block
+//     holding a code above 192 (scales >= 2^66, including the 255 = inf code)
+//     falls back to multiplying the weights in bf16 exactly like the reference.
+//   * bf16 / f32 scales (reference: cast to bf16, one bf16 multiply) are
+//     multiplied into the decoded weights, which reproduces that rounding.
+//   * each warp streams its own tasks through a private ring of S stages,
+//     filled by five 2-D TMA copies per stage (tokens, two code tiles, two
+//     scale tiles) issued by lane 0, with prefetch running ahead across task
+//     boundaries; token tiles land 128-byte swizzled so B-fragment loads are
+//     bank-conflict free.
+#include "fp4_decode.cuh"
+
+namespace dwm {
+namespace gmv {
+
+using namespace fp4;
+
+constexpr int MAX_GROUPS = 1024;
+constexpr int KSTAGE = 64;        // k per ring stage
+constexpr int CODE_BYTES = 2048;  // 4 column blocks x 4 k16 blocks x 32 words
+constexpr uint32_t kBf16x2_2p64 = 0x5F805F80u;   // bf16 2^64, both halves
+constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
+constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
+
+// Ring depth per warp (stages of 64 k) for 1 and 2 n8 token tiles.
+#ifndef DWM_GMV_STAGES1
+#define DWM_GMV_STAGES1 4
+#endif
+#ifndef DWM_GMV_STAGES2
+#define DWM_GMV_STAGES2 3
+#endif
+// 1: feed the raw decode (value * 2^-126, a bf16 subnormal for 0.5) to the
+// MMA on the E8M0 path; 0: first normalise it by 2^62 (4 more multiplies per
+// word, exact either way).
+#ifndef DWM_GMV_RAW_TVALS
+#define DWM_GMV_RAW_TVALS 1
+#endif
+// 1: waiting warps sleep between mbarrier polls (leaving issue slots to the
+// warps that have data).
+#ifndef DWM_GMV_BACKOFF
+#define DWM_GMV_BACKOFF 0
+#endif
+
+template <int SD, int NT>
+struct Cfg {
+  static constexpr bool POST = SD == DWM_U8;  // E8M0: scale the f32 partials
+  static constexpr int es = ScaleTraits<SD>::bytes;
+  static constexpr int S = NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2;
+  static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
+  // Largest E8M0 code of the post-MMA path: the k-block factor 2^(c-65)
+  // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
+  static constexpr uint32_t POST_MAX = RAW ? 192u : 254u;
+  static constexpr int TOK = 8 * NT * KSTAGE * 2;  // token tile, 128-byte rows
+  // 2 scale tiles of 2 k32 rows x 32 columns, each tile 128-byte aligned.
+  static constexpr int SC_TILE = 64 * es < 128 ? 128 : 64 * es;
+  static constexpr int SC = 2 * SC_TILE;
+  static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 1023) & ~1023;
+  static constexpr int WARPS = (NT == 1 && SD != DWM_F32) ? 16 : 12;
+  static constexpr int OFF_BAR = WARPS * WARP_BYTES;
+  static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
+  static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
+  static constexpr int BYTES = OFF_TASKS + (MAX_GROUPS + 1) * 4;
+  static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment (128-byte swizzle)
+  static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * 64 * es;
+  static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
+  static_assert(TOK % 1024 == 0 && (S * TOK) % 1024 == 0, "token tiles need 1 KiB alignment");
+};
+
+struct Args {
+  const int32_t* group_sizes;
+  int num_groups, group_offset, n_local;
+  int m, k, n;
+  int act;
+  float limit;
+  int out_f32;
+  int zero_init;
+  void* out;
+  int ldo;
+  int quads;  // tasks per row chunk: n / 64
+  int* status;
+};
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d = a * b (accumulator starts at zero).
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                            uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+struct Task {
+  int g;     // local group
+  int quad;  // 64-column task inside the group
+  int row0;  // first lhs row of the chunk
+  int rows;  // valid rows in the chunk (1..8*NT)
+};
+
+template <int NT>
+__device__ __forceinline__ Task get_task(int idx, const int* row_start, const int* task_prefix,
+                                         const Args& a) {
+  int lo = 0, hi = a.n_local;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (task_prefix[mid] <= idx) lo = mid; else hi = mid;
+  }
+  Task t;
+  t.g = lo;
+  const int local = idx - task_prefix[lo];
+  const int chunk = local / a.quads;
+  t.quad = local - chunk * a.quads;
+  const int gs0 = row_start[a.group_offset + lo];
+  const int gsn = row_start[a.group_offset + lo + 1] - gs0;
+  t.row0 = gs0 + chunk * 8 * NT;
+  t.rows = min(8 * NT, gsn - chunk * 8 * NT);
+  return t;
+}
+
+// First column block of each of the task's two block pairs: adjacent 64
+// columns, or the gate and up halves for SwiGLU.
+__device__ __forceinline__ void task_blocks(const Task& t, const Args& a, int& cb0, int& cb1) {
+  if (a.act == DWM_ACT_NONE) {
+    cb0 = 4 * t.quad;
+    cb1 = cb0 + 2;
+  } else {
+    cb0 = 2 * t.quad;
+    cb1 = a.n / 32 + 2 * t.quad;
+  }
+}
+
+template <int SD, int NT>
+__global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
+    gmv_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
+                   const __grid_constant__ CUtensorMap tm_codes,
+                   const __grid_constant__ CUtensorMap tm_scales, const Args a) {
+  using C = Cfg<SD, NT>;
+  constexpr int S = C::S;
+  constexpr int es = C::es;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  int* row_start = reinterpret_cast<int*>(smem + C::OFF_ROWS);
+  int* task_prefix = reinterpret_cast<int*>(smem + C::OFF_TASKS);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint8_t* tok_s = smem + warp * C::WARP_BYTES;  // [S][TOK]
+  uint8_t* code_s = tok_s + S * C::TOK;           // [S][CODE_BYTES]
+  uint8_t* sc_s = code_s + S * CODE_BYTES;        // [S][SC]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR) + warp * S;
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tm_lhs);
+    tma_prefetch_desc(&tm_codes);
+    tma_prefetch_desc(&tm_scales);
+  }
+  if (warp == 0) {
+    // Row starts over all groups, then the task prefix over local groups.
+    const int G = a.num_groups;
+    const int per = (G + 31) / 32;
+    int sum = 0;
+    for (int i = 0; i < per; ++i) {
+      const int g = lane * per + i;
+      if (g < G) {
+        int v = a.group_sizes[g];
+        if (v < 0) { report(a.status, DWM_DEV_BAD_INDEX); v = 0; }
+        sum += v;
+      }
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - sum;
+    for (int i = 0; i < per; ++i) {
+      const int g = lane * per + i;
+      if (g < G) {
+        row_start[g] = min(run, a.m);
+        run += max(a.group_sizes[g], 0);
+      }
+    }
+    if (lane == 31) {
+      row_start[G] = min(run, a.m);
+      if (run > a.m) report(a.status, DWM_DEV_BAD_INDEX);
+    }
+    __syncwarp();
+    const int NL = a.n_local;
+    const int per2 = (NL + 31) / 32;
+    int tsum = 0;
+    for (int i = 0; i < per2; ++i) {
+      const int g = lane * per2 + i;
+      if (g < NL) {
+        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        tsum += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
+      }
+    }
+    int tincl = tsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, tincl, o);
+      if (lane >= o) tincl += y;
+    }
+    int trun = tincl - tsum;
+    for (int i = 0; i < per2; ++i) {
+      const int g = lane * per2 + i;
+      if (g < NL) {
+        task_prefix[g] = trun;
+        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        trun += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
+      }
+    }
+    if (lane == 31) task_prefix[NL] = trun;
+  }
+  __syncthreads();
+  const int total = task_prefix[a.n_local];
+
+  if (a.zero_init) {
+    const int oes = a.out_f32 ? 4 : 2;
+    const int lo = row_start[a.group_offset];
+    const int hi = row_start[a.group_offset + a.n_local];
+    const int64_t n16 = (int64_t)a.ldo * oes / 16;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    uint4* o = reinterpret_cast<uint4*>(a.out);
+    for (int64_t i = tid; i < (int64_t)lo * n16; i += stride) o[i] = z;
+    for (int64_t i = (int64_t)hi * n16 + tid; i < (int64_t)a.m * n16; i += stride) o[i] = z;
+  }
+
+  const int gid = lane >> 2, tig = lane & 3;
+  const int NSTAGE = a.k / KSTAGE;
+  const int wstride = gridDim.x * C::WARPS;
+  const int first = blockIdx.x * C::WARPS + warp;
+
+  // ---- producer state (lane 0): the next (task, stage) to fetch ----
+  uint64_t pol_stream = 0, pol_keep = 0;
+  int iss_idx = first, iss_st = 0;
+  Task iss_t{};
+  int iss_cb0 = 0, iss_cb1 = 0;
+  uint32_t issued = 0;  // stages issued so far (ring sequence)
+  auto issue_one = [&]() {
+    const int slot = (int)(issued % S);
+    uint64_t* bar = &bars[slot];
+    mbar_arrive_expect_tx(bar, C::TX);
+    const int x_codes = iss_st * 4 * 32;
+    const int y_blocks = iss_t.g * (a.n / 16);
+    const int y_scales = iss_t.g * (a.k / 32) + iss_st * 2;
+    tma_load_2d(tok_s + slot * C::TOK, &tm_lhs, bar, iss_st * KSTAGE, iss_t.row0, pol_keep);
+    tma_load_2d(code_s + slot * CODE_BYTES, &tm_codes, bar, x_codes, y_blocks + iss_cb0,
+                pol_stream);
+    tma_load_2d(code_s + slot * CODE_BYTES + 1024, &tm_codes, bar, x_codes, y_blocks + iss_cb1,
+                pol_stream);
+    tma_load_2d(sc_s + slot * C::SC, &tm_scales, bar, 16 * iss_cb0, y_scales, pol_stream);
+    tma_load_2d(sc_s + slot * C::SC + C::SC_TILE, &tm_scales, bar, 16 * iss_cb1, y_scales,
+                pol_stream);
+    ++issued;
+    if (++iss_st == NSTAGE) {
+      iss_st = 0;
+      iss_idx += wstride;
+      if (iss_idx < total) {
+        iss_t = get_task<NT>(iss_idx, row_start, task_prefix, a);
+        task_blocks(iss_t, a, iss_cb0, iss_cb1);
+      }
+    }
+  };
+  if (lane == 0 && first < total) {
+    pol_stream = policy_evict_first();
+    pol_keep = policy_evict_last();
+    iss_t = get_task<NT>(first, row_start, task_prefix, a);
+    task_blocks(iss_t, a, iss_cb0, iss_cb1);
+    while (issued < (uint32_t)S && iss_idx < total) issue_one();
+  }
+  __syncwarp();
+
+  uint32_t seq = 0;  // stages consumed
+  bool ok = true;
+  for (int idx = first; idx < total && ok; idx += wstride) {
+    const Task t = get_task<NT>(idx, row_start, task_prefix, a);
+    int cb0, cb1;
+    task_blocks(t, a, cb0, cb1);
+
+    float acc[4][NT][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.0f;
+
+    for (int st = 0; st < NSTAGE; ++st, ++seq) {
+      const int slot = (int)(seq % S);
+      const bool got =
+          mbar_wait<DWM_GMV_BACKOFF != 0>(&bars[slot], (seq / S) & 1, nullptr, a.status);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* tok = tok_s + slot * C::TOK;
+      const uint8_t* code = code_s + slot * CODE_BYTES;
+      const uint8_t* sc = sc_s + slot * C::SC;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // 32-deep k block inside the stage
+        // Scales of the lane's columns: block i, column gid (+8 for hc = 1);
+        // tile i/2 holds 2 rows (k32 blocks) of 32 columns.
+        uint32_t code8[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int hc = 0; hc < 2; ++hc) {
+            const uint8_t* p =
+                sc + (i >> 1) * C::SC_TILE + (h * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
+            if constexpr (SD == DWM_U8) {
+              code8[i][hc] = *p;
+            } else if constexpr (SD == DWM_BF16) {
+              code8[i][hc] = *reinterpret_cast<const uint16_t*>(p);
+            } else {
+              code8[i][hc] = f32_to_bf16_bits(*reinterpret_cast<const float*>(p));
+            }
+          }
+        bool slow = !C::POST;
+        if constexpr (C::POST) {
+          bool big = false;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            big |= (code8[i][0] > C::POST_MAX) | (code8[i][1] > C::POST_MAX);
+          slow = __any_sync(0xffffffffu, big);
+        }
+        // Per-column factors applied to the partial (fast path) or to the
+        // weights (slow path).
+        float post[4][2];
+        uint32_t wmul[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int hc = 0; hc < 2; ++hc) {
+            const uint32_t c = code8[i][hc];
+            if constexpr (C::POST) {
+              if (C::RAW)
+                post[i][hc] = slow ? 1.0f : (c ? __uint_as_float((c + 62u) << 23) : 0.0f);
+              else
+                post[i][hc] = slow ? 1.0f : __uint_as_float(c << 23);  // c = 0 -> +0
+              wmul[i][hc] = (c << 7) * 0x10001u;  // bf16 2^(c-127), c = 0 -> +0
+            } else {
+              post[i][hc] = 1.0f;
+              wmul[i][hc] = c * 0x10001u;  // the bf16 scale, both halves
+            }
+          }
+        float part[4][NT][4];
+#pragma unroll
+        for (int kk2 = 0; kk2 < 2; ++kk2) {
+          const int kk = 2 * h + kk2;  // k16 block inside the stage
+          uint32_t b[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int r = nt * 8 + gid;  // token row; the 128-byte swizzle XORs chunk with r%8
+            const uint8_t* row = tok + r * 128 + 4 * tig;
+            uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk) ^ gid) << 4));
+            uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk + 1) ^ gid) << 4));
+            if (r >= t.rows) b0 = b1 = 0u;
+            if constexpr (C::POST) {
+              b0 = hmul2_bf16(b0, kBf16x2_2p64);
+              b1 = hmul2_bf16(b1, kBf16x2_2p64);
+            }
+            b[nt][0] = b0;
+            b[nt][1] = b1;
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t w =
+                *reinterpret_cast<const uint32_t*>(code + i * 512 + kk * 128 + lane * 4);
+            uint32_t af[4];
+            tvals<true>(w, af);
+            if (slow) {
+              const uint32_t m1 = C::POST ? kBf16x2_2p62 : kBf16x2_2p126;
+              af[0] = hmul2_bf16(hmul2_bf16(af[0], m1), wmul[i][0]);
+              af[1] = hmul2_bf16(hmul2_bf16(af[1], m1), wmul[i][1]);
+              af[2] = hmul2_bf16(hmul2_bf16(af[2], m1), wmul[i][0]);
+              af[3] = hmul2_bf16(hmul2_bf16(af[3], m1), wmul[i][1]);
+            } else if (!C::RAW) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) af[j] = hmul2_bf16(af[j], kBf16x2_2p62);
+            }
+            if constexpr (C::POST) {
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                if (kk2 == 0)
+                  mma_16816_z(part[i][nt], af, b[nt][0], b[nt][1]);
+                else
+                  mma_16816(part[i][nt], af, b[nt][0], b[nt][1]);
+              }
+            } else {
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) mma_16816(acc[i][nt], af, b[nt][0], b[nt][1]);
+            }
+          }
+        }
+        if constexpr (C::POST) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                acc[i][nt][e] = fmaf(part[i][nt][e], post[i][e >> 1], acc[i][nt][e]);
+        }
+      }
+      __syncwarp();  // every lane is done with this slot
+      if (lane == 0 && iss_idx < total) issue_one();
+      __syncwarp();
+    }
+    if (!ok) break;
+
+    // Epilogue: c0,c1 = (column gid, tokens 2t, 2t+1), c2,c3 = (column gid+8, ...).
+    const int colbase[4] = {16 * cb0, 16 * cb0 + 16, 16 * cb1, 16 * cb1 + 16};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = nt * 8 + 2 * tig + e;
+        if (r >= t.rows) continue;
+        const int64_t row = t.row0 + r;
+        if (a.act == DWM_ACT_NONE) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              const float v = acc[i][nt][hc * 2 + e];
+              const int64_t off = row * a.ldo + colbase[i] + gid + 8 * hc;
+              if (a.out_f32)
+                reinterpret_cast<float*>(a.out)[off] = v;
+              else
+                reinterpret_cast<uint16_t*>(a.out)[off] = (uint16_t)f32_to_bf16_bits(v);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              float g = acc[i][nt][hc * 2 + e];
+              float u = acc[i + 2][nt][hc * 2 + e];
+              if (a.act == DWM_ACT_SWIGLU_CLAMP) {
+                g = fminf(g, a.limit);
+                u = fminf(fmaxf(u, -a.limit), a.limit);
+              }
+              const float hv = g * (1.0f / (1.0f + expf(-g))) * u;
+              const int64_t off = row * a.ldo + colbase[i] + gid + 8 * hc;
+              if (a.out_f32)
+                reinterpret_cast<float*>(a.out)[off] = hv;
+              else
+                reinterpret_cast<uint16_t*>(a.out)[off] = (uint16_t)f32_to_bf16_bits(hv);
+            }
+          }
+        }
+      }
+    }
+  }
+  // On abort, let every copy this warp issued land before the CTA can exit.
+  if (!ok && lane == 0) {
+    for (uint32_t q = seq; q < issued; ++q)
+      mbar_wait(&bars[q % S], (q / S) & 1, nullptr, a.status);
+  }
+}
+
+template <int SD, int NT>
+int launch_impl(const void* lhs, const void* codes, const void* scales, const Args& a,
+                cudaStream_t stream) {
+  using C = Cfg<SD, NT>;
+  CUtensorMap tm_lhs, tm_codes, tm_scales;
+  // lhs [m, k] bf16: box of 64 k x 8*NT rows, 128-byte swizzle.
+  int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)a.k,
+                          (uint64_t)a.m, (uint64_t)a.k * 2, KSTAGE, 8 * NT,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // codes: rows = column blocks [n_local * n/16], each (k/16) x 32 words;
+  // box of 4 k16 blocks (128 words) x 2 column blocks.
+  rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes, (uint64_t)(a.k / 16) * 32,
+                      (uint64_t)a.n_local * (a.n / 16), (uint64_t)(a.k / 16) * 128, 4 * 32, 2,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  // scales [n_local * k/32, n]: box of 32 columns x 2 k32 rows.
+  rc = encode_tmap_2d(&tm_scales, ScaleTraits<SD>::tma, scales, (uint64_t)a.n,
+                      (uint64_t)a.n_local * (a.k / 32), (uint64_t)a.n * ScaleTraits<SD>::bytes, 32,
+                      2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    rc = check_cuda(cudaFuncSetAttribute(gmv_fp4_kernel<SD, NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::ALLOC),
+                    "gmv smem attribute");
+    if (rc) return rc;
+    attr_set[dev] = true;
+  }
+  gmv_fp4_kernel<SD, NT><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(tm_lhs, tm_codes,
+                                                                         tm_scales, a);
+  return check_cuda(cudaGetLastError(), "gmv_fp4 launch");
+}
+
+}  // namespace gmv
+
+// Decode-regime grouped GEMM on the B200 layout (called by the dwm_gmm_fp4
+// dispatcher after argument validation: k % 64 == 0, n % 256 == 0, 16-byte
+// aligned pointers). nt: 1 or 2 n8 token tiles per task.
+int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+               const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
+               int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
+               cudaStream_t stream) {
+  gmv::Args a;
+  a.group_sizes = group_sizes;
+  a.num_groups = num_groups;
+  a.group_offset = group_offset;
+  a.n_local = n_local;
+  a.m = m;
+  a.k = k;
+  a.n = n;
+  a.act = act;
+  a.limit = limit;
+  a.out_f32 = out_dtype == DWM_F32;
+  a.zero_init = zero_init;
+  a.out = out;
+  a.ldo = act == DWM_ACT_NONE ? n : n / 2;
+  a.quads = n / 64;
+  a.status = status_ptr();
+#define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT>(lhs, codes, scales, a, stream)
+  if (nt <= 1) {
+    if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 1);
+    if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 1);
+    DWM_GMV(DWM_F32, 1);
+  }
+  if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 2);
+  if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 2);
+  DWM_GMV(DWM_F32, 2);
+#undef DWM_GMV
+}
+
+}  // namespace dwm

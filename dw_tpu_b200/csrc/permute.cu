@@ -13,13 +13,12 @@
 //             sequence.
 #include <algorithm>
 
-#include "common.cuh"
+#include "moe_common.cuh"
 
 namespace dwm {
 namespace perm {
 
-constexpr int PERMUTE_THREADS = 1024;
-constexpr int PERMUTE_WARPS = PERMUTE_THREADS / 32;
+using namespace moe;
 
 __global__ void sorted_token_indices_kernel(const int32_t* __restrict__ in, int64_t n, int topk,
                                             int32_t* __restrict__ out) {
@@ -28,99 +27,12 @@ __global__ void sorted_token_indices_kernel(const int32_t* __restrict__ in, int6
     out[i] = in[i] / topk;
 }
 
-// hist: [PERMUTE_WARPS][e] ints in dynamic shared memory, then the scan.
-__global__ void __launch_bounds__(PERMUTE_THREADS, 1)
+__global__ void __launch_bounds__(SORT_THREADS, 1)
     permute_kernel(const int32_t* __restrict__ ids, int n, int topk, int e,
                    int32_t* __restrict__ argsort, int32_t* __restrict__ tok,
                    int32_t* __restrict__ revert, int32_t* __restrict__ group_sizes, int* status) {
   extern __shared__ int sm[];
-  int* hist = sm;                          // [W][e]
-  int* totals = sm + PERMUTE_WARPS * e;    // [e]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < PERMUTE_WARPS * e; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-
-  // Contiguous segment per warp, a multiple of 32 entries.
-  const int seg = ((n + PERMUTE_WARPS - 1) / PERMUTE_WARPS + 31) & ~31;
-  const int s0 = warp * seg, s1 = min(n, s0 + seg);
-  int* my = hist + warp * e;
-  for (int base = s0; base < s1; base += 32) {
-    const int j = base + lane;
-    int x = -1;
-    if (j < s1) {
-      x = ids[j];
-      if (x < 0 || x >= e) { report(status, DWM_DEV_BAD_INDEX); x = -1; }
-    }
-    const unsigned act = __ballot_sync(0xffffffffu, x >= 0);
-    const unsigned peers = __match_any_sync(0xffffffffu, x);
-    if (x >= 0 && (peers & act) && (__ffs(peers) - 1) == lane) my[x] += __popc(peers);
-    __syncwarp();
-  }
-  __syncthreads();
-
-  // totals[x] = sum over warps; hist[w][x] <- sum over earlier warps.
-  for (int x = threadIdx.x; x < e; x += blockDim.x) {
-    int run = 0;
-    for (int w = 0; w < PERMUTE_WARPS; ++w) {
-      const int v = hist[w * e + x];
-      hist[w * e + x] = run;
-      run += v;
-    }
-    totals[x] = run;
-    if (group_sizes) group_sizes[x] = run;
-  }
-  __syncthreads();
-  // Exclusive scan of totals (e entries) by warp 0, chunked per lane.
-  if (warp == 0) {
-    const int per = (e + 31) / 32;
-    int sum = 0;
-    for (int i = 0; i < per; ++i) {
-      const int x = lane * per + i;
-      if (x < e) sum += totals[x];
-    }
-    int incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    int run = incl - sum;
-    for (int i = 0; i < per; ++i) {
-      const int x = lane * per + i;
-      if (x < e) {
-        const int v = totals[x];
-        totals[x] = run;
-        run += v;
-      }
-    }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < PERMUTE_WARPS * e; i += blockDim.x) hist[i] += totals[i % e];
-  __syncthreads();
-
-  // In-order scatter.
-  for (int base = s0; base < s1; base += 32) {
-    const int j = base + lane;
-    int x = -1;
-    if (j < s1) {
-      x = ids[j];
-      if (x < 0 || x >= e) x = -1;
-    }
-    const unsigned peers = __match_any_sync(0xffffffffu, x);
-    const unsigned lower = peers & ((1u << lane) - 1u);
-    int pos = -1;
-    if (x >= 0) pos = my[x] + __popc(lower);
-    __syncwarp();
-    if (x >= 0 && lower == 0) my[x] += __popc(peers);
-    __syncwarp();
-    if (x >= 0) {
-      if (argsort) argsort[pos] = j;
-      if (tok) tok[pos] = j / topk;
-      if (revert) revert[j] = pos;
-    } else if (j < s1 && revert) {
-      revert[j] = -1;
-    }
-  }
+  counting_sort_block(ids, n, topk, e, argsort, tok, revert, group_sizes, nullptr, status, sm);
 }
 
 // out[r, :] = hidden[tok[r], :], rows of h bf16 (h % 8 == 0).
@@ -142,24 +54,6 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ hidden, int t, int6
   }
 }
 
-template <int XD>
-__device__ __forceinline__ void load8(const void* x, int64_t off, float (&v)[8]) {
-  if constexpr (XD == DWM_BF16) {
-    const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[2 * i] = __uint_as_float(w[i] << 16);
-      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    }
-  } else {
-    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
-    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + off + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-}
-
 // One thread per 8 output columns of one token.
 template <int XD, int WD, int OD>
 __global__ void combine_kernel(const void* __restrict__ x, int64_t x_rows,
@@ -176,41 +70,17 @@ __global__ void combine_kernel(const void* __restrict__ x, int64_t x_rows,
     for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
     for (int k = 0; k < topk; ++k) {
       const int64_t r = idx[tt * topk + k];
-      float wk;
-      if constexpr (WD == DWM_BF16)
-        wk = __uint_as_float((uint32_t)static_cast<const uint16_t*>(w)[tt * topk + k] << 16);
-      else
-        wk = static_cast<const float*>(w)[tt * topk + k];
+      const float wk = load_weight<WD>(w, tt * topk + k);
       if (r < 0 || r >= x_rows) {
         report(status, DWM_DEV_BAD_INDEX);
         continue;
       }
       float v[8];
       load8<XD>(x, r * h + (int64_t)c * 8, v);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(v[q], wk));
+      mul_add8(acc, v, wk);
     }
-    if constexpr (OD == DWM_BF16) {
-      uint4 o;
-      o.x = f32_to_bf16_bits(acc[0]) | (f32_to_bf16_bits(acc[1]) << 16);
-      o.y = f32_to_bf16_bits(acc[2]) | (f32_to_bf16_bits(acc[3]) << 16);
-      o.z = f32_to_bf16_bits(acc[4]) | (f32_to_bf16_bits(acc[5]) << 16);
-      o.w = f32_to_bf16_bits(acc[6]) | (f32_to_bf16_bits(acc[7]) << 16);
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + tt * h + (int64_t)c * 8) = o;
-    } else {
-      float* o = static_cast<float*>(out) + tt * h + (int64_t)c * 8;
-      *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    }
+    store8<OD>(out, tt * h + (int64_t)c * 8, acc);
   }
-}
-
-static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-inline unsigned grid_for(int64_t work, int threads, int per_sm = 16) {
-  int64_t b = (work + threads - 1) / threads;
-  int64_t cap = (int64_t)num_sms() * per_sm;
-  return (unsigned)std::max<int64_t>(1, std::min(b, cap));
 }
 
 }  // namespace perm
@@ -224,7 +94,7 @@ extern "C" int dwm_sorted_token_indices(const int32_t* topk_argsort, int64_t n, 
   DWM_CHECK_ARG(n >= 0 && (n == 0 || (topk_argsort && out)), "bad arguments");
   if (n == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  perm::sorted_token_indices_kernel<<<perm::grid_for(n, 256), 256, 0, s>>>(topk_argsort, n, topk,
+  perm::sorted_token_indices_kernel<<<moe::grid_for(n, 256), 256, 0, s>>>(topk_argsort, n, topk,
                                                                            out);
   return check_cuda(cudaGetLastError(), "sorted_token_indices launch");
 }
@@ -239,19 +109,19 @@ extern "C" int dwm_permute(const int32_t* topk_ids, int t, int topk, int e, int3
   DWM_CHECK_ARG(group_sizes, "group_sizes is required");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n = t * topk;
-  const size_t smem = (size_t)(perm::PERMUTE_WARPS * e + e) * sizeof(int);
+  const size_t smem = (size_t)(moe::SORT_WARPS * e + e) * sizeof(int);
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
     int rc = check_cuda(cudaFuncSetAttribute(perm::permute_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)((perm::PERMUTE_WARPS * 1024 + 1024) * sizeof(int))),
+                                             (int)((moe::SORT_WARPS * 1024 + 1024) * sizeof(int))),
                         "permute smem attribute");
     if (rc) return rc;
     attr_set[dev] = true;
   }
-  perm::permute_kernel<<<1, perm::PERMUTE_THREADS, smem, s>>>(
+  perm::permute_kernel<<<1, moe::SORT_THREADS, smem, s>>>(
       topk_ids, n, topk, e, topk_argsort, token_indices_sorted, revert, group_sizes,
       status_ptr());
   return check_cuda(cudaGetLastError(), "permute launch");
@@ -263,11 +133,11 @@ extern "C" int dwm_dispatch_gather(const void* hidden, int t, int h,
   DWM_CHECK_ARG(t >= 0 && h > 0 && rows >= 0, "bad shape");
   DWM_CHECK_ARG(h % 8 == 0, "h=%d must be a multiple of 8", h);
   DWM_CHECK_ARG(rows == 0 || (hidden && token_indices_sorted && out), "NULL pointer");
-  DWM_CHECK_ARG(perm::aligned16(hidden) && perm::aligned16(out), "pointers must be 16-byte aligned");
+  DWM_CHECK_ARG(moe::aligned16(hidden) && moe::aligned16(out), "pointers must be 16-byte aligned");
   if (rows == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t h16 = h / 8;
-  perm::gather_rows_kernel<<<perm::grid_for(rows * h16, 256), 256, 0, s>>>(
+  perm::gather_rows_kernel<<<moe::grid_for(rows * h16, 256), 256, 0, s>>>(
       static_cast<const uint4*>(hidden), t, h16, token_indices_sorted, rows,
       static_cast<uint4*>(out), status_ptr());
   return check_cuda(cudaGetLastError(), "gather launch");
@@ -282,10 +152,10 @@ extern "C" int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int
   DWM_CHECK_ARG(w_dtype == DWM_BF16 || w_dtype == DWM_F32, "w dtype must be bf16 or f32");
   DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
   DWM_CHECK_ARG(t == 0 || (x && indices && w && out), "NULL pointer");
-  DWM_CHECK_ARG(perm::aligned16(x) && perm::aligned16(out), "pointers must be 16-byte aligned");
+  DWM_CHECK_ARG(moe::aligned16(x) && moe::aligned16(out), "pointers must be 16-byte aligned");
   if (t == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned grid = perm::grid_for((int64_t)t * (h / 8), 256);
+  const unsigned grid = moe::grid_for((int64_t)t * (h / 8), 256);
   int* st = status_ptr();
 #define DWM_COMBINE(XD, WD, OD)                                                             \
   if (x_dtype == XD && w_dtype == WD && out_dtype == OD) {                                  \

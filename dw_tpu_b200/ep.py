@@ -1,0 +1,273 @@
+"""Expert-parallel MoE on B200: the one-shot NVLink exchange (dwm_ep_*) and
+the EP layer built on it.
+
+The reference's GMM_EP path all-gathers every rank's tokens and routing
+(``all_gather_local``, KO:152-164), sorts the gathered batch and keeps the rows
+of the rank's own experts (X0101:56-104, X0107:34-51), runs the grouped
+matmuls, then forms a masked f32 partial combine over all gathered tokens and
+reduce-scatters it (X0107:15-29, ``reduce_scatter_local`` KO:167-185). Here a
+rank instead stores each of its (token, k) rows straight into the expert
+owner's receive buffer, in the same receive order, and the owner stores each
+expert output straight back into the source's combine buffer, where the token
+owner forms the k-order combine (KC:14-21). One process per GPU; peers' buffers
+are mapped with CUDA IPC, exchanged once over ``torch.distributed``.
+
+``all_gather_local`` / ``reduce_scatter_local`` below are the NCCL
+comparison path (the reference's collectives on ``torch.distributed``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from . import ops
+from .fused_moe import FP4MoEWeights
+
+
+class _DeviceArray:
+    """Zero-copy ``__cuda_array_interface__`` view of library-owned memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape),
+                                         "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class EPContext:
+    """One rank's side of the exchange (``dwm_ep_create``): its symmetric
+    buffer, the receive view and the receive group sizes.
+
+    Rank ``rank`` of ``world`` owns experts [rank*E/world, (rank+1)*E/world).
+    ``recv`` is a bf16 [capacity, hidden] view of the receive buffer (owned by
+    the context: keep the context alive while it is used)."""
+
+    def __init__(self, rank: int, world: int, *, max_tokens: int, hidden: int, topk: int,
+                 num_experts: int):
+        self.rank, self.world = int(rank), int(world)
+        self.max_tokens, self.hidden, self.topk = int(max_tokens), int(hidden), int(topk)
+        self.num_experts = int(num_experts)
+        self.local_experts = self.num_experts // self.world if self.world else 0
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = L.lib()
+        ctx = ctypes.c_void_p()
+        L.check(lib.dwm_ep_create(self.rank, self.world, self.max_tokens, self.hidden,
+                                  self.topk, self.num_experts, ctypes.byref(ctx)),
+                "dwm_ep_create")
+        self._ctx = ctx
+        recv = ctypes.c_void_p()
+        cap = ctypes.c_int64()
+        L.check(lib.dwm_ep_recv_buffer(ctx, ctypes.byref(recv), ctypes.byref(cap)),
+                "dwm_ep_recv_buffer")
+        self.capacity = cap.value
+        self.recv = torch.as_tensor(_DeviceArray(recv.value, (self.capacity, self.hidden), "<i2"),
+                                    device=self.device).view(torch.bfloat16)
+        self.recv_group_sizes = torch.zeros(self.local_experts, dtype=torch.int32,
+                                            device=self.device)
+        self.num_tokens = 0
+
+    # -- wiring -------------------------------------------------------------
+    def ipc_handle(self) -> bytes:
+        buf = (ctypes.c_char * L.EP_HANDLE_BYTES)()
+        L.check(L.lib().dwm_ep_ipc_handle(self._ctx, buf), "dwm_ep_ipc_handle")
+        return bytes(buf)
+
+    def connect(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world or any(len(h) != L.EP_HANDLE_BYTES for h in handles):
+            raise ValueError("expected one IPC handle per rank")
+        blob = b"".join(handles)
+        L.check(L.lib().dwm_ep_connect(self._ctx, blob), "dwm_ep_connect")
+
+    @staticmethod
+    def connect_local(ctxs: list["EPContext"]) -> None:
+        arr = (ctypes.c_void_p * len(ctxs))(*[c._ctx.value for c in ctxs])
+        for c in ctxs:
+            L.check(L.lib().dwm_ep_connect_local(c._ctx, arr), "dwm_ep_connect_local")
+
+    # -- exchange -----------------------------------------------------------
+    def dispatch(self, hidden: torch.Tensor, topk_ids: torch.Tensor, *, phases: int = L.EP_ALL,
+                 stream: int | None = None):
+        """hidden bf16 [T, H], topk_ids int32 [T, topk] -> (recv view
+        [capacity, H], recv_group_sizes int32 [E/world]); rows
+        [0, sum(recv_group_sizes)) are valid."""
+        L.require_cuda(hidden, topk_ids)
+        if hidden.dtype != torch.bfloat16 or topk_ids.dtype != torch.int32:
+            raise ValueError("hidden must be bf16 and topk_ids int32")
+        t = hidden.shape[0]
+        if hidden.shape != (t, self.hidden) or topk_ids.shape != (t, self.topk):
+            raise ValueError(f"expected hidden [T, {self.hidden}] and ids [T, {self.topk}]")
+        hidden, topk_ids = hidden.contiguous(), topk_ids.contiguous()
+        self.num_tokens = t
+        L.check(L.lib().dwm_ep_dispatch(self._ctx, hidden.data_ptr(), topk_ids.data_ptr(), t,
+                                        self.recv_group_sizes.data_ptr(), phases,
+                                        L.stream_ptr() if stream is None else stream),
+                "dwm_ep_dispatch")
+        return self.recv, self.recv_group_sizes
+
+    def combine(self, y: torch.Tensor, topk_weights: torch.Tensor,
+                out: torch.Tensor | None = None, *, phases: int = L.EP_PUSH | L.EP_REDUCE,
+                stream: int | None = None) -> torch.Tensor | None:
+        """y [capacity (or more), H] expert outputs in receive order (bf16 or
+        f32), topk_weights [T, topk] of this rank's dispatched tokens ->
+        out [T, H] (bf16 unless ``out`` says otherwise)."""
+        L.require_cuda(y, topk_weights)
+        if y.dim() != 2 or y.shape[1] != self.hidden or not y.is_contiguous():
+            raise ValueError(f"y must be a contiguous [rows, {self.hidden}] tensor")
+        t = self.num_tokens
+        if topk_weights.shape != (t, self.topk):
+            raise ValueError(f"topk_weights must be [{t}, {self.topk}]")
+        if out is None and phases & L.EP_REDUCE:
+            out = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=y.device)
+        L.check(L.lib().dwm_ep_combine(self._ctx, y.data_ptr(), L.dtype_code(y.dtype),
+                                       topk_weights.contiguous().data_ptr(),
+                                       L.dtype_code(topk_weights.dtype),
+                                       L.ptr(out), L.dtype_code(out.dtype) if out is not None
+                                       else L.BF16, phases,
+                                       L.stream_ptr() if stream is None else stream),
+                "dwm_ep_combine")
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_ctx", None) is not None and self._ctx.value:
+            L.lib().dwm_ep_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def create_context(group=None, *, max_tokens: int, hidden: int, topk: int,
+                   num_experts: int) -> EPContext:
+    """Collective: every rank of ``group`` creates its context on its current
+    device, the IPC handles are all-gathered, and every rank maps its peers."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    ctx = EPContext(rank, world, max_tokens=max_tokens, hidden=hidden, topk=topk,
+                    num_experts=num_experts)
+    handles: list = [None] * world
+    dist.all_gather_object(handles, ctx.ipc_handle(), group=group)
+    ctx.connect(handles)
+    dist.barrier(group=group)
+    return ctx
+
+
+def create_local_contexts(world: int, **kw) -> list[EPContext]:
+    """All ``world`` ranks' contexts in this process on the current device:
+    the exchange emulated on one GPU (drive it with ``emulated_dispatch`` and
+    ``emulated_combine``, which issue every rank's phases in order)."""
+    ctxs = [EPContext(r, world, **kw) for r in range(world)]
+    EPContext.connect_local(ctxs)
+    return ctxs
+
+
+def emulated_dispatch(ctxs: list[EPContext], hiddens, ids):
+    for phase in (L.EP_COUNTS, L.EP_ROWS, L.EP_WAIT):
+        for c, h, i in zip(ctxs, hiddens, ids):
+            c.dispatch(h, i, phases=phase)
+    return [(c.recv, c.recv_group_sizes) for c in ctxs]
+
+
+def emulated_combine(ctxs: list[EPContext], ys, weights, outs=None):
+    outs = outs or [None] * len(ctxs)
+    for c, y, w in zip(ctxs, ys, weights):
+        c.combine(y, w, None, phases=L.EP_PUSH)
+    return [c.combine(y, w, o, phases=L.EP_REDUCE)
+            for c, y, w, o in zip(ctxs, ys, weights, outs)]
+
+
+# ---------------------------------------------------------------------------
+# NCCL comparison path: the reference's collectives
+# ---------------------------------------------------------------------------
+
+def all_gather_local(x: torch.Tensor, group=None) -> torch.Tensor:
+    """KO:152-164: rank-major concatenation of every rank's block (NCCL)."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype,
+                      device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def reduce_scatter_local(x: torch.Tensor, group=None,
+                         out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """KO:167-185: rank r receives the f32 sum over ranks of block r (NCCL's
+    summation order, not the reference's rank order)."""
+    world = dist.get_world_size(group)
+    xf = x.float().contiguous()
+    out = torch.empty((x.shape[0] // world,) + tuple(x.shape[1:]), dtype=torch.float32,
+                      device=x.device)
+    dist.reduce_scatter_tensor(out, xf, op=dist.ReduceOp.SUM, group=group)
+    return out.to(out_dtype or x.dtype)
+
+
+# ---------------------------------------------------------------------------
+# The EP layer
+# ---------------------------------------------------------------------------
+
+def gemm_variant(layout: str, expected_rows: float) -> int:
+    """Kernel choice for a local expert receiving ``expected_rows`` rows on
+    average (the receive buffer's row count is a capacity, not a size)."""
+    if layout != "b200":
+        return 0
+    if expected_rows <= 8:
+        return 3  # mma.sync kernel, 8-row token tiles
+    if expected_rows <= 16:
+        return 4  # mma.sync kernel, 16-row token tiles
+    return 1      # tcgen05 kernel
+
+
+class EPMoELayer:
+    """Expert-parallel FP4 MoE layer: local routing, one-shot dispatch, the
+    two grouped matmuls on the rank's experts, one-shot combine (the GMM_EP
+    layer of X0104:88-98 / X0107 with the exchange above).
+
+    ``weights`` holds the rank's E/world experts (global experts
+    [rank*E/world, (rank+1)*E/world)); routing runs over all E experts."""
+
+    def __init__(self, weights: FP4MoEWeights, ctx: EPContext, top_k: int, *,
+                 scoring_fn: str = "sigmoid", renormalize: bool = True,
+                 act_limit: float | None = None, f32_reduce: bool = False,
+                 expected_rows: float | None = None):
+        if weights.num_experts != ctx.local_experts:
+            raise ValueError(f"weights hold {weights.num_experts} experts, the context "
+                             f"{ctx.local_experts} per rank")
+        if top_k != ctx.topk:
+            raise ValueError("top_k differs from the context's")
+        self.w, self.ctx = weights, ctx
+        self.top_k = int(top_k)
+        self.scoring_fn, self.renormalize = scoring_fn, renormalize
+        self.act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
+        self.act_limit = 0.0 if act_limit is None else float(act_limit)
+        dev = ctx.device
+        t, k = ctx.max_tokens, self.top_k
+        self.ids = torch.empty((t, k), dtype=torch.int32, device=dev)
+        self.w16 = torch.empty((t, k), dtype=torch.bfloat16, device=dev)
+        cap, i, h = ctx.capacity, weights.intermediate_size, weights.hidden_size
+        self.h1 = torch.empty((cap, i), dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty((cap, h), dtype=torch.float32 if f32_reduce else torch.bfloat16,
+                             device=dev)
+        if expected_rows is None:  # uniform routing over all experts
+            expected_rows = t * k / ctx.num_experts * ctx.world
+        self.variant = gemm_variant(weights.layout, expected_rows)
+
+    kernels_per_forward = 8  # route, 3 dispatch, 2 gmm, 2 combine
+
+    def forward(self, hidden: torch.Tensor, logits: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        t = hidden.shape[0]
+        ids, w16 = self.ids[:t], self.w16[:t]
+        ops.route_topk_out(logits, self.top_k, ids, w16_out=w16, scoring_fn=self.scoring_fn,
+                           renormalize=self.renormalize)
+        recv, gs = self.ctx.dispatch(hidden, ids)
+        ops.gmm_fp4_out(recv, self.w.w13, self.w.s13, gs, self.h1, act=self.act,
+                        act_limit=self.act_limit, layout=self.w.layout, variant=self.variant)
+        ops.gmm_fp4_out(self.h1, self.w.w2, self.w.s2, gs, self.y, layout=self.w.layout,
+                        variant=self.variant)
+        return self.ctx.combine(self.y, w16, out)
+
+    __call__ = forward

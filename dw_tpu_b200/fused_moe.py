@@ -27,24 +27,34 @@ class FP4MoEWeights:
     """Expert weights in the stored layouts of X0103:240-245 / E0901:250-253
     (scale unit dim dropped): w13 [E, H, 2I] = [gate | up] as packed e2m1
     bytes [E, H, I]; s13 [E, H/32, 2I]; w2 bytes [E, I, H/2]; s2 [E, I/32, H].
-    Scales are uint8 E8M0 codes, bf16 or f32."""
+    Scales are uint8 E8M0 codes, bf16 or f32. ``layout`` is "e2m1" (raw
+    nibbles) or "b200" (re-laid once for the faster decode, ``to_b200``)."""
 
     w13: torch.Tensor
     s13: torch.Tensor
     w2: torch.Tensor
     s2: torch.Tensor
+    layout: str = "e2m1"
+
+    def to_b200(self) -> "FP4MoEWeights":
+        """Load-time re-layout of both projections into the B200 decode layout
+        (w13 [E, 2I, H/2], w2 [E, H, I/2]; B01:276-299 counterpart)."""
+        if self.layout == "b200":
+            return self
+        return FP4MoEWeights(ops.fp4_to_b200_out(self.w13), self.s13,
+                             ops.fp4_to_b200_out(self.w2), self.s2, "b200")
 
     @property
     def num_experts(self) -> int:
-        return self.w13.shape[0]
+        return self.s13.shape[0]
 
     @property
     def hidden_size(self) -> int:
-        return self.w13.shape[1]
+        return self.s13.shape[1] * 32
 
     @property
     def intermediate_size(self) -> int:
-        return self.w2.shape[1]
+        return self.s2.shape[1] * 32
 
     def weight_bytes_per_expert(self) -> int:
         per = lambda t: t.numel() * t.element_size() // t.shape[0]  # noqa: E731
@@ -96,9 +106,9 @@ class MoELayer:
         ops.dispatch_gather_out(hidden, self.tok[:rows], x)
         h1 = self.h1[:rows]
         ops.gmm_fp4_out(x, self.w.w13, self.w.s13, self.group_sizes, h1, act=self.act,
-                        act_limit=self.act_limit)
+                        act_limit=self.act_limit, layout=self.w.layout)
         y = self.y[:rows]
-        ops.gmm_fp4_out(h1, self.w.w2, self.w.s2, self.group_sizes, y)
+        ops.gmm_fp4_out(h1, self.w.w2, self.w.s2, self.group_sizes, y, layout=self.w.layout)
         if out is None:
             out = torch.empty((t, self.w.hidden_size), dtype=torch.bfloat16,
                               device=hidden.device)

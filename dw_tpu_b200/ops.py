@@ -39,19 +39,32 @@ def _scale_view(s: torch.Tensor):
 # FP4 grouped matmul
 # ----------------------------------------------------------------------------
 
+def fp4_dims(codes: torch.Tensor, layout: str):
+    """(groups, k, n) of packed FP4 weights: "e2m1" [g, k, n/2], "b200" [g, n, k/2]."""
+    if codes.dim() != 3:
+        raise ValueError("FP4 weights must be 3-D packed bytes")
+    g, a, b = codes.shape
+    if layout == "e2m1":
+        return g, a, 2 * b
+    if layout == "b200":
+        return g, 2 * b, a
+    raise ValueError(f"unknown FP4 layout {layout!r}")
+
+
 def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
                 num_local_groups=None, act=L.ACT_NONE, act_limit=0.0,
-                zero_init=False, stream=None):
-    """out <- grouped matmul of lhs with the FP4 weights (see dwm_gmm_fp4)."""
+                zero_init=False, layout="e2m1", variant=0, stream=None):
+    """out <- grouped matmul of lhs with the FP4 weights (see dwm_gmm_fp4).
+    ``layout`` is "e2m1" (raw [g, k, n/2]) or "b200" (``fp4_to_b200_out``);
+    ``variant`` 0 picks the kernel; 1 forces the tcgen05 kernel and 2-4 the
+    mma.sync decode kernel (auto / 8 / 16-row token tiles); 1-4 need the
+    B200 layout."""
     L.require_cuda(lhs, codes, scales, group_sizes, out)
     if lhs.dtype != torch.bfloat16 or lhs.dim() != 2:
         raise ValueError("lhs must be a 2-D bf16 tensor")
     codes = _u8view(codes)
-    if codes.dim() != 3:
-        raise ValueError("codes must be [groups, k, n/2] bytes")
     sc, sd = _scale_view(scales)
-    g, k, n2 = codes.shape
-    n = 2 * n2
+    g, k, n = fp4_dims(codes, layout)
     if sc.numel() != g * (k // 32) * n:
         raise ValueError(f"scales must hold [groups, k/32, n] = [{g}, {k // 32}, {n}]")
     m = lhs.shape[0]
@@ -67,26 +80,48 @@ def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
     for t in (lhs, codes, sc, group_sizes, out):
         if not t.is_contiguous():
             raise ValueError("tensors must be contiguous")
-    rc = L.lib().dwm_gmm_fp4(
-        lhs.data_ptr(), codes.data_ptr(), L.FP4_E2M1, sc.data_ptr(), sd,
+    rc = L.lib().dwm_gmm_fp4_variant(
+        lhs.data_ptr(), codes.data_ptr(), L.LAYOUTS[layout], sc.data_ptr(), sd,
         group_sizes.data_ptr(), group_sizes.numel(), m, k, n, int(group_offset), nl, act,
         float(act_limit), L.dtype_code(out.dtype), int(bool(zero_init)), out.data_ptr(),
-        L.stream_ptr() if stream is None else stream)
+        int(variant), L.stream_ptr() if stream is None else stream)
     L.check(rc, "gmm_fp4")
     return out
 
 
-def fp4_dequant_out(codes, scales, out, stream=None):
+def fp4_dequant_out(codes, scales, out, layout="e2m1", stream=None):
     L.require_cuda(codes, scales, out)
     codes = _u8view(codes)
     sc, sd = _scale_view(scales)
-    g, k, n2 = codes.shape
-    if out.shape != (g, k, 2 * n2) or out.dtype != torch.bfloat16:
+    g, k, n = fp4_dims(codes, layout)
+    if out.shape != (g, k, n) or out.dtype != torch.bfloat16:
         raise ValueError("out must be bf16 [groups, k, n]")
-    rc = L.lib().dwm_fp4_dequant(codes.data_ptr(), sc.data_ptr(), sd, g, k, 2 * n2,
-                                 out.data_ptr(), L.stream_ptr() if stream is None else stream)
+    rc = L.lib().dwm_fp4_dequant(codes.data_ptr(), L.LAYOUTS[layout], sc.data_ptr(), sd, g, k,
+                                 n, out.data_ptr(), L.stream_ptr() if stream is None else stream)
     L.check(rc, "fp4_dequant")
     return out
+
+
+def fp4_to_b200_out(src, inverse=False, stream=None):
+    """Raw e2m1 [g, k, n/2] -> the B200 layout (u32 words [g][n/16][k/16][32],
+    returned as bytes shaped [g, n, k/2]), or back with ``inverse``; returns a
+    new tensor."""
+    L.require_cuda(src)
+    src = _u8view(src).contiguous()
+    if src.dim() != 3:
+        raise ValueError("expected packed FP4 weights [g, k, n/2] (or [g, n, k/2])")
+    if inverse:
+        g, n, k2 = src.shape
+        k = 2 * k2
+        dst = torch.empty((g, k, n // 2), dtype=torch.uint8, device=src.device)
+    else:
+        g, k, n2 = src.shape
+        n = 2 * n2
+        dst = torch.empty((g, n, k // 2), dtype=torch.uint8, device=src.device)
+    rc = L.lib().dwm_fp4_to_b200(src.data_ptr(), dst.data_ptr(), g, k, n, int(inverse),
+                                 L.stream_ptr() if stream is None else stream)
+    L.check(rc, "fp4_to_b200")
+    return dst
 
 
 def fp4_codes_convert_out(src, dst, from_format, to_format, stream=None):
@@ -210,20 +245,21 @@ def e8m0_decode_out(codes, out, stream=None):
 @torch.library.custom_op("dw_moe::gmm_fp4", mutates_args=())
 def gmm_fp4(lhs: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
             group_sizes: torch.Tensor, group_offset: int, num_local_groups: int, act: int,
-            act_limit: float, out_f32: bool, zero_init: bool) -> torch.Tensor:
-    n = codes.shape[-1] * 2
+            act_limit: float, out_f32: bool, zero_init: bool,
+            layout: str = "e2m1") -> torch.Tensor:
+    n = fp4_dims(codes, layout)[2]
     n_out = n if act == L.ACT_NONE else n // 2
     dt = torch.float32 if out_f32 else torch.bfloat16
     out = torch.empty((lhs.shape[0], n_out), dtype=dt, device=lhs.device)
     return gmm_fp4_out(lhs, codes, scales, group_sizes, out, group_offset=group_offset,
                        num_local_groups=num_local_groups, act=act, act_limit=act_limit,
-                       zero_init=zero_init)
+                       zero_init=zero_init, layout=layout)
 
 
 @gmm_fp4.register_fake
 def _(lhs, codes, scales, group_sizes, group_offset, num_local_groups, act, act_limit, out_f32,
-      zero_init):
-    n = codes.shape[-1] * 2
+      zero_init, layout="e2m1"):
+    n = fp4_dims(codes, layout)[2]
     n_out = n if act == L.ACT_NONE else n // 2
     return lhs.new_empty((lhs.shape[0], n_out),
                          dtype=torch.float32 if out_f32 else torch.bfloat16)

@@ -9,8 +9,8 @@
  * that ran out, an index out of range, a buffer overflow) are OR-ed into a
  * per-device status word read with dwm_device_status().
  *
- * Reference interfaces each entry point replaces are cited as project-relative
- * paths of jamesdborin/dw-tpu (see the alias table in DESIGN.md):
+ * Reference interfaces each entry point replaces are cited as file:line in
+ * jamesdborin/dw-tpu, with these aliases for its files:
  *   TK  = patches/tokamax/0001-gmm_v2-fp4-emulation-v6e.patch
  *   B01 = patches/tpu-inference/0001-dsv4-v6e-enablement.patch
  *   KD  = kernels/tpu_inference/layers/common/moe_fast_dispatch.py
@@ -52,6 +52,12 @@ extern "C" {
 
 #define DWM_FP4_E2M1 0    /* OCP e2m1 nibbles (sign | e1 e0 | m) */
 #define DWM_FP4_TOKAMAX 1 /* tokamax codes q = sign*(2e+m), int4 two's compl. */
+#define DWM_FP4_B200 2    /* the B200 load-time layout (dwm_fp4_to_b200):
+                             u32 words [groups][n/16][k/16][32] (as many
+                             bytes as [groups, n, k/2]); word l of a 16x16
+                             (k, column) block is lane l's A fragment of an
+                             m16n8k16 MMA for W^T, its bits permuted for a
+                             one-PRMT bf16 decode */
 
 #define DWM_SCORE_SOFTMAX 0
 #define DWM_SCORE_SIGMOID 1
@@ -73,9 +79,10 @@ int dwm_device_status(void* stream, int* bits);
  *
  *   lhs     bf16 [m, k], rows sorted by group (group g owns rows
  *           [sum(group_sizes[:g]), +group_sizes[g]))
- *   codes   uint8 [num_local_groups, k, n/2]: two e2m1 nibbles per byte,
- *           element 2j in the low nibble (DWM_FP4_E2M1 only; convert tokamax
- *           codes once with dwm_fp4_codes_convert)
+ *   codes   DWM_FP4_E2M1: uint8 [num_local_groups, k, n/2], two e2m1 nibbles
+ *           per byte, element 2j in the low nibble; DWM_FP4_B200: the same
+ *           values re-laid by dwm_fp4_to_b200 (faster decode); convert
+ *           tokamax codes once with dwm_fp4_codes_convert
  *   scales  [num_local_groups, k/32, n] of scale_dtype: DWM_U8 (E8M0 codes,
  *           KE:37-40), DWM_BF16 or DWM_F32 (cast to bf16 before use)
  *   group_sizes int32 [num_groups] on the device
@@ -89,11 +96,36 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
                 int n, int group_offset, int num_local_groups, int act, float act_limit,
                 int out_dtype, int zero_init, void* out, void* stream);
 
+/* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4:
+ * B200 codes whose local groups average <= 16 rows take 2, others 1),
+ * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles),
+ * 2 = mma.sync on weights decoded straight into registers (decode-sized
+ * groups; 8- or 16-row token tiles by the average rows per local group),
+ * 3 / 4 = the same with 8 / 16-row token tiles. 1-4 need DWM_FP4_B200
+ * codes. Every variant decodes the same bf16 weights and accumulates in f32; results
+ * differ between variants only by f32 summation order. Same reference
+ * interface as dwm_gmm_fp4 (TK:107-153). */
+int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
+                        int scale_dtype, const int32_t* group_sizes, int num_groups, int m,
+                        int k, int n, int group_offset, int num_local_groups, int act,
+                        float act_limit, int out_dtype, int zero_init, void* out, int variant,
+                        void* stream);
+
 /* Dequantise FP4 weights to bf16 with the reference's order (decode to bf16,
- * scale cast to bf16, one bf16 multiply; E0901:84-95): codes [g, k, n/2],
- * scales [g, k/32, n] -> out bf16 [g, k, n]. The same decode the GEMM uses. */
-int dwm_fp4_dequant(const void* codes, const void* scales, int scale_dtype, int groups, int k,
-                    int n, void* out, void* stream);
+ * scale cast to bf16, one bf16 multiply; E0901:84-95): codes as for
+ * dwm_gmm_fp4 (DWM_FP4_E2M1 [g, k, n/2] or DWM_FP4_B200 [g, n, k/2]), scales
+ * [g, k/32, n] -> out bf16 [g, k, n]. The same decode the GEMM uses.
+ * Counterpart of tokamax decode_codes (TK:33-41) plus the block-scale
+ * multiply. */
+int dwm_fp4_dequant(const void* codes, int codes_format, const void* scales, int scale_dtype,
+                    int groups, int k, int n, void* out, void* stream);
+
+/* Load-time re-layout of packed e2m1 weights: raw [g, k, n/2] -> DWM_FP4_B200
+ * [g, n, k/2] (inverse = 0) or back (inverse = 1); lossless, out of place.
+ * Counterpart of the reference's one-time stored-code re-encoding
+ * fp4_weight_to_codes (B01:276-299, TK:17-30). k % 16 == 0, n % 16 == 0. */
+int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int n, int inverse,
+                    void* stream);
 
 /* Re-encode packed nibbles between DWM_FP4_E2M1 and DWM_FP4_TOKAMAX
  * (tokamax e2m1_to_codes, TK:17-30, and its inverse); in == out allowed. */
@@ -142,6 +174,64 @@ int dwm_dispatch_gather(const void* hidden, int t, int h, const int32_t* token_i
 int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int32_t* indices,
                 const void* w, int w_dtype, int t, int h, int topk, void* out, int out_dtype,
                 void* stream);
+
+/* ---- expert-parallel exchange over NVLink peer memory ---------------------
+ * Replaces the GMM_EP exchange: all_gather_local + the per-shard stable sort
+ * (KO:152-164, X0101:56-104, X0107:34-51) on the way in, and the masked f32
+ * combine + reduce_scatter_local (X0107:15-29, KO:167-185) on the way out,
+ * with one-shot kernels that store rows straight into peer GPUs' buffers.
+ * One context per rank (one process per GPU); rank r owns experts
+ * [r*E/world, (r+1)*E/world). Receive order on rank r: expert-major over its
+ * experts, then (source rank, source token, k slot), i.e. the rows the
+ * reference's global stable argsort over the rank-major gathered batch keeps
+ * on rank r. The combine is the k-order f32 weighted sum of each token's
+ * expert outputs from +0.0, rounded once (KC:14-21, the combine contract of
+ * the single-device path). Every rank must make the same sequence of calls
+ * with the same dtypes; calls on one context are stream-ordered and must not
+ * overlap. Device-side waits give up after 2 s with DWM_DEV_TIMEOUT. */
+#define DWM_EP_HANDLE_BYTES 64 /* size of one rank's IPC handle */
+#define DWM_EP_COUNTS 1        /* dispatch phases (DWM_EP_ALL = all three) */
+#define DWM_EP_ROWS 2
+#define DWM_EP_WAIT 4
+#define DWM_EP_ALL 7
+#define DWM_EP_PUSH 1          /* combine phases */
+#define DWM_EP_REDUCE 2
+
+typedef struct dwm_ep dwm_ep;
+
+/* Allocate this rank's symmetric buffer (receive rows for world*max_tokens*
+ * topk pairs, their tags, a combine buffer of max_tokens*topk rows, counts
+ * and flags) on the current device. num_experts % world == 0,
+ * num_experts <= 1024, hidden % 8 == 0, world <= 8. */
+int dwm_ep_create(int rank, int world, int max_tokens, int hidden, int topk, int num_experts,
+                  dwm_ep** ctx);
+/* This rank's CUDA IPC handle (DWM_EP_HANDLE_BYTES bytes) for the exchange. */
+int dwm_ep_ipc_handle(dwm_ep* ctx, void* handle);
+/* Map every peer's buffer: handles = world handles, rank-major. */
+int dwm_ep_connect(dwm_ep* ctx, const void* handles);
+/* Single-process form: `ranks` holds all world contexts, created on the same
+ * device (an emulation of the exchange on one GPU: the phases of all ranks
+ * must then be issued phase by phase, COUNTS of every rank before ROWS of any,
+ * and so on, so that no wait depends on a later launch). */
+int dwm_ep_connect_local(dwm_ep* ctx, dwm_ep* const* ranks);
+/* The receive buffer (bf16 [capacity_rows, hidden]) inside the symmetric
+ * buffer; rows [0, sum(recv_group_sizes)) are valid after a dispatch. */
+int dwm_ep_recv_buffer(dwm_ep* ctx, void** recv, int64_t* capacity_rows);
+/* hidden bf16 [num_tokens, hidden], topk_ids int32 [num_tokens, topk] (ids
+ * outside [0, num_experts) are reported and dropped) -> the receive buffer
+ * and recv_group_sizes int32 [num_experts/world] (device). Counterpart of
+ * all_gather_local + sort (X0101:56-104). */
+int dwm_ep_dispatch(dwm_ep* ctx, const void* hidden, const int32_t* topk_ids, int num_tokens,
+                    int32_t* recv_group_sizes, int phases, void* stream);
+/* y [capacity_rows, hidden] (bf16 or f32: expert outputs of the received
+ * rows, in receive order) -> out [num_tokens, hidden] of out_dtype, with
+ * topk_weights [num_tokens, topk] (bf16 or f32) of the dispatch's tokens.
+ * Counterpart of the masked combine + reduce_scatter_local (X0107:15-29,
+ * KO:167-185) with the k-order contract of fast_combine (KC:14-21). */
+int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
+                   int w_dtype, void* out, int out_dtype, int phases, void* stream);
+/* Synchronise the context's device, unmap peers and free the buffers. */
+int dwm_ep_destroy(dwm_ep* ctx);
 
 #ifdef __cplusplus
 }

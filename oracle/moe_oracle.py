@@ -38,7 +38,8 @@ import numpy as np
 __all__ = [
     "E2M1_MAGNITUDES", "f32_to_bf16_bits", "bf16_bits_to_f32", "round_bf16",
     "pack_nibbles", "unpack_nibbles", "e2m1_decode", "e2m1_to_codes",
-    "codes_to_e2m1", "decode_codes", "round_to_e2m1", "e8m0_encode",
+    "codes_to_e2m1", "decode_codes", "round_to_e2m1", "b200_swizzle",
+    "b200_unswizzle", "to_b200_layout", "from_b200_layout", "e8m0_encode",
     "e8m0_decode", "scales_to_f32", "dequant_fp4_block", "dequant_fp4_f32",
     "gmm_f32", "gmm_ref", "silu_and_mul", "quantize_fp4_block32",
     "dequantize_fp4_block32", "apply_scoring_fn", "route_topk",
@@ -154,6 +155,83 @@ def round_to_e2m1(x: np.ndarray) -> np.ndarray:
     code = np.where(mag == grid[hi], hi, code).astype(np.uint8)
     sign = (np.signbit(x) & (code != 0)).astype(np.uint8) << 3
     return (code | sign).astype(np.uint8)
+
+
+def b200_swizzle(packed: np.ndarray) -> np.ndarray:
+    """The B200 decode layout of packed e2m1 bytes: inside every 32-bit word
+    (little-endian, 8 columns), output pair p = raw byte p moves its 2-bit
+    fields (bits 1:0, 3:2 of the low nibble, 1:0, 3:2 of the high nibble) to
+    bits B, B+4, B+8, B+12 with B = 0, 2, 16, 18 for p = 0..3. Not part of
+    the reference: a lossless storage permutation (tests pin it as such)."""
+    w = np.ascontiguousarray(packed, dtype=np.uint8).view(np.uint32)
+    out = np.zeros_like(w)
+    for p in range(4):
+        byte = (w >> np.uint32(8 * p)) & np.uint32(0xFF)
+        base = (p & 1) * 2 + (p >> 1) * 16
+        for f in range(4):
+            out |= ((byte >> np.uint32(2 * f)) & np.uint32(3)) << np.uint32(base + 4 * f)
+    return out.view(np.uint8).reshape(np.asarray(packed).shape)
+
+
+def b200_fragment_coords():
+    """(dk, dc) of nibble j of word l inside a 16x16 (k, column) block: the
+    A fragment of an m16n8k16 MMA for W^T (gid = l // 4, t = l % 4; columns
+    gid, gid + 8; k pairs 2t, 2t + 8), nibble order
+    (2t,gid) (2t+1,gid) (2t,gid+8) (2t+1,gid+8) then the same at k + 8."""
+    l = np.arange(32)[:, None]
+    j = np.arange(8)[None, :]
+    gid, t = l >> 2, l & 3
+    dk = 2 * t + (j & 1) + ((j >> 2) << 3)
+    dc = gid + (((j >> 1) & 1) << 3)
+    return dk, dc
+
+
+def to_b200_layout(packed: np.ndarray) -> np.ndarray:
+    """Raw e2m1 weights [g, k, n/2] -> the B200 layout, returned as uint8
+    [g, n, k/2] (same byte count): u32 words [g][n/16][k/16][32], word l of
+    block (cb, kb) holding the 8 nibbles ``b200_fragment_coords`` lists
+    (nibble j in bits 4j..4j+3), then ``b200_swizzle`` on every word. Not part
+    of the reference: a lossless load-time re-layout."""
+    packed = np.asarray(packed, np.uint8)
+    g, k, n2 = packed.shape
+    n = 2 * n2
+    nib = unpack_nibbles(packed).astype(np.uint32)          # [g, k, n]
+    blocks = nib.reshape(g, k // 16, 16, n // 16, 16).transpose(0, 3, 1, 2, 4)
+    dk, dc = b200_fragment_coords()
+    sel = blocks[:, :, :, dk, dc]                            # [g, n/16, k/16, 32, 8]
+    words = np.zeros(sel.shape[:-1], np.uint32)
+    for j in range(8):
+        words |= sel[..., j] << np.uint32(4 * j)
+    raw = np.ascontiguousarray(words).view(np.uint8).reshape(g, n, k // 2)
+    return b200_swizzle(raw)
+
+
+def from_b200_layout(b200: np.ndarray) -> np.ndarray:
+    """Inverse of ``to_b200_layout``."""
+    b200 = np.asarray(b200, np.uint8)
+    g, n, k2 = b200.shape
+    k = 2 * k2
+    words = np.ascontiguousarray(b200_unswizzle(b200)).view(np.uint32).reshape(
+        g, n // 16, k // 16, 32)
+    dk, dc = b200_fragment_coords()
+    blocks = np.zeros((g, n // 16, k // 16, 16, 16), np.uint8)
+    for j in range(8):
+        blocks[:, :, :, dk[:, j], dc[:, j]] = (words >> np.uint32(4 * j)) & np.uint32(0xF)
+    nib = blocks.transpose(0, 2, 3, 1, 4).reshape(g, k, n)
+    return pack_nibbles(nib)
+
+
+def b200_unswizzle(packed: np.ndarray) -> np.ndarray:
+    """Inverse of ``b200_swizzle``."""
+    o = np.ascontiguousarray(packed, dtype=np.uint8).view(np.uint32)
+    w = np.zeros_like(o)
+    for p in range(4):
+        base = (p & 1) * 2 + (p >> 1) * 16
+        byte = np.zeros_like(o)
+        for f in range(4):
+            byte |= ((o >> np.uint32(base + 4 * f)) & np.uint32(3)) << np.uint32(2 * f)
+        w |= byte << np.uint32(8 * p)
+    return w.view(np.uint8).reshape(np.asarray(packed).shape)
 
 
 # ----------------------------------------------------------------------------
@@ -431,7 +509,7 @@ def combine(x: np.ndarray, indices, topk_weights, topk: int,
 
 
 # ----------------------------------------------------------------------------
-# Single-device MoE layer (the fused_moe_func GMM path, SURVEY call stack 3.1)
+# Single-device MoE layer (the fused_moe_func GMM path, X0104:88-98)
 # ----------------------------------------------------------------------------
 
 def fused_moe(hidden, logits, w13_packed, w13_scales, w2_packed, w2_scales,

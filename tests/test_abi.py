@@ -79,7 +79,12 @@ def test_other_entry_points_validate(lib):
     assert lib.dwm_route_topk(fake, 0, 4, 8, 9, 1, 1, None, -1, fake, None, None, None) == -1
     assert lib.dwm_route_topk(fake, 0, 4, 8, 2, 7, 1, None, -1, fake, None, None, None) == -1
     assert lib.dwm_fp4_codes_convert(fake, fake, 16, 0, 5, None) == -1
-    assert lib.dwm_fp4_dequant(fake, fake, 2, 1, 48, 64, fake, None) == -1
+    assert lib.dwm_fp4_dequant(fake, 0, fake, 2, 1, 48, 64, fake, None) == -1
+    assert lib.dwm_fp4_dequant(fake, 1, fake, 2, 1, 64, 64, fake, None) == -1
+    assert lib.dwm_fp4_to_b200(fake, fake + 64, 1, 12, 8, 0, None) == -1
+    assert lib.dwm_fp4_to_b200(fake, fake, 1, 16, 8, 0, None) == -1
+    assert lib.dwm_gmm_fp4_variant(fake, fake, 0, fake, 2, fake, 8, 16, 64, 256, 0, 8, 0, 0.0,
+                                   0, 0, fake, 2, None) == -1  # explicit variant needs B200
     assert lib.dwm_device_status(None, None) == -1
 
 

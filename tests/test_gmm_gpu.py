@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from oracle import moe_oracle as O
-from tests.gpu_util import assert_gemm_close, bf16_to_np, np_to_bf16
+from tests.gpu_util import assert_gemm_close, bf16_to_np, np_to_bf16, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -159,6 +159,117 @@ def test_gmm_tokamax_codes_equal_e2m1(dw):
     assert np.array_equal(bf16_to_np(a), bf16_to_np(b))
     conv = dw.e2m1_to_codes(torch.from_numpy(packed).cuda())
     assert np.array_equal(conv.cpu().numpy(), tok)
+
+
+@pytest.mark.parametrize("sd", ["u8", "bf16", "f32"])
+def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
+    """The load-time B200 re-layout decodes to the same bf16 weights; the
+    tcgen05 kernel on it gives the same bits as the raw e2m1 path, and the
+    mma.sync kernel (another f32 summation order) stays within the GEMM
+    tolerance of the oracle, for plain, SwiGLU and f32 outputs."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    lhs, packed, scales, gs = _case(9, 400, 128, 512, 4, gs=[3, 0, 70, 300], lo=120, hi=140)
+    if sd == "u8":
+        sc = torch.from_numpy(scales)
+    elif sd == "bf16":
+        sc = torch.from_numpy(O.e8m0_decode(scales)).to(torch.bfloat16)
+    else:
+        sc = torch.from_numpy(O.e8m0_decode(scales))
+    sc = sc.cuda()
+    raw = torch.from_numpy(packed).cuda()
+    b200 = dw.fp4_weight_to_codes(raw)
+    assert np.array_equal(b200.cpu().numpy(), O.to_b200_layout(packed))
+    assert torch.equal(dw.b200_to_e2m1(b200), raw)
+    d0 = dw.decode_codes(raw, sc)
+    d1 = dw.decode_codes(b200, sc, layout="b200")
+    assert torch.equal(d0.view(torch.int16), d1.view(torch.int16))
+    assert np.array_equal(bf16_to_np(d0), O.dequant_fp4_block(packed, O.e8m0_decode(scales)))
+    x = np_to_bf16(lhs)
+    g = torch.from_numpy(gs).cuda()
+    for act, n_out, dt in ((L.ACT_NONE, 512, torch.bfloat16), (L.ACT_SWIGLU, 256, torch.bfloat16),
+                           (L.ACT_NONE, 512, torch.float32)):
+        ref = ops.gmm_fp4_out(x, raw, sc, g, torch.empty((400, n_out), dtype=dt, device="cuda"),
+                              act=act, zero_init=True)
+        kind = "swiglu" if act == L.ACT_SWIGLU else None
+        r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
+                         out_dtype="f32" if dt == torch.float32 else "bf16")
+        r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
+        for variant in (0, 1, 2):
+            got = ops.gmm_fp4_out(x, b200, sc, g,
+                                  torch.empty((400, n_out), dtype=dt, device="cuda"), act=act,
+                                  zero_init=True, layout="b200", variant=variant)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            if variant in (0, 1):  # 100 rows per group on average: tcgen05
+                assert torch.equal(ref.view(torch.int16), got.view(torch.int16)), (act, variant)
+            else:
+                assert_gemm_close(to_np(got), O.round_bf16(r), r32, 128, rows=v)
+                assert np.all(to_np(got)[~v] == 0)
+    r, v = O.gmm_ref(lhs, packed, scales, gs)
+    r32, _ = O.gmm_f32(lhs, packed, scales, gs)
+    out = dw.gmm_v2(x, b200, g, sc, rhs_layout="b200")
+    assert_gemm_close(bf16_to_np(out), r, r32, 128, rows=v)
+
+
+@pytest.mark.parametrize("gs,k,act,limit,sd,out_dt", [
+    ([1, 0, 2, 3, 5, 8, 0, 7], 192, None, None, "u8", "bf16"),        # <= 8 rows: one n8 tile
+    ([9, 16, 11, 0, 14, 3, 12, 15], 256, None, None, "u8", "f32"),    # 9-16 rows: two n8 tiles
+    ([4, 6, 0, 2, 8, 1, 3, 5], 128, "swiglu", None, "u8", "bf16"),
+    ([4, 6, 0, 2, 8, 1, 3, 5], 320, "swiglu", 7.0, "bf16", "bf16"),
+    ([13, 2, 16, 7, 0, 10, 1, 9], 64, None, None, "f32", "bf16"),
+    ([3, 1, 4, 1, 5, 9, 2, 6], 448, None, None, "u8_wide", "bf16"),   # e8m0 codes 0 and > 132
+])
+def test_gmm_decode_regime_b200(dw, gs, k, act, limit, sd, out_dt):
+    """Decode-sized groups on the B200 layout take the mma.sync kernel."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    m = sum(gs) + 5
+    n = 512
+    lo, hi = (0, 140) if sd == "u8_wide" else (118, 132)
+    lhs, packed, scales, gs = _case(11, m, k, n, len(gs), gs=gs, lo=lo, hi=hi)
+    if sd in ("u8", "u8_wide"):
+        sc = torch.from_numpy(scales)
+    elif sd == "bf16":
+        sc = torch.from_numpy(O.e8m0_decode(scales)).to(torch.bfloat16)
+    else:
+        sc = torch.from_numpy(O.e8m0_decode(scales))
+    b200 = dw.fp4_weight_to_codes(torch.from_numpy(packed).cuda())
+    kind = "swiglu" if act else None
+    a = {None: L.ACT_NONE, "swiglu": L.ACT_SWIGLU}[act]
+    if limit is not None:
+        a = L.ACT_SWIGLU_CLAMP
+    dt = torch.float32 if out_dt == "f32" else torch.bfloat16
+    n_out = n // 2 if act else n
+    out = torch.full((m, n_out), 3.0, dtype=dt, device="cuda")
+    ops.gmm_fp4_out(np_to_bf16(lhs), b200, sc.cuda(), torch.from_numpy(gs).cuda(), out, act=a,
+                    act_limit=limit or 0.0, zero_init=True, layout="b200")
+    torch.cuda.synchronize()
+    L.raise_on_device_error()
+    r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind, limit=limit, out_dtype=out_dt)
+    r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind, limit=limit)
+    got = to_np(out)
+    assert_gemm_close(got, O.round_bf16(r), r32, k, rows=v)
+    assert np.all(got[m - 5:] == 0)
+
+
+def test_gmm_decode_regime_group_offset(dw):
+    """EP shard through the mma.sync kernel: groups [3, 6) local, other rows
+    untouched without zero_init."""
+    from dw_tpu_b200 import ops
+    lhs, packed, scales, gs = _case(12, 60, 128, 256, 8, gs=[5, 9, 2, 7, 0, 4, 11, 6])
+    loc = slice(3, 6)
+    b200 = dw.fp4_weight_to_codes(torch.from_numpy(packed[loc]).cuda())
+    out = torch.full((60, 256), 3.0, dtype=torch.bfloat16, device="cuda")
+    ops.gmm_fp4_out(np_to_bf16(lhs), b200, torch.from_numpy(scales[loc]).cuda(),
+                    torch.from_numpy(gs).cuda(), out, group_offset=3, num_local_groups=3,
+                    layout="b200")
+    torch.cuda.synchronize()
+    r, v = O.gmm_ref(lhs, packed[loc], scales[loc], gs, group_offset=3)
+    r32, _ = O.gmm_f32(lhs, packed[loc], scales[loc], gs, group_offset=3)
+    got = bf16_to_np(out)
+    assert_gemm_close(got, r, r32, 128, rows=v)
+    assert np.all(got[~v] == 3.0)
 
 
 def test_gmm_deterministic(dw):

@@ -45,6 +45,37 @@ def test_pack_unpack_low_nibble_first():
     assert np.array_equal(O.unpack_nibbles(packed), nib)
 
 
+def test_b200_swizzle_is_a_lossless_bit_permutation():
+    rng = np.random.default_rng(8)
+    packed = rng.integers(0, 256, (2, 16, 64), dtype=np.uint8)
+    sw = O.b200_swizzle(packed)
+    assert np.array_equal(O.b200_unswizzle(sw), packed)
+    # every bit lands on a distinct position: popcounts are preserved
+    assert np.array_equal(np.unpackbits(sw).sum(), np.unpackbits(packed).sum())
+    one = np.zeros(4, np.uint8)
+    seen = set()
+    for bit in range(32):
+        w = np.array([1 << bit], np.uint32).view(np.uint8)
+        s = int(O.b200_swizzle(w).view(np.uint32)[0])
+        assert bin(s).count("1") == 1 and s not in seen
+        seen.add(s)
+    assert one.sum() == 0
+    raw = rng.integers(0, 256, (2, 64, 16), dtype=np.uint8)   # [g, k, n/2]
+    b = O.to_b200_layout(raw)
+    assert b.shape == (2, 32, 32)                             # [g, n, k/2]
+    assert np.array_equal(O.from_b200_layout(b), raw)
+    # element check of the fragment order against a direct formula
+    nib = O.unpack_nibbles(raw)                               # [g, k, n]
+    words = O.b200_unswizzle(b).view(np.uint32).reshape(2, 32 // 16, 64 // 16, 32)
+    for (g, kk, c) in [(0, 0, 0), (1, 63, 31), (0, 9, 17), (1, 22, 5), (0, 40, 30)]:
+        kb, dk, cb, dc = kk // 16, kk % 16, c // 16, c % 16
+        gid, j_hi = dc % 8, dc // 8
+        t, j_lo, j_k8 = (dk % 8) // 2, dk % 2, dk // 8
+        j = j_lo | (j_hi << 1) | (j_k8 << 2)
+        got = (int(words[g, cb, kb, gid * 4 + t]) >> (4 * j)) & 0xF
+        assert got == nib[g, kk, c], (g, kk, c)
+
+
 def test_e8m0_roundtrip_and_lossless_flag():
     e = np.arange(-126, 128)
     s = np.ldexp(np.ones(e.shape, np.float32), e).astype(np.float32)
