@@ -5,9 +5,11 @@
 One step = one MoE layer forward over one batch of synthetic tokens:
 route (top-8 sigmoid) -> permute -> gather -> gmm1 (SwiGLU) -> gmm2 ->
 combine. At N=1 the workload is BASELINE config 1 (T=64 tokens, H=4096,
-I=2048, E=256 FP4 experts with E8M0 scales); N>1 runs the same per-rank batch
-(weak scaling). The weights (3.3 GB) exceed L2, so every step streams them
-from HBM.
+I=2048, E=256 FP4 experts with E8M0 scales). N>1 runs the expert-parallel
+layer (weak scaling): every rank routes its own 64 tokens over all 256
+experts, holds experts [r*E/N, (r+1)*E/N), and exchanges rows with the
+one-shot NVLink dispatch/combine. The weights (3.3 GB, or 3.3/N GB per rank)
+exceed L2, so every step streams them from HBM.
 
 Printed (rank 0, one JSON line): value (device-timed, inputs resident), e2e
 (public API with pinned host buffers, copies inside the timed region),
@@ -198,11 +200,26 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     # Load-time re-layout of the FP4 weights for the B200 decode (once, untimed).
-    weights = synthetic.moe_weights(E, H, I, seed=args.seed, device=dev).to_b200()
+    # With N ranks, rank r holds experts [r*E/N, (r+1)*E/N) (expert parallel).
+    le = E // world
+    full = synthetic.moe_weights(E, H, I, seed=args.seed, device=dev)
+    if world > 1:
+        sl = slice(rank * le, (rank + 1) * le)
+        full = dw.FP4MoEWeights(full.w13[sl].clone(), full.s13[sl].clone(),
+                                full.w2[sl].clone(), full.s2[sl].clone())
+    weights = full.to_b200()
+    del full
+    torch.cuda.empty_cache()
     x_cpu, router = synthetic.layer_inputs(T_RANK, H, E, seed=args.seed + 100 * rank)
     x = x_cpu.to(dev)
     logits = (x.float() @ router.to(dev).float()).to(torch.bfloat16)
-    layer = dw.MoELayer(weights, TOPK, T_RANK)
+    ep_ctx = None
+    if world > 1:
+        from dw_tpu_b200 import ep as ep_mod
+        ep_ctx = ep_mod.create_context(max_tokens=T_RANK, hidden=H, topk=TOPK, num_experts=E)
+        layer = ep_mod.EPMoELayer(weights, ep_ctx, TOPK)
+    else:
+        layer = dw.MoELayer(weights, TOPK, T_RANK)
     out = torch.empty((T_RANK, H), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -229,8 +246,22 @@ def run_ours(args, rank, world, local_rank):
         gmm_ev.append((e0, e1, kw.get("act", L.ACT_NONE)))
         return r
 
-    import dw_tpu_b200.fused_moe as fm
-    fm.ops.gmm_fp4_out = timed_gmm
+    ops.gmm_fp4_out = timed_gmm
+    xchg_ev = []
+    if ep_ctx is not None:  # events around the exchange calls too
+        orig_d, orig_c = ep_ctx.dispatch, ep_ctx.combine
+
+        def timed(fn, tag):
+            def run(*a, **kw):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                r = fn(*a, **kw)
+                e1.record(stream)
+                xchg_ev.append((e0, e1, tag))
+                return r
+            return run
+        ep_ctx.dispatch, ep_ctx.combine = timed(orig_d, "dispatch"), timed(orig_c, "combine")
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
@@ -242,9 +273,14 @@ def run_ours(args, rank, world, local_rank):
         end.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
-    fm.ops.gmm_fp4_out = orig
+    ops.gmm_fp4_out = orig
+    if ep_ctx is not None:
+        ep_ctx.dispatch, ep_ctx.combine = orig_d, orig_c
     ms = start.elapsed_time(end)
     gmm_ms = [(a.elapsed_time(b), act) for a, b, act in gmm_ev]
+    xchg_ms = {"dispatch": [], "combine": []}
+    for a, b, tag in xchg_ev:
+        xchg_ms[tag].append(a.elapsed_time(b))
 
     # e2e through the public API with pinned host buffers.
     hx = x.cpu().pin_memory()
@@ -280,9 +316,9 @@ def run_ours(args, rank, world, local_rank):
     ms, e2e_ms = t.tolist()
 
     # Roofline of the dominant kernel (gmm_fp4): algorithmic bytes per launch.
-    gs = layer.group_sizes.cpu().numpy()
+    gs = (ep_ctx.recv_group_sizes if ep_ctx is not None else layer.group_sizes).cpu().numpy()
     active = int((gs > 0).sum())
-    rows = T_RANK * TOPK
+    rows = int(gs.sum())  # rows this rank's experts received
     w13_bytes = H * I + (H // 32) * 2 * I          # codes + e8m0 scales per expert
     w2_bytes = I * (H // 2) + (I // 32) * H
     gmm1_bytes = active * w13_bytes + rows * H * 2 + rows * I * 2
@@ -312,7 +348,25 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
         "h2d": hx.numel() * 2 + hl.numel() * 2,
         "d2h": hout.numel() * 2,
+        "launches_per_step": layer.kernels_per_forward,
     }
+    if ep_ctx is not None:
+        # NVLink bytes this rank sent per step: rows to other ranks' experts
+        # (dispatch, bf16) and expert outputs back to other ranks (combine).
+        ids = layer.ids.cpu().numpy()
+        remote_pairs = int(((ids // le) != rank).sum())
+        recv_remote = rows - int(np.bincount((ids // le).reshape(-1), minlength=world)[rank])
+        d_ms = statistics.mean(xchg_ms["dispatch"])
+        c_ms = statistics.mean(xchg_ms["combine"])
+        res["exchange"] = {
+            "dispatch_ms": round(d_ms, 4), "combine_ms": round(c_ms, 4),
+            "remote_pairs_sent": remote_pairs, "remote_pairs_received": recv_remote,
+            "nvlink_bytes_out_per_step": remote_pairs * H * 2 * 2,
+            "dispatch_GBps_out": round(remote_pairs * H * 2 / (d_ms * 1e-3) / 1e9, 1),
+            "combine_GBps_out": round(recv_remote * H * 2 / (c_ms * 1e-3) / 1e9, 1),
+            "link_peak_GBps": 770.0,
+        }
+        ep_ctx.close()
     return res
 
 
@@ -325,7 +379,7 @@ def main():
         print(f"--gpus {args.gpus} != WORLD_SIZE {world}", file=sys.stderr)
     config = {"workload": WORKLOAD, "tokens_per_rank": T_RANK, "hidden": H, "intermediate": I,
               "experts": E, "top_k": TOPK, "global_batch": T_RANK * world,
-              "parallelism": f"replicas{world}" if world > 1 else "single",
+              "parallelism": f"ep{world}" if world > 1 else "single",
               "l2": "inputs larger than L2 (3.3 GB of FP4 weights streamed per step)"}
 
     if args.impl == "reference":
@@ -376,9 +430,11 @@ def main():
         {k: (round(cb[k], 3) if k == "value" else cb[k])
          for k in ("value", "unit", "cores", "kind", "sample")},
         "clocks": res["clocks"],
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": res["launches_per_step"] * args.steps,
         "active_experts": res["active"],
     }
+    if "exchange" in res:
+        line["exchange"] = res["exchange"]
     print(json.dumps(line), flush=True)
 
 

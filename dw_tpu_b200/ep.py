@@ -142,6 +142,18 @@ class EPContext:
             pass
 
 
+def exchange_handles(handle: bytes, group=None) -> list[bytes]:
+    """All-gather one fixed-size handle per rank, in rank order."""
+    if len(handle) != L.EP_HANDLE_BYTES:
+        raise ValueError(f"handle must be {L.EP_HANDLE_BYTES} bytes")
+    world = dist.get_world_size(group)
+    handles: list = [None] * world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    if any(not isinstance(h, bytes) or len(h) != L.EP_HANDLE_BYTES for h in handles):
+        raise RuntimeError("a rank sent a malformed IPC handle")
+    return handles
+
+
 def create_context(group=None, *, max_tokens: int, hidden: int, topk: int,
                    num_experts: int) -> EPContext:
     """Collective: every rank of ``group`` creates its context on its current
@@ -149,9 +161,7 @@ def create_context(group=None, *, max_tokens: int, hidden: int, topk: int,
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     ctx = EPContext(rank, world, max_tokens=max_tokens, hidden=hidden, topk=topk,
                     num_experts=num_experts)
-    handles: list = [None] * world
-    dist.all_gather_object(handles, ctx.ipc_handle(), group=group)
-    ctx.connect(handles)
+    ctx.connect(exchange_handles(ctx.ipc_handle(), group))
     dist.barrier(group=group)
     return ctx
 
@@ -257,17 +267,37 @@ class EPMoELayer:
 
     kernels_per_forward = 8  # route, 3 dispatch, 2 gmm, 2 combine
 
-    def forward(self, hidden: torch.Tensor, logits: torch.Tensor,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-        t = hidden.shape[0]
+    def _route(self, logits: torch.Tensor):
+        t = logits.shape[0]
         ids, w16 = self.ids[:t], self.w16[:t]
         ops.route_topk_out(logits, self.top_k, ids, w16_out=w16, scoring_fn=self.scoring_fn,
                            renormalize=self.renormalize)
-        recv, gs = self.ctx.dispatch(hidden, ids)
-        ops.gmm_fp4_out(recv, self.w.w13, self.w.s13, gs, self.h1, act=self.act,
+        return ids, w16
+
+    def _experts(self) -> None:
+        gs = self.ctx.recv_group_sizes
+        ops.gmm_fp4_out(self.ctx.recv, self.w.w13, self.w.s13, gs, self.h1, act=self.act,
                         act_limit=self.act_limit, layout=self.w.layout, variant=self.variant)
         ops.gmm_fp4_out(self.h1, self.w.w2, self.w.s2, gs, self.y, layout=self.w.layout,
                         variant=self.variant)
+
+    def forward(self, hidden: torch.Tensor, logits: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        ids, w16 = self._route(logits)
+        self.ctx.dispatch(hidden, ids)
+        self._experts()
         return self.ctx.combine(self.y, w16, out)
 
     __call__ = forward
+
+    @staticmethod
+    def forward_emulated(layers: list["EPMoELayer"], hiddens, logits, outs=None):
+        """All ranks' layers in one process on one device (contexts from
+        ``create_local_contexts``): each exchange phase is issued for every
+        rank before the next phase."""
+        routed = [ly._route(lg) for ly, lg in zip(layers, logits)]
+        emulated_dispatch([ly.ctx for ly in layers], hiddens, [r[0] for r in routed])
+        for ly in layers:
+            ly._experts()
+        return emulated_combine([ly.ctx for ly in layers], [ly.y for ly in layers],
+                                [r[1] for r in routed], outs)

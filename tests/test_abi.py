@@ -86,6 +86,17 @@ def test_other_entry_points_validate(lib):
     assert lib.dwm_gmm_fp4_variant(fake, fake, 0, fake, 2, fake, 8, 16, 64, 256, 0, 8, 0, 0.0,
                                    0, 0, fake, 2, None) == -1  # explicit variant needs B200
     assert lib.dwm_device_status(None, None) == -1
+    import ctypes
+    ctx = ctypes.c_void_p()
+    assert lib.dwm_ep_create(0, 9, 4, 64, 2, 16, ctypes.byref(ctx)) == -1   # world > 8
+    assert lib.dwm_ep_create(2, 2, 4, 64, 2, 16, ctypes.byref(ctx)) == -1   # rank >= world
+    assert lib.dwm_ep_create(0, 3, 4, 64, 2, 16, ctypes.byref(ctx)) == -1   # 16 % 3
+    assert lib.dwm_ep_create(0, 2, 4, 60, 2, 16, ctypes.byref(ctx)) == -1   # hidden % 8
+    assert ctx.value is None
+    assert lib.dwm_ep_dispatch(None, fake, fake, 4, fake, 7, None) == -1
+    assert lib.dwm_ep_combine(None, fake, 0, fake, 0, fake, 0, 3, None) == -1
+    assert lib.dwm_ep_ipc_handle(None, None) == -1
+    assert lib.dwm_ep_destroy(None) == 0
 
 
 def test_python_shims_raise_value_error_without_gpu():

@@ -1,0 +1,192 @@
+"""Expert-parallel one-shot dispatch / combine on the GPU vs the oracle,
+bit-exact: the exchange of ``world`` ranks emulated on one device (all
+contexts in this process, phases issued rank by rank so that every wait is
+already satisfied when it runs)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests.gpu_util import bf16_to_np, np_to_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ep():
+    from dw_tpu_b200 import ep as E
+    return E
+
+
+def _inputs(world, t_per_rank, e, k, h, seed, dist="uniform"):
+    from dw_tpu_b200 import synthetic
+    rng = np.random.default_rng(seed)
+    hid, ids, w = [], [], []
+    for r in range(world):
+        t = t_per_rank[r] if isinstance(t_per_rank, (list, tuple)) else t_per_rank
+        hid.append(O.round_bf16(rng.standard_normal((t, h)).astype(np.float32)))
+        if t:
+            i, ww = synthetic.route_ids(t, e, k, seed=seed * 31 + r, dist=dist)
+        else:
+            i, ww = np.zeros((0, k), np.int32), np.zeros((0, k), np.float32)
+        ids.append(i)
+        w.append(ww)
+    return hid, ids, w
+
+
+def _bits(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("world,t,e,k,h,dist", [
+    (2, 16, 256, 8, 4096, "uniform"),
+    (4, 128, 256, 8, 512, "zipf"),
+    (8, 64, 256, 8, 256, "uniform"),
+    (8, [5, 0, 17, 64, 1, 33, 2, 9], 64, 6, 128, "zipf"),   # ragged, one empty rank
+    (1, 40, 16, 4, 64, "uniform"),                           # degenerate: no exchange
+])
+def test_ep_dispatch_combine_bit_exact(ep, world, t, e, k, h, dist):
+    hid, ids, w = _inputs(world, t, e, k, h, seed=world + e, dist=dist)
+    tmax = max(x.shape[0] for x in hid) or 1
+    ctxs = ep.create_local_contexts(world, max_tokens=tmax, hidden=h, topk=k, num_experts=e)
+    try:
+        res = ep.emulated_dispatch(ctxs, [np_to_bf16(x) for x in hid],
+                                   [torch.from_numpy(i).cuda() for i in ids])
+        torch.cuda.synchronize()
+        from dw_tpu_b200 import _lib as L
+        L.raise_on_device_error()
+        ref = O.ep_dispatch(hid, ids, e)
+        ys = []
+        for r, ((recv, gs), (rrows, rgs, rsrc)) in enumerate(zip(res, ref)):
+            n = int(rgs.sum())
+            assert np.array_equal(gs.cpu().numpy(), rgs), r
+            assert np.array_equal(_bits(recv[:n]), O.f32_to_bf16_bits(rrows)), r
+            # expert outputs: any values, in receive order
+            y = O.round_bf16(np.random.default_rng(r).standard_normal(
+                (ctxs[r].capacity, h)).astype(np.float32))
+            ys.append(y)
+        outs = ep.emulated_combine(ctxs, [np_to_bf16(y) for y in ys],
+                                   [torch.from_numpy(x).cuda() for x in w])
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        want = O.ep_combine_korder([y[:int(g[1].sum())] for y, g in zip(ys, ref)],
+                                   [g[2] for g in ref], w)
+        for r in range(world):
+            assert np.array_equal(bf16_to_np(outs[r]), want[r]), r
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_ep_repeated_steps_and_f32_outputs(ep):
+    """Monotonic epochs: several steps in a row with new inputs each time; f32
+    expert outputs and f32 combine output."""
+    world, e, k, h = 4, 32, 4, 256
+    ctxs = ep.create_local_contexts(world, max_tokens=48, hidden=h, topk=k, num_experts=e)
+    from dw_tpu_b200 import _lib as L
+    try:
+        for step in range(5):
+            t = [48, 7, 30, 0][step % 4:] + [48, 7, 30, 0][:step % 4]
+            hid, ids, w = _inputs(world, t, e, k, h, seed=100 + step, dist="zipf")
+            ep.emulated_dispatch(ctxs, [np_to_bf16(x) for x in hid],
+                                 [torch.from_numpy(i).cuda() for i in ids])
+            ref = O.ep_dispatch(hid, ids, e)
+            ys = [np.random.default_rng(step * 8 + r).standard_normal(
+                (ctxs[r].capacity, h)).astype(np.float32) for r in range(world)]
+            outs = [torch.empty((hid[r].shape[0], h), dtype=torch.float32, device="cuda")
+                    for r in range(world)]
+            ep.emulated_combine(ctxs, [torch.from_numpy(y).cuda() for y in ys],
+                                [torch.from_numpy(x).cuda() for x in w], outs)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            for r in range(world):
+                n = int(ref[r][1].sum())
+                assert np.array_equal(ctxs[r].recv_group_sizes.cpu().numpy(), ref[r][1])
+                assert np.array_equal(_bits(ctxs[r].recv[:n]), O.f32_to_bf16_bits(ref[r][0]))
+            want = O.ep_combine_korder([y[:int(g[1].sum())] for y, g in zip(ys, ref)],
+                                       [g[2] for g in ref], w, out_dtype="f32")
+            for r in range(world):
+                assert np.array_equal(outs[r].cpu().numpy(), want[r]), (step, r)
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_ep_invalid_ids_reported_and_dropped(ep):
+    world, e, k, h = 2, 16, 2, 64
+    ctxs = ep.create_local_contexts(world, max_tokens=8, hidden=h, topk=k, num_experts=e)
+    from dw_tpu_b200 import _lib as L
+    try:
+        hid, ids, w = _inputs(world, 8, e, k, h, seed=5)
+        ids[0][3, 1] = 99   # out of range: dropped, reported
+        ep.emulated_dispatch(ctxs, [np_to_bf16(x) for x in hid],
+                             [torch.from_numpy(i).cuda() for i in ids])
+        assert L.device_status() & L.DEV_BAD_INDEX
+        gs = [c.recv_group_sizes.cpu().numpy() for c in ctxs]
+        assert sum(int(g.sum()) for g in gs) == 2 * 8 * k - 1
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_ep_rejects_bad_arguments(ep):
+    from dw_tpu_b200 import _lib as L
+    with pytest.raises(ValueError):
+        ep.EPContext(0, 3, max_tokens=4, hidden=64, topk=2, num_experts=16)  # 16 % 3
+    with pytest.raises(ValueError):
+        ep.EPContext(0, 2, max_tokens=4, hidden=60, topk=2, num_experts=16)  # h % 8
+    ctxs = ep.create_local_contexts(2, max_tokens=4, hidden=64, topk=2, num_experts=16)
+    try:
+        x = torch.zeros((5, 64), dtype=torch.bfloat16, device="cuda")
+        i = torch.zeros((5, 2), dtype=torch.int32, device="cuda")
+        with pytest.raises(ValueError):
+            ctxs[0].dispatch(x, i)  # 5 tokens > max_tokens
+        assert L.OK == 0
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+@pytest.mark.parametrize("layout,t", [("b200", 24), ("b200", 3), ("e2m1", 10)])
+def test_ep_layer_matches_single_device_layer(ep, layout, t):
+    """The EP layer of 4 emulated ranks gives every rank the output of the
+    single-device layer (all experts) on that rank's tokens, within the GEMM
+    tolerance (the grouped matmuls see the rows in another order)."""
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import synthetic
+    from tests.gpu_util import gemm_rel_tol, rel_fro
+    world, e, h, i, k = 4, 16, 512, 256, 4
+    w = synthetic.moe_weights(e, h, i, seed=4, device="cuda")
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 9, "cuda", lo=118,
+                                               hi=121))
+    if layout == "b200":
+        w = w.to_b200()
+    le = e // world
+    ctxs = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        layers = []
+        for r in range(world):
+            lw = dw.FP4MoEWeights(w.w13[r * le:(r + 1) * le], w.s13[r * le:(r + 1) * le],
+                                  w.w2[r * le:(r + 1) * le], w.s2[r * le:(r + 1) * le],
+                                  w.layout)
+            layers.append(ep.EPMoELayer(lw, ctxs[r], k))
+        xs, lgs = [], []
+        for r in range(world):
+            x, router = synthetic.layer_inputs(t, h, e, seed=20 + r)
+            xs.append(x.cuda())
+            lgs.append((x.float() @ router.float()).to(torch.bfloat16).cuda())
+        outs = ep.EPMoELayer.forward_emulated(layers, xs, lgs)
+        torch.cuda.synchronize()
+        from dw_tpu_b200 import _lib as L
+        L.raise_on_device_error()
+        single = dw.MoELayer(w, k, t)
+        for r in range(world):
+            ref = single(xs[r], lgs[r])
+            torch.cuda.synchronize()
+            rf = rel_fro(bf16_to_np(outs[r]), bf16_to_np(ref))
+            assert rf < gemm_rel_tol(i), (r, rf)
+    finally:
+        for c in ctxs:
+            c.close()
