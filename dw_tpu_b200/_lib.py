@@ -73,6 +73,9 @@ SIGNATURES = {
     "dwm_permute": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "dwm_dispatch_gather": ([_P, _I, _I, _P, _I64, _P, _P], _I),
     "dwm_combine": ([_P, _I, _I64, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
+    "dwm_moe_layer_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
+    "dwm_moe_layer_fp4": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I,
+                           _F, _I, _P, _SZ, _P, _P], _I),
     "dwm_ep_create": ([_I, _I, _I, _I, _I, _I, _c.POINTER(_P)], _I),
     "dwm_ep_ipc_handle": ([_P, _P], _I),
     "dwm_ep_connect": ([_P, _P], _I),

@@ -158,8 +158,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   using L = Smem<SD>;
   constexpr int CS = L::CS;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // 1 KiB alignment by pointer arithmetic on the shared array itself, so the
+  // compiler keeps every access below in the shared window (LDS/STS, not LD/ST).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* cs_full = bars;
   uint64_t* cs_empty = cs_full + CS;

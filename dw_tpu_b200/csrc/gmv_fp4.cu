@@ -19,9 +19,10 @@
 //     token fragments are pre-scaled by 2^64 and the k-block factor is
 //     2^(c-65), all exact powers of two, so the result equals the reference's
 //     bf16(value * scale) x bf16 token products (E0901:84-95) up to the f32
-//     summation order. Codes 0 (scale +0) and 1..192 take this path; a k block
-//     holding a code above 192 (scales >= 2^66, including the 255 = inf code)
-//     falls back to multiplying the weights in bf16 exactly like the reference.
+//     summation order. Codes 1..192 take this path; a stage holding code 0
+//     (scale +0) or a code above 192 (scales >= 2^66, including the 255 = inf
+//     code) multiplies the weights in bf16 instead, exactly like the
+//     reference. The check is one SWAR test per lane per stage.
 //   * bf16 / f32 scales (reference: cast to bf16, one bf16 multiply) are
 //     multiplied into the decoded weights, which reproduces that rounding.
 //   * each warp streams its own tasks through a private ring of S stages,
@@ -29,6 +30,8 @@
 //     scale tiles) issued by lane 0, with prefetch running ahead across task
 //     boundaries; token tiles land 128-byte swizzled so B-fragment loads are
 //     bank-conflict free.
+#include <type_traits>
+
 #include "fp4_decode.cuh"
 
 namespace dwm {
@@ -49,6 +52,10 @@ constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
 #endif
 #ifndef DWM_GMV_STAGES2
 #define DWM_GMV_STAGES2 3
+#endif
+// Warps per CTA for 8-row token tiles (E8M0 / bf16 scales).
+#ifndef DWM_GMV_WARPS1
+#define DWM_GMV_WARPS1 16
 #endif
 // 1: feed the raw decode (value * 2^-126, a bf16 subnormal for 0.5) to the
 // MMA on the E8M0 path; 0: first normalise it by 2^62 (4 more multiplies per
@@ -76,7 +83,7 @@ struct Cfg {
   static constexpr int SC_TILE = 64 * es < 128 ? 128 : 64 * es;
   static constexpr int SC = 2 * SC_TILE;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 1023) & ~1023;
-  static constexpr int WARPS = (NT == 1 && SD != DWM_F32) ? 16 : 12;
+  static constexpr int WARPS = (NT == 1 && SD != DWM_F32) ? DWM_GMV_WARPS1 : 12;
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
@@ -103,8 +110,7 @@ struct Args {
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -113,8 +119,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // d = a * b (accumulator starts at zero).
 __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                             uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%10,%10,%10,%10};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
@@ -168,8 +173,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
   constexpr int S = C::S;
   constexpr int es = C::es;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // 1 KiB alignment by pointer arithmetic on the shared array itself, so the
+  // compiler keeps every access below in the shared window (LDS, not LD).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   int* row_start = reinterpret_cast<int*>(smem + C::OFF_ROWS);
   int* task_prefix = reinterpret_cast<int*>(smem + C::OFF_TASKS);
   const int warp = threadIdx.x >> 5;
@@ -271,39 +277,43 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
   // ---- producer state (lane 0): the next (task, stage) to fetch ----
   uint64_t pol_stream = 0, pol_keep = 0;
   int iss_idx = first, iss_st = 0;
-  Task iss_t{};
-  int iss_cb0 = 0, iss_cb1 = 0;
+  // Per-task TMA coordinates: token row, the two code-tile rows, the two
+  // scale-tile columns and the task's first scale row.
+  int y_tok = 0, y_c0 = 0, y_c1 = 0, x_s0 = 0, x_s1 = 0, y_s = 0;
+  auto set_task = [&](int idx) {
+    const Task t = get_task<NT>(idx, row_start, task_prefix, a);
+    int cb0, cb1;
+    task_blocks(t, a, cb0, cb1);
+    y_tok = t.row0;
+    y_c0 = t.g * (a.n / 16) + cb0;
+    y_c1 = t.g * (a.n / 16) + cb1;
+    x_s0 = 16 * cb0;
+    x_s1 = 16 * cb1;
+    y_s = t.g * (a.k / 32);
+  };
   uint32_t issued = 0;  // stages issued so far (ring sequence)
   auto issue_one = [&]() {
     const int slot = (int)(issued % S);
     uint64_t* bar = &bars[slot];
     mbar_arrive_expect_tx(bar, C::TX);
-    const int x_codes = iss_st * 4 * 32;
-    const int y_blocks = iss_t.g * (a.n / 16);
-    const int y_scales = iss_t.g * (a.k / 32) + iss_st * 2;
-    tma_load_2d(tok_s + slot * C::TOK, &tm_lhs, bar, iss_st * KSTAGE, iss_t.row0, pol_keep);
-    tma_load_2d(code_s + slot * CODE_BYTES, &tm_codes, bar, x_codes, y_blocks + iss_cb0,
-                pol_stream);
-    tma_load_2d(code_s + slot * CODE_BYTES + 1024, &tm_codes, bar, x_codes, y_blocks + iss_cb1,
-                pol_stream);
-    tma_load_2d(sc_s + slot * C::SC, &tm_scales, bar, 16 * iss_cb0, y_scales, pol_stream);
-    tma_load_2d(sc_s + slot * C::SC + C::SC_TILE, &tm_scales, bar, 16 * iss_cb1, y_scales,
-                pol_stream);
+    const int xc = iss_st * 4 * 32;
+    tma_load_2d(tok_s + slot * C::TOK, &tm_lhs, bar, iss_st * KSTAGE, y_tok, pol_keep);
+    tma_load_2d(code_s + slot * CODE_BYTES, &tm_codes, bar, xc, y_c0, pol_stream);
+    tma_load_2d(code_s + slot * CODE_BYTES + 1024, &tm_codes, bar, xc, y_c1, pol_stream);
+    uint8_t* sdst = sc_s + slot * C::SC;
+    tma_load_2d(sdst, &tm_scales, bar, x_s0, y_s + 2 * iss_st, pol_stream);
+    tma_load_2d(sdst + C::SC_TILE, &tm_scales, bar, x_s1, y_s + 2 * iss_st, pol_stream);
     ++issued;
     if (++iss_st == NSTAGE) {
       iss_st = 0;
       iss_idx += wstride;
-      if (iss_idx < total) {
-        iss_t = get_task<NT>(iss_idx, row_start, task_prefix, a);
-        task_blocks(iss_t, a, iss_cb0, iss_cb1);
-      }
+      if (iss_idx < total) set_task(iss_idx);
     }
   };
   if (lane == 0 && first < total) {
     pol_stream = policy_evict_first();
     pol_keep = policy_evict_last();
-    iss_t = get_task<NT>(first, row_start, task_prefix, a);
-    task_blocks(iss_t, a, iss_cb0, iss_cb1);
+    set_task(first);
     while (issued < (uint32_t)S && iss_idx < total) issue_one();
   }
   __syncwarp();
@@ -334,111 +344,116 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
       const uint8_t* tok = tok_s + slot * C::TOK;
       const uint8_t* code = code_s + slot * CODE_BYTES;
       const uint8_t* sc = sc_s + slot * C::SC;
+      // PRE: multiply the decoded weights by their scale in bf16 (the
+      // reference's rounding; bf16/f32 scales, or E8M0 codes outside the
+      // post-MMA range), else scale the f32 partial of each k32 block.
+      auto stage = [&](auto pre_tag) {
+        constexpr bool PRE = decltype(pre_tag)::value;
+        constexpr uint32_t M1 = C::POST ? kBf16x2_2p62 : kBf16x2_2p126;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // 32-deep k block inside the stage
-        // Scales of the lane's columns: block i, column gid (+8 for hc = 1);
-        // tile i/2 holds 2 rows (k32 blocks) of 32 columns.
-        uint32_t code8[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int hc = 0; hc < 2; ++hc) {
-            const uint8_t* p =
-                sc + (i >> 1) * C::SC_TILE + (h * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
-            if constexpr (SD == DWM_U8) {
-              code8[i][hc] = *p;
-            } else if constexpr (SD == DWM_BF16) {
-              code8[i][hc] = *reinterpret_cast<const uint16_t*>(p);
-            } else {
-              code8[i][hc] = f32_to_bf16_bits(*reinterpret_cast<const float*>(p));
-            }
-          }
-        bool slow = !C::POST;
-        if constexpr (C::POST) {
-          bool big = false;
+        for (int h = 0; h < 2; ++h) {  // 32-deep k block inside the stage
+          // Scales of the lane's columns: block i, column gid (+8 for hc =
+          // 1); tile i/2 holds 2 rows (k32 blocks) of 32 columns.
+          uint32_t wm[4][2];
+          float post[4][2];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            big |= (code8[i][0] > C::POST_MAX) | (code8[i][1] > C::POST_MAX);
-          slow = __any_sync(0xffffffffu, big);
-        }
-        // Per-column factors applied to the partial (fast path) or to the
-        // weights (slow path).
-        float post[4][2];
-        uint32_t wmul[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int hc = 0; hc < 2; ++hc) {
-            const uint32_t c = code8[i][hc];
-            if constexpr (C::POST) {
-              if (C::RAW)
-                post[i][hc] = slow ? 1.0f : (c ? __uint_as_float((c + 62u) << 23) : 0.0f);
+            for (int hc = 0; hc < 2; ++hc) {
+              const uint8_t* p =
+                  sc + (i >> 1) * C::SC_TILE + (h * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
+              uint32_t c;
+              if constexpr (SD == DWM_U8)
+                c = *p;
+              else if constexpr (SD == DWM_BF16)
+                c = *reinterpret_cast<const uint16_t*>(p);
               else
-                post[i][hc] = slow ? 1.0f : __uint_as_float(c << 23);  // c = 0 -> +0
-              wmul[i][hc] = (c << 7) * 0x10001u;  // bf16 2^(c-127), c = 0 -> +0
-            } else {
-              post[i][hc] = 1.0f;
-              wmul[i][hc] = c * 0x10001u;  // the bf16 scale, both halves
-            }
-          }
-        float part[4][NT][4];
-#pragma unroll
-        for (int kk2 = 0; kk2 < 2; ++kk2) {
-          const int kk = 2 * h + kk2;  // k16 block inside the stage
-          uint32_t b[NT][2];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const int r = nt * 8 + gid;  // token row; the 128-byte swizzle XORs chunk with r%8
-            const uint8_t* row = tok + r * 128 + 4 * tig;
-            uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk) ^ gid) << 4));
-            uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk + 1) ^ gid) << 4));
-            if (r >= t.rows) b0 = b1 = 0u;
-            if constexpr (C::POST) {
-              b0 = hmul2_bf16(b0, kBf16x2_2p64);
-              b1 = hmul2_bf16(b1, kBf16x2_2p64);
-            }
-            b[nt][0] = b0;
-            b[nt][1] = b1;
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t w =
-                *reinterpret_cast<const uint32_t*>(code + i * 512 + kk * 128 + lane * 4);
-            uint32_t af[4];
-            tvals<true>(w, af);
-            if (slow) {
-              const uint32_t m1 = C::POST ? kBf16x2_2p62 : kBf16x2_2p126;
-              af[0] = hmul2_bf16(hmul2_bf16(af[0], m1), wmul[i][0]);
-              af[1] = hmul2_bf16(hmul2_bf16(af[1], m1), wmul[i][1]);
-              af[2] = hmul2_bf16(hmul2_bf16(af[2], m1), wmul[i][0]);
-              af[3] = hmul2_bf16(hmul2_bf16(af[3], m1), wmul[i][1]);
-            } else if (!C::RAW) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) af[j] = hmul2_bf16(af[j], kBf16x2_2p62);
-            }
-            if constexpr (C::POST) {
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                if (kk2 == 0)
-                  mma_16816_z(part[i][nt], af, b[nt][0], b[nt][1]);
-                else
-                  mma_16816(part[i][nt], af, b[nt][0], b[nt][1]);
+                c = f32_to_bf16_bits(*reinterpret_cast<const float*>(p));
+              if constexpr (PRE) {
+                wm[i][hc] = SD == DWM_U8 ? (c << 7) * 0x10001u  // bf16 2^(c-127), 0 -> +0
+                                         : c * 0x10001u;        // the bf16 scale
+              } else {
+                post[i][hc] = C::RAW ? __uint_as_float((c + 62u) << 23)  // 2^(c-65)
+                                     : __uint_as_float(c << 23);         // 2^(c-127)
               }
-            } else {
+            }
+          float part[4][NT][4];
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) mma_16816(acc[i][nt], af, b[nt][0], b[nt][1]);
+          for (int kk2 = 0; kk2 < 2; ++kk2) {
+            const int kk = 2 * h + kk2;  // k16 block inside the stage
+            // B fragments. Rows past the task (other groups' tokens or the
+            // tile's zero fill) only reach output columns that are not stored.
+            uint32_t b[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              // token row nt*8 + gid; the 128-byte swizzle XORs the chunk with gid
+              const uint8_t* row = tok + (nt * 8 + gid) * 128 + 4 * tig;
+              uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk) ^ gid) << 4));
+              uint32_t b1 =
+                  *reinterpret_cast<const uint32_t*>(row + (((2 * kk + 1) ^ gid) << 4));
+              if constexpr (C::POST) {
+                b0 = hmul2_bf16(b0, kBf16x2_2p64);
+                b1 = hmul2_bf16(b1, kBf16x2_2p64);
+              }
+              b[nt][0] = b0;
+              b[nt][1] = b1;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t w =
+                  *reinterpret_cast<const uint32_t*>(code + i * 512 + kk * 128 + lane * 4);
+              uint32_t af[4];
+              tvals<true>(w, af);
+              if constexpr (PRE) {
+                af[0] = hmul2_bf16(hmul2_bf16(af[0], M1), wm[i][0]);
+                af[1] = hmul2_bf16(hmul2_bf16(af[1], M1), wm[i][1]);
+                af[2] = hmul2_bf16(hmul2_bf16(af[2], M1), wm[i][0]);
+                af[3] = hmul2_bf16(hmul2_bf16(af[3], M1), wm[i][1]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma_16816(acc[i][nt], af, b[nt][0], b[nt][1]);
+              } else {
+                if constexpr (!C::RAW) {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) af[j] = hmul2_bf16(af[j], kBf16x2_2p62);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  if (kk2 == 0)
+                    mma_16816_z(part[i][nt], af, b[nt][0], b[nt][1]);
+                  else
+                    mma_16816(part[i][nt], af, b[nt][0], b[nt][1]);
+                }
+              }
             }
           }
+          if constexpr (!PRE) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  acc[i][nt][e] = fmaf(part[i][nt][e], post[i][e >> 1], acc[i][nt][e]);
+          }
         }
-        if constexpr (C::POST) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                acc[i][nt][e] = fmaf(part[i][nt][e], post[i][e >> 1], acc[i][nt][e]);
-        }
+      };
+      if constexpr (C::POST) {
+        // One check per stage for the whole warp: lane l tests 4 of the 128
+        // scale bytes; the post-MMA path needs every code in [1, POST_MAX].
+        const uint32_t v =
+            *reinterpret_cast<const uint32_t*>(sc + (lane >> 4) * C::SC_TILE + (lane & 15) * 4);
+        const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
+        uint32_t high_byte;
+        if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
+          high_byte = ((v & 0x7F7F7F7Fu) + 0x3F3F3F3Fu) & v & 0x80808080u;
+        else  // a byte == 255
+          high_byte = (~v - 0x01010101u) & v & 0x80808080u;
+        if (__any_sync(0xffffffffu, (zero_byte | high_byte) != 0u))
+          stage(std::true_type{});
+        else
+          stage(std::false_type{});
+      } else {
+        stage(std::true_type{});
       }
       __syncwarp();  // every lane is done with this slot
       if (lane == 0 && iss_idx < total) issue_one();

@@ -67,7 +67,7 @@ class MoELayer:
     def __init__(self, weights: FP4MoEWeights, top_k: int, max_tokens: int, *,
                  scoring_fn: str = "sigmoid", renormalize: bool = True,
                  act_limit: float | None = None, f32_reduce: bool = False,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", gemm_variant: int = 0):
         self.w = weights
         self.top_k = int(top_k)
         self.max_tokens = int(max_tokens)
@@ -76,6 +76,7 @@ class MoELayer:
         self.act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
         self.act_limit = 0.0 if act_limit is None else float(act_limit)
         self.f32_reduce = f32_reduce
+        self.gemm_variant = int(gemm_variant)  # 0: chosen per call (dwm_gmm_fp4_variant)
         e, h, i = weights.num_experts, weights.hidden_size, weights.intermediate_size
         rows = self.max_tokens * self.top_k
         dev = torch.device(device)
@@ -106,9 +107,11 @@ class MoELayer:
         ops.dispatch_gather_out(hidden, self.tok[:rows], x)
         h1 = self.h1[:rows]
         ops.gmm_fp4_out(x, self.w.w13, self.w.s13, self.group_sizes, h1, act=self.act,
-                        act_limit=self.act_limit, layout=self.w.layout)
+                        act_limit=self.act_limit, layout=self.w.layout,
+                        variant=self.gemm_variant)
         y = self.y[:rows]
-        ops.gmm_fp4_out(h1, self.w.w2, self.w.s2, self.group_sizes, y, layout=self.w.layout)
+        ops.gmm_fp4_out(h1, self.w.w2, self.w.s2, self.group_sizes, y, layout=self.w.layout,
+                        variant=self.gemm_variant)
         if out is None:
             out = torch.empty((t, self.w.hidden_size), dtype=torch.bfloat16,
                               device=hidden.device)

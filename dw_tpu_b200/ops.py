@@ -221,6 +221,39 @@ def combine_out(x, indices, topk_weights, topk, out, stream=None):
     return out
 
 
+def moe_layer_workspace_bytes(num_tokens, hidden, inter, topk, num_experts, y_f32=False):
+    return int(L.lib().dwm_moe_layer_workspace_bytes(int(num_tokens), int(hidden), int(inter),
+                                                     int(topk), int(num_experts), int(y_f32)))
+
+
+def moe_layer_fp4_out(hidden, logits, top_k, w13, s13, w2, s2, out, workspace, *,
+                      layout="e2m1", scoring_fn="sigmoid", renormalize=True, act_limit=None,
+                      f32_reduce=False, stream=None):
+    """The whole single-device layer in one C call (dwm_moe_layer_fp4):
+    route -> permute -> gather -> gmm1 (SwiGLU) -> gmm2 -> combine, with its
+    intermediates in ``workspace`` (uint8, moe_layer_workspace_bytes)."""
+    L.require_cuda(hidden, logits, w13, s13, w2, s2, out, workspace)
+    if hidden.dtype != torch.bfloat16 or hidden.dim() != 2 or not hidden.is_contiguous():
+        raise ValueError("hidden must be a contiguous bf16 [t, h] tensor")
+    t, h = hidden.shape
+    if logits.dim() != 2 or logits.shape[0] != t or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous [t, e] tensor")
+    e = logits.shape[1]
+    if scoring_fn not in _SCORING:
+        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
+    inter = s2.shape[1] * 32
+    act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
+    rc = L.lib().dwm_moe_layer_fp4(
+        hidden.data_ptr(), logits.data_ptr(), L.dtype_code(logits.dtype), t, h, e, int(top_k),
+        _SCORING[scoring_fn], int(bool(renormalize)), _u8view(w13).data_ptr(), s13.data_ptr(),
+        _u8view(w2).data_ptr(), s2.data_ptr(), L.LAYOUTS[layout], L.dtype_code(s13.dtype),
+        inter, act, 0.0 if act_limit is None else float(act_limit), int(bool(f32_reduce)),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(), out.data_ptr(),
+        L.stream_ptr() if stream is None else stream)
+    L.check(rc, "moe_layer_fp4")
+    return out
+
+
 def e8m0_encode_out(scale, codes, lossless, stream=None):
     L.require_cuda(scale, codes, lossless)
     if scale.dtype != torch.float32:

@@ -31,6 +31,8 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--layout", default="b200", choices=["b200", "e2m1"])
+    p.add_argument("--variant", type=int, default=0,
+                   help="dwm_gmm_fp4_variant kernel choice (0 = automatic)")
     a = p.parse_args()
     e, h, i, t, k = a.experts, a.hidden, a.inter, a.tokens, a.topk
     w = synthetic.moe_weights(e, h, i, seed=a.seed, device="cuda")
@@ -39,7 +41,7 @@ def main():
     x, router = synthetic.layer_inputs(t, h, e, seed=a.seed)
     x = x.cuda()
     logits = (x.float() @ router.cuda().float()).to(torch.bfloat16)
-    layer = MoELayer(w, k, t)
+    layer = MoELayer(w, k, t, gemm_variant=a.variant)
     out = torch.empty((t, h), dtype=torch.bfloat16, device="cuda")
     for _ in range(a.warmup):
         layer(x, logits, out=out)
@@ -80,6 +82,8 @@ def main():
         "experts": e, "active": active, "tokens": t, "step_ms": round(step, 4),
         "gmm1_ms": round(m1, 4), "gmm1_GBps": round(b1 / m1 / 1e6, 1),
         "gmm2_ms": round(m2, 4), "gmm2_GBps": round(b2 / m2 / 1e6, 1),
+        "gmm1_TFLOPs": round(2 * rows * h * 2 * i / m1 / 1e9, 1),
+        "gmm2_TFLOPs": round(2 * rows * i * h / m2 / 1e9, 1),
         "tokens_per_s": round(t / step * 1e3, 1),
     }))
 

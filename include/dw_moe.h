@@ -175,6 +175,26 @@ int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int32_t* indic
                 const void* w, int w_dtype, int t, int h, int topk, void* out, int out_dtype,
                 void* stream);
 
+/* ---- the single-device layer in one call ---------------------------------
+ * fused_moe_func's GMM path (X0104:88-98, X0405, X0404 on one device):
+ * dwm_route_topk -> dwm_permute -> dwm_dispatch_gather -> dwm_gmm_fp4 (gmm1,
+ * SwiGLU) -> dwm_gmm_fp4 (gmm2) -> dwm_combine, bit-identical to making those
+ * calls in turn. hidden bf16 [num_tokens, hidden_size]; logits [num_tokens,
+ * num_experts] (bf16 or f32); w13 / s13 / w2 / s2 as dwm_gmm_fp4 takes them
+ * (w13: k = hidden_size, n = 2*inter; w2: k = inter, n = hidden_size);
+ * y_f32 = 1 keeps gmm2's output in f32 (MOE_F32_REDUCE, X0106:18-29);
+ * out bf16 [num_tokens, hidden_size]. The intermediates live in `workspace`
+ * (256-byte aligned, at least dwm_moe_layer_workspace_bytes bytes; nothing in
+ * it needs to start at zero). */
+size_t dwm_moe_layer_workspace_bytes(int num_tokens, int hidden, int inter, int topk,
+                                     int num_experts, int y_f32);
+int dwm_moe_layer_fp4(const void* hidden, const void* logits, int logits_dtype, int num_tokens,
+                      int hidden_size, int num_experts, int topk, int scoring, int renormalize,
+                      const void* w13, const void* s13, const void* w2, const void* s2,
+                      int codes_format, int scale_dtype, int inter, int act, float act_limit,
+                      int y_f32, void* workspace, size_t workspace_bytes, void* out,
+                      void* stream);
+
 /* ---- expert-parallel exchange over NVLink peer memory ---------------------
  * Replaces the GMM_EP exchange: all_gather_local + the per-shard stable sort
  * (KO:152-164, X0101:56-104, X0107:34-51) on the way in, and the masked f32

@@ -91,3 +91,36 @@ def test_layer_graph_capture_replays_bitwise(dw):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(res.view(torch.int16), out.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout,f32_reduce,limit", [("e2m1", False, None), ("b200", True, None),
+                                                      ("b200", False, 7.0)])
+def test_one_call_layer_matches_layer_object(dw, layout, f32_reduce, limit):
+    """dwm_moe_layer_fp4 (one C call, caller workspace) gives the bits of the
+    six-call MoELayer, on two calls in a row with new tokens."""
+    from dw_tpu_b200 import ops, synthetic
+    t, e, h, i, k = 40, 16, 512, 256, 4
+    w = synthetic.moe_weights(e, h, i, seed=6, device="cuda")
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 11, "cuda", lo=118,
+                                               hi=121))
+    if layout == "b200":
+        w = w.to_b200()
+    layer = dw.MoELayer(w, k, t, f32_reduce=f32_reduce, act_limit=limit)
+    nbytes = ops.moe_layer_workspace_bytes(t, h, i, k, e, f32_reduce)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    for seed in (30, 31):
+        x, router = synthetic.layer_inputs(t, h, e, seed=seed)
+        x = x.cuda()
+        lg = (x.float() @ router.cuda().float()).to(torch.bfloat16)
+        ref = layer(x, lg)
+        got = torch.empty_like(ref)
+        ops.moe_layer_fp4_out(x, lg, k, w.w13, w.s13, w.w2, w.s2, got, ws, layout=layout,
+                              f32_reduce=f32_reduce, act_limit=limit)
+        torch.cuda.synchronize()
+        from dw_tpu_b200 import _lib
+        _lib.raise_on_device_error()
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), seed
+    with pytest.raises(ValueError):
+        ops.moe_layer_fp4_out(x, lg, k, w.w13, w.s13, w.w2, w.s2, got, ws[:nbytes // 2],
+                              layout=layout, f32_reduce=f32_reduce, act_limit=limit)
