@@ -49,6 +49,15 @@ struct ScaleTraits<DWM_F32> {
 constexpr uint32_t kLutLo = 0xC0804000u;
 constexpr uint32_t kLutHi = 0x81800100u;
 
+// PTX prmt in its default mode. The selectors built below never set bit 3
+// of a nibble (the sign-replicate bit), so this is exactly __byte_perm, whose
+// documented semantics would make the compiler mask every selector first.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
 template <bool B200>
 __device__ __forceinline__ void tvals(uint32_t w, uint32_t (&t)[4]) {
   if constexpr (!B200) {
@@ -59,10 +68,10 @@ __device__ __forceinline__ void tvals(uint32_t w, uint32_t (&t)[4]) {
   } else {
     const uint32_t x = (w & 0x33333333u) | 0x40404040u;
     const uint32_t y = ((w >> 2) & 0x33333333u) | 0x40404040u;
-    t[0] = __byte_perm(kLutLo, kLutHi, x);
-    t[1] = __byte_perm(kLutLo, kLutHi, y);
-    t[2] = __byte_perm(kLutLo, kLutHi, x >> 16);
-    t[3] = __byte_perm(kLutLo, kLutHi, y >> 16);
+    t[0] = prmt(kLutLo, kLutHi, x);
+    t[1] = prmt(kLutLo, kLutHi, y);
+    t[2] = prmt(kLutLo, kLutHi, x >> 16);
+    t[3] = prmt(kLutLo, kLutHi, y >> 16);
   }
 }
 

@@ -44,7 +44,6 @@ constexpr int KSTAGE = 64;        // k per ring stage
 constexpr int CODE_BYTES = 2048;  // 4 column blocks x 4 k16 blocks x 32 words
 constexpr uint32_t kBf16x2_2p64 = 0x5F805F80u;   // bf16 2^64, both halves
 constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
-constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
 
 // Ring depth per warp (stages of 64 k) for 1 and 2 n8 token tiles.
 #ifndef DWM_GMV_STAGES1
@@ -53,7 +52,7 @@ constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
 #ifndef DWM_GMV_STAGES2
 #define DWM_GMV_STAGES2 3
 #endif
-// Warps per CTA for 8-row token tiles (E8M0 / bf16 scales).
+// Warps per CTA (E8M0 / bf16 scales; f32 scales take 12).
 #ifndef DWM_GMV_WARPS1
 #define DWM_GMV_WARPS1 16
 #endif
@@ -63,6 +62,12 @@ constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
 #ifndef DWM_GMV_RAW_TVALS
 #define DWM_GMV_RAW_TVALS 1
 #endif
+// E8M0 scales: 1 = scale the f32 partial of each k32 block after the MMA;
+// 0 = multiply each decoded weight register by 2^(c-1-4) in bf16 (exact for
+// codes 1..132; the 2^-4 is removed in the epilogue).
+#ifndef DWM_GMV_POST
+#define DWM_GMV_POST 0
+#endif
 // 1: waiting warps sleep between mbarrier polls (leaving issue slots to the
 // warps that have data).
 #ifndef DWM_GMV_BACKOFF
@@ -71,19 +76,20 @@ constexpr uint32_t kBf16x2_2p126 = 0x7E807E80u;  // bf16 2^126
 
 template <int SD, int NT>
 struct Cfg {
-  static constexpr bool POST = SD == DWM_U8;  // E8M0: scale the f32 partials
+  static constexpr bool POST = SD == DWM_U8 && DWM_GMV_POST;  // E8M0: scale f32 partials
+  static constexpr int DELTA = (SD == DWM_U8 && !POST) ? kDelta : 0;  // weight-side bias
   static constexpr int es = ScaleTraits<SD>::bytes;
   static constexpr int S = NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2;
   static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
   // Largest E8M0 code of the post-MMA path: the k-block factor 2^(c-65)
   // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
-  static constexpr uint32_t POST_MAX = RAW ? 192u : 254u;
+  static constexpr uint32_t POST_MAX = POST ? (RAW ? 192u : 254u) : 128u + kDelta;
   static constexpr int TOK = 8 * NT * KSTAGE * 2;  // token tile, 128-byte rows
   // 2 scale tiles of 2 k32 rows x 32 columns, each tile 128-byte aligned.
   static constexpr int SC_TILE = 64 * es < 128 ? 128 : 64 * es;
   static constexpr int SC = 2 * SC_TILE;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 1023) & ~1023;
-  static constexpr int WARPS = (NT == 1 && SD != DWM_F32) ? DWM_GMV_WARPS1 : 12;
+  static constexpr int WARPS = SD != DWM_F32 ? DWM_GMV_WARPS1 : 12;
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
@@ -349,7 +355,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
       // post-MMA range), else scale the f32 partial of each k32 block.
       auto stage = [&](auto pre_tag) {
         constexpr bool PRE = decltype(pre_tag)::value;
-        constexpr uint32_t M1 = C::POST ? kBf16x2_2p62 : kBf16x2_2p126;
+        constexpr uint32_t M1 = C::POST ? kBf16x2_2p62 : pow2_126_minus_delta_x2<C::DELTA>();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // 32-deep k block inside the stage
           // Scales of the lane's columns: block i, column gid (+8 for hc =
@@ -372,6 +378,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
               if constexpr (PRE) {
                 wm[i][hc] = SD == DWM_U8 ? (c << 7) * 0x10001u  // bf16 2^(c-127), 0 -> +0
                                          : c * 0x10001u;        // the bf16 scale
+              } else if constexpr (!C::POST) {
+                wm[i][hc] = ((c + 126u - C::DELTA) << 7) * 0x10001u;  // 2^(c-1-delta)
               } else {
                 post[i][hc] = C::RAW ? __uint_as_float((c + 62u) << 23)  // 2^(c-65)
                                      : __uint_as_float(c << 23);         // 2^(c-127)
@@ -411,6 +419,13 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
                 af[3] = hmul2_bf16(hmul2_bf16(af[3], M1), wm[i][1]);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_16816(acc[i][nt], af, b[nt][0], b[nt][1]);
+              } else if constexpr (!C::POST) {  // one exact multiply per register
+                af[0] = hmul2_bf16(af[0], wm[i][0]);
+                af[1] = hmul2_bf16(af[1], wm[i][1]);
+                af[2] = hmul2_bf16(af[2], wm[i][0]);
+                af[3] = hmul2_bf16(af[3], wm[i][1]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma_16816(acc[i][nt], af, b[nt][0], b[nt][1]);
               } else {
                 if constexpr (!C::RAW) {
 #pragma unroll
@@ -426,7 +441,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
               }
             }
           }
-          if constexpr (!PRE) {
+          if constexpr (!PRE && C::POST) {
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -437,15 +452,18 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
           }
         }
       };
-      if constexpr (C::POST) {
+      if constexpr (SD == DWM_U8) {
         // One check per stage for the whole warp: lane l tests 4 of the 128
-        // scale bytes; the post-MMA path needs every code in [1, POST_MAX].
+        // scale bytes; the fast path needs every code in [1, POST_MAX].
         const uint32_t v =
             *reinterpret_cast<const uint32_t*>(sc + (lane >> 4) * C::SC_TILE + (lane & 15) * 4);
         const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
         uint32_t high_byte;
         if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
           high_byte = ((v & 0x7F7F7F7Fu) + 0x3F3F3F3Fu) & v & 0x80808080u;
+        else if constexpr (C::POST_MAX == 128u + kDelta)  // a byte >= 133: low 7 bits >= 5
+          high_byte = ((v & 0x7F7F7F7Fu) + (0x80808080u - (1u + kDelta) * 0x01010101u)) & v &
+                      0x80808080u;
         else  // a byte == 255
           high_byte = (~v - 0x01010101u) & v & 0x80808080u;
         if (__any_sync(0xffffffffu, (zero_byte | high_byte) != 0u))
@@ -461,7 +479,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
     }
     if (!ok) break;
 
-    // Epilogue: c0,c1 = (column gid, tokens 2t, 2t+1), c2,c3 = (column gid+8, ...).
+    // Epilogue: c0,c1 = (column gid, tokens 2t, 2t+1), c2,c3 = (column gid+8, ...);
+    // kAccScale removes the weight-side 2^-delta exactly.
+    constexpr float kAccScale = (float)(1 << C::DELTA);
     const int colbase[4] = {16 * cb0, 16 * cb0 + 16, 16 * cb1, 16 * cb1 + 16};
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -475,7 +495,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
           for (int i = 0; i < 4; ++i) {
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
-              const float v = acc[i][nt][hc * 2 + e];
+              const float v = acc[i][nt][hc * 2 + e] * kAccScale;
               const int64_t off = row * a.ldo + colbase[i] + gid + 8 * hc;
               if (a.out_f32)
                 reinterpret_cast<float*>(a.out)[off] = v;
@@ -488,8 +508,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
           for (int i = 0; i < 2; ++i) {
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
-              float g = acc[i][nt][hc * 2 + e];
-              float u = acc[i + 2][nt][hc * 2 + e];
+              float g = acc[i][nt][hc * 2 + e] * kAccScale;
+              float u = acc[i + 2][nt][hc * 2 + e] * kAccScale;
               if (a.act == DWM_ACT_SWIGLU_CLAMP) {
                 g = fminf(g, a.limit);
                 u = fminf(fmaxf(u, -a.limit), a.limit);
