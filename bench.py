@@ -330,7 +330,8 @@ def run_ours(args, rank, world, local_rank):
     achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
     peaks = measured_peaks()
     peak = peaks["hbm_gbs"] if peaks else 6650.0
-    traffic = read_traffic()
+    # The committed ncu traffic figure is for the single-GPU cfg1 launch.
+    traffic = read_traffic() if world == 1 else None
     res = {
         "ms": ms, "e2e_ms": e2e_ms, "active": active,
         "roofline": {
