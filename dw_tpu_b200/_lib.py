@@ -39,6 +39,7 @@ LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200}
 SCORE_SOFTMAX = 0
 SCORE_SIGMOID = 1
 SCORE_SQRTSOFTPLUS = 2
+LAYER_SCRATCH_BYTES = 33554432  # DWM_LAYER_SCRATCH_BYTES
 EP_HANDLE_BYTES = 64
 EP_COUNTS = 1
 EP_ROWS = 2
@@ -76,6 +77,8 @@ SIGNATURES = {
     "dwm_moe_layer_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
     "dwm_moe_layer_fp4": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I,
                            _F, _I, _P, _SZ, _P, _P], _I),
+    "dwm_moe_layer_fp4_noalloc": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I,
+                                   _I, _I, _F, _I, _P, _P], _I),
     "dwm_ep_create": ([_I, _I, _I, _I, _I, _I, _c.POINTER(_P)], _I),
     "dwm_ep_ipc_handle": ([_P, _P], _I),
     "dwm_ep_connect": ([_P, _P], _I),

@@ -4,6 +4,8 @@
 // entry point the caller could make itself, so results are bit-identical to
 // that sequence; the call only saves the host round trips (one call instead of
 // six) and the intermediate bookkeeping.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dwm {
@@ -88,4 +90,64 @@ extern "C" int dwm_moe_layer_fp4(const void* hidden, const void* logits, int log
   if (rc) return rc;
   return dwm_combine(y, y_f32 ? DWM_F32 : DWM_BF16, rows, revert, w16, DWM_BF16, num_tokens,
                      hidden_size, topk, out, DWM_BF16, stream);
+}
+
+// ---------------------------------------------------------------------------
+// The same layer for callers that cannot allocate device memory: the
+// intermediates live in one file-scope device array of fixed size
+// (DWM_LAYER_SCRATCH_BYTES) instead of a caller workspace.
+// ---------------------------------------------------------------------------
+
+namespace dwm {
+namespace layer {
+
+__device__ __align__(256) uint8_t g_scratch[DWM_LAYER_SCRATCH_BYTES];
+
+// Address of g_scratch on the current device, resolved once per device (with
+// that device current) and cached.
+int scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return set_error(DWM_ERR_UNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_scratch), "cudaGetSymbolAddress(layer scratch)");
+    if (rc) return rc;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return DWM_OK;
+}
+
+}  // namespace layer
+}  // namespace dwm
+
+extern "C" int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits,
+                                         int logits_dtype, int num_tokens, int hidden_size,
+                                         int num_experts, int topk, int scoring, int renormalize,
+                                         const void* w13, const void* s13, const void* w2,
+                                         const void* s2, int codes_format, int scale_dtype,
+                                         int inter, int act, float act_limit, int y_f32,
+                                         void* out, void* stream) {
+  DWM_CHECK_ARG(num_tokens >= 0 && hidden_size > 0 && inter > 0 && topk >= 1 &&
+                    num_experts >= 1,
+                "bad shape t=%d h=%d i=%d topk=%d e=%d", num_tokens, hidden_size, inter, topk,
+                num_experts);
+  const size_t need =
+      layer::plan(num_tokens, hidden_size, inter, topk, num_experts, y_f32).total;
+  DWM_CHECK_ARG(need <= (size_t)DWM_LAYER_SCRATCH_BYTES,
+                "the layer needs %zu bytes of scratch, more than the %d bytes built in "
+                "(DWM_LAYER_SCRATCH_BYTES)",
+                need, DWM_LAYER_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = layer::scratch_address(&scratch);  // a num_tokens = 0 call does only this setup
+  if (rc) return rc;
+  return dwm_moe_layer_fp4(hidden, logits, logits_dtype, num_tokens, hidden_size, num_experts,
+                           topk, scoring, renormalize, w13, s13, w2, s2, codes_format,
+                           scale_dtype, inter, act, act_limit, y_f32, scratch,
+                           (size_t)DWM_LAYER_SCRATCH_BYTES, out, stream);
 }

@@ -254,6 +254,33 @@ def moe_layer_fp4_out(hidden, logits, top_k, w13, s13, w2, s2, out, workspace, *
     return out
 
 
+def moe_layer_fp4_noalloc_out(hidden, logits, top_k, w13, s13, w2, s2, out, *, layout="e2m1",
+                              scoring_fn="sigmoid", renormalize=True, act_limit=None,
+                              f32_reduce=False, stream=None):
+    """``moe_layer_fp4_out`` without a workspace (dwm_moe_layer_fp4_noalloc):
+    the intermediates live in the library's fixed device scratch
+    (DWM_LAYER_SCRATCH_BYTES per device); larger inputs raise ValueError.
+    Overlapping calls on one device race on that scratch."""
+    L.require_cuda(hidden, logits, w13, s13, w2, s2, out)
+    if hidden.dtype != torch.bfloat16 or hidden.dim() != 2 or not hidden.is_contiguous():
+        raise ValueError("hidden must be a contiguous bf16 [t, h] tensor")
+    t, h = hidden.shape
+    if logits.dim() != 2 or logits.shape[0] != t or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous [t, e] tensor")
+    if scoring_fn not in _SCORING:
+        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
+    act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
+    rc = L.lib().dwm_moe_layer_fp4_noalloc(
+        hidden.data_ptr(), logits.data_ptr(), L.dtype_code(logits.dtype), t, h, logits.shape[1],
+        int(top_k), _SCORING[scoring_fn], int(bool(renormalize)), _u8view(w13).data_ptr(),
+        s13.data_ptr(), _u8view(w2).data_ptr(), s2.data_ptr(), L.LAYOUTS[layout],
+        L.dtype_code(s13.dtype), s2.shape[1] * 32, act,
+        0.0 if act_limit is None else float(act_limit), int(bool(f32_reduce)), out.data_ptr(),
+        L.stream_ptr() if stream is None else stream)
+    L.check(rc, "moe_layer_fp4_noalloc")
+    return out
+
+
 def e8m0_encode_out(scale, codes, lossless, stream=None):
     L.require_cuda(scale, codes, lossless)
     if scale.dtype != torch.float32:

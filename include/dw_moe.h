@@ -195,6 +195,24 @@ int dwm_moe_layer_fp4(const void* hidden, const void* logits, int logits_dtype, 
                       int y_f32, void* workspace, size_t workspace_bytes, void* out,
                       void* stream);
 
+/* dwm_moe_layer_fp4 for callers that cannot allocate device memory: no
+ * workspace argument; the intermediates live in one file-scope device array
+ * of DWM_LAYER_SCRATCH_BYTES (32 MiB: e.g. 128 tokens x top-8 at hidden 4096,
+ * intermediate 2048 with f32 gmm2 output), one per device, whose address is
+ * resolved once per device. Inputs needing more scratch are rejected
+ * (DWM_ERR_INVALID). Nothing in the scratch needs to start at zero. Calls that
+ * overlap on one device (other streams or host threads) race on that one
+ * array. The first call on a device (a num_tokens = 0 call does only that
+ * setup) must come before any stream capture. No counterpart in the
+ * reference. */
+#define DWM_LAYER_SCRATCH_BYTES 33554432
+int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits_dtype,
+                              int num_tokens, int hidden_size, int num_experts, int topk,
+                              int scoring, int renormalize, const void* w13, const void* s13,
+                              const void* w2, const void* s2, int codes_format, int scale_dtype,
+                              int inter, int act, float act_limit, int y_f32, void* out,
+                              void* stream);
+
 /* ---- expert-parallel exchange over NVLink peer memory ---------------------
  * Replaces the GMM_EP exchange: all_gather_local + the per-shard stable sort
  * (KO:152-164, X0101:56-104, X0107:34-51) on the way in, and the masked f32

@@ -97,6 +97,13 @@ def test_other_entry_points_validate(lib):
     assert lib.dwm_ep_combine(None, fake, 0, fake, 0, fake, 0, 3, None) == -1
     assert lib.dwm_ep_ipc_handle(None, None) == -1
     assert lib.dwm_ep_destroy(None) == 0
+    # the no-alloc layer rejects inputs larger than its built-in scratch on the host
+    assert lib.dwm_moe_layer_fp4_noalloc(fake, fake, 0, 1024, 4096, 16, 8, 1, 1, fake, fake, fake,
+                                         fake, 2, 2, 2048, 1, 0.0, 0, fake, None) == -1
+    from dw_tpu_b200 import _lib
+    assert "scratch" in _lib.last_error()
+    assert lib.dwm_moe_layer_fp4(fake, fake, 0, 8, 512, 16, 4, 1, 1, fake, fake, fake, fake, 2, 2,
+                                 256, 1, 0.0, 0, fake, 16, fake, None) == -1  # workspace too small
 
 
 def test_python_shims_raise_value_error_without_gpu():
