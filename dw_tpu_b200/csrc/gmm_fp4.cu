@@ -47,7 +47,6 @@ enum Variant { kMN = 0, kKS = 1 };
 constexpr int NSUB = 2;    // sub-tiles (accumulators) per tile
 constexpr int BW = 128;    // weight columns per sub-tile (UMMA M)
 constexpr int BK = 64;     // K per pipeline stage (128 bytes of bf16)
-constexpr int BT = 128;    // max token rows per tile (UMMA N)
 constexpr int NUM_THREADS = 768;
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
@@ -55,13 +54,12 @@ constexpr int TOKEN_WARP = 6;
 constexpr int DEC_WARP0 = 8;
 constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
 constexpr int MAX_GROUPS = 1024;
-constexpr int TMEM_COLS = 512;    // 2 buffers x NSUB x BT f32 columns
+constexpr int TMEM_COLS = 512;    // NBUF buffers x NSUB x BT f32 columns
 
 constexpr int A_SUB_BYTES = BW * BK * 2;     // 16 KiB bf16 sub-tile
 constexpr int A_STAGE = NSUB * A_SUB_BYTES;  // 32 KiB
 constexpr int A_LBO_MN = 8192;               // MN-major: MN-atom (64 columns) stride
 constexpr int A_SBO_MN = 1024;               // MN-major: K-atom (8 rows) stride
-constexpr int T_STAGE = 16384;               // token stage: 8 boxes of 16 rows x 64 k
 constexpr int T_BOX_ROWS = 16;
 constexpr int T_BOX_BYTES = T_BOX_ROWS * BK * 2;  // 2 KiB
 constexpr int C_SUB_BYTES = BK * (BW / 2);        // 4 KiB of packed nibbles per sub-tile
@@ -78,11 +76,15 @@ static_assert(C_SUB_BYTES % 128 == 0, "TMA needs 128 B alignment");
 #ifndef DWM_GMM_CS
 #define DWM_GMM_CS 8
 #endif
-constexpr int TS = DWM_GMM_TS;
-constexpr int AS = DWM_GMM_AS;
-
-template <int SD>
+// BT = token rows per tile (the UMMA N): 128 (two TMEM accumulator buffers,
+// the epilogue overlaps the next tile) or 256 (one buffer; every weight
+// column is decoded once per 256 rows and each UMMA does twice the work).
+template <int SD, int BT>
 struct Smem {
+  static constexpr int TS = BT == 128 ? DWM_GMM_TS : 2;
+  static constexpr int AS = BT == 128 ? DWM_GMM_AS : 2;
+  static constexpr int T_STAGE = BT * BK * 2;  // BT/16 boxes of 16 rows x 64 k
+  static constexpr int NBUF = TMEM_COLS / (NSUB * BT);
   static constexpr int CS = ScaleTraits<SD>::bytes == 4 ? (DWM_GMM_CS * 3) / 4 : DWM_GMM_CS;
   static constexpr int S_STAGE = NSUB * 2 * BW * ScaleTraits<SD>::bytes;
   static constexpr int OFF_A = 0;
@@ -124,6 +126,7 @@ struct Tile {
   int n_idx;  // column tile
 };
 
+template <int BT>
 __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
                                          const Args& a) {
   int lo = 0, hi = a.n_local;  // tile_prefix[lo] <= idx < tile_prefix[hi]
@@ -144,19 +147,24 @@ __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const in
 }
 
 // Token-stage geometry: a tile needs nb 16-row boxes per k-step; rounded up
-// to a power of two (nbp) a stage of 8 boxes covers 8 / nbp k-steps.
+// to a power of two (nbp) a stage of BT/16 boxes covers (BT/16) / nbp k-steps.
+template <int BT>
 __device__ __forceinline__ int token_span(int nb, int& nbp) {
-  nbp = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;
-  return 8 / nbp;
+  nbp = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16;
+  return (BT / T_BOX_ROWS) / nbp;
 }
 
-template <int SD, int VAR>
+template <int SD, int VAR, int BT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
-  using L = Smem<SD>;
+  using L = Smem<SD, BT>;
   constexpr int CS = L::CS;
+  constexpr int TS = L::TS;
+  constexpr int AS = L::AS;
+  constexpr int T_STAGE = L::T_STAGE;
+  constexpr int NBUF = L::NBUF;
   extern __shared__ uint8_t smem_raw[];
   // 1 KiB alignment by pointer arithmetic on the shared array itself, so the
   // compiler keeps every access below in the shared window (LDS/STS, not LD/ST).
@@ -297,9 +305,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
     int it = 0;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++it) {
-      const Tile t = get_tile(idx, row_start, tile_prefix, a);
-      const int buf = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
+      const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
+      const int buf = it % NBUF;
+      const uint32_t ph = (it / NBUF) & 1;
       const bool got = mbar_wait<true>(&acc_full[buf], ph, abort_flag, a.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
@@ -360,7 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int half = a.n / 2;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
         int col[NSUB];
         if (a.act == DWM_ACT_NONE) {
           col[0] = t.n_idx * (NSUB * BW);
@@ -404,10 +412,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t ts_ph = 0, ts_armed = 0, ts_par = 0;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
         const int nb = (t.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
         int nbp;
-        const int kspan = token_span(nb, nbp);
+        const int kspan = token_span<BT>(nb, nbp);
         for (int k0 = 0; k0 < KT; k0 += kspan) {
           const int kn = min(kspan, KT - k0);
           if (!mbar_wait(&tk_empty[ts], ts_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
@@ -433,14 +441,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
-        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
         const int nmma = (t.rows + 15) & ~15;
         const int nb = nmma / T_BOX_ROWS;
         int nbp;
-        const int kspan = token_span(nb, nbp);
+        const int kspan = token_span<BT>(nb, nbp);
         const uint32_t idesc = idesc_bf16(128, nmma, /*a_mn=*/VAR == kMN, /*b_mn=*/false);
-        const int buf = it & 1;
-        const uint32_t ph = (it >> 1) & 1;
+        const int buf = it % NBUF;
+        const uint32_t ph = (it / NBUF) & 1;
         if (!mbar_wait(&acc_empty[buf], ph ^ 1, abort_flag, a.status)) break;
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * NSUB * BT);
@@ -797,11 +805,11 @@ __global__ void fp4_codes_convert_kernel(const uint8_t* __restrict__ in, uint8_t
 // Host launch
 // ---------------------------------------------------------------------------
 
-template <int SD, int VAR>
+template <int SD, int VAR, int BT>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
-  using L = Smem<SD>;
+  using L = Smem<SD, BT>;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
                           (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
@@ -825,7 +833,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmm_fp4_kernel<SD, VAR>,
+    rc = check_cuda(cudaFuncSetAttribute(gmm_fp4_kernel<SD, VAR, BT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC),
                     "gmm smem attribute");
     if (rc) return rc;
@@ -847,8 +855,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.n_tiles = n / (NSUB * BW);
   a.status = status_ptr();
-  gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
-                                                                       tm_scales, a);
+  gmm_fp4_kernel<SD, VAR, BT><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
+                                                                           tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmm_fp4 launch");
 }
 
@@ -889,11 +897,13 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
   return DWM_OK;
 }
 
-// variant: 0 = choose, 1 = tcgen05 (shared-memory decode), 2 = mma.sync
-// decode kernel (B200 layout only) with 8- or 16-row token tiles by the
-// average rows per local group, 3 / 4 = the same with 8 / 16-row tiles. The
-// automatic choice sends the B200 layout to mma.sync when the local groups
-// average at most 16 rows.
+// variant: 0 = choose, 1 = tcgen05 (shared-memory decode) with 128-row
+// tiles, 5 = the same with 256-row tiles, 2 = mma.sync decode kernel (B200
+// layout only) with 8- or 16-row token tiles by the average rows per local
+// group, 3 / 4 = the same with 8 / 16-row tiles. The automatic choice sends
+// the B200 layout to mma.sync when the local groups average at most 16 rows,
+// else 128-row tiles (256-row tiles measured slower at 256 rows per group:
+// one TMEM buffer, shallower rings and fewer tiles to balance).
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
                int group_offset, int num_local_groups, int act, float act_limit, int out_dtype,
@@ -907,23 +917,27 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     return DWM_OK;
   }
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
-  if (variant == 0 && codes_format == DWM_FP4_B200) variant = avg <= 16 ? 2 : 1;
-  if (variant >= 2)
+  if (variant == 0) variant = codes_format == DWM_FP4_B200 && avg <= 16 ? 2 : 1;
+  if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
                       variant == 3 ? 1 : variant == 4 ? 2 : (avg <= 8 ? 1 : 2), s);
-#define DWM_GMM_LAUNCH(SD, VAR)                                                          \
-  return launch<SD, VAR>(lhs, codes, scales, group_sizes, num_groups, m, k, n,          \
-                         group_offset, num_local_groups, act, act_limit, out_dtype,      \
-                         zero_init, out, s)
-#define DWM_GMM_BY_SCALE(VAR)                                   \
-  do {                                                          \
-    if (scale_dtype == DWM_U8) DWM_GMM_LAUNCH(DWM_U8, VAR);     \
-    if (scale_dtype == DWM_BF16) DWM_GMM_LAUNCH(DWM_BF16, VAR); \
-    DWM_GMM_LAUNCH(DWM_F32, VAR);                               \
+#define DWM_GMM_LAUNCH(SD, VAR, BT)                                                       \
+  return launch<SD, VAR, BT>(lhs, codes, scales, group_sizes, num_groups, m, k, n,      \
+                             group_offset, num_local_groups, act, act_limit, out_dtype,  \
+                             zero_init, out, s)
+#define DWM_GMM_BY_SCALE(VAR, BT)                                   \
+  do {                                                              \
+    if (scale_dtype == DWM_U8) DWM_GMM_LAUNCH(DWM_U8, VAR, BT);     \
+    if (scale_dtype == DWM_BF16) DWM_GMM_LAUNCH(DWM_BF16, VAR, BT); \
+    DWM_GMM_LAUNCH(DWM_F32, VAR, BT);                               \
   } while (0)
-  if (codes_format == DWM_FP4_B200) DWM_GMM_BY_SCALE(kKS);
-  DWM_GMM_BY_SCALE(kMN);
+  if (codes_format == DWM_FP4_B200) {
+    if (variant == 5) DWM_GMM_BY_SCALE(kKS, 256);
+    DWM_GMM_BY_SCALE(kKS, 128);
+  }
+  if (variant == 5) DWM_GMM_BY_SCALE(kMN, 256);
+  DWM_GMM_BY_SCALE(kMN, 128);
 #undef DWM_GMM_BY_SCALE
 #undef DWM_GMM_LAUNCH
 }
@@ -952,8 +966,9 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 4,
-                "variant must be 0 (auto), 1 (tcgen05) or 2-4 (mma.sync decode kernel)");
+  DWM_CHECK_ARG(variant >= 0 && variant <= 5,
+                "variant must be 0 (auto), 1 / 5 (tcgen05, 128 / 256-row tiles) or 2-4 "
+                "(mma.sync decode kernel)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
                 "explicit variants need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,

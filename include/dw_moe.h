@@ -96,12 +96,14 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
                 int n, int group_offset, int num_local_groups, int act, float act_limit,
                 int out_dtype, int zero_init, void* out, void* stream);
 
-/* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4:
- * B200 codes whose local groups average <= 16 rows take 2, others 1),
- * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles),
+/* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4),
+ * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
+ * automatic choice above 16 rows), 5 = the same with 256-row tiles (one TMEM
+ * accumulator buffer),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8- or 16-row token tiles by the average rows per local group),
- * 3 / 4 = the same with 8 / 16-row token tiles. 1-4 need DWM_FP4_B200
+ * 3 / 4 = the same with 8 / 16-row token tiles (2-4: the automatic choice
+ * for B200 codes whose groups average at most 16 rows). 1-5 need DWM_FP4_B200
  * codes. Every variant decodes the same bf16 weights and accumulates in f32; results
  * differ between variants only by f32 summation order. Same reference
  * interface as dwm_gmm_fp4 (TK:107-153). */

@@ -195,13 +195,13 @@ def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
         r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
                          out_dtype="f32" if dt == torch.float32 else "bf16")
         r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in (0, 1, 2):
+        for variant in (0, 1, 2, 5):
             got = ops.gmm_fp4_out(x, b200, sc, g,
                                   torch.empty((400, n_out), dtype=dt, device="cuda"), act=act,
                                   zero_init=True, layout="b200", variant=variant)
             torch.cuda.synchronize()
             L.raise_on_device_error()
-            if variant in (0, 1):  # 100 rows per group on average: tcgen05
+            if variant in (0, 1):  # 100 rows per group on average: tcgen05, 128-row tiles
                 assert torch.equal(ref.view(torch.int16), got.view(torch.int16)), (act, variant)
             else:
                 assert_gemm_close(to_np(got), O.round_bf16(r), r32, 128, rows=v)
@@ -270,6 +270,33 @@ def test_gmm_decode_regime_group_offset(dw):
     got = bf16_to_np(out)
     assert_gemm_close(got, r, r32, 128, rows=v)
     assert np.all(got[~v] == 3.0)
+
+
+@pytest.mark.parametrize("layout", ["b200", "e2m1"])
+def test_gmm_prefill_tiles(dw, layout):
+    """Groups of 129-300 rows: 128- and 256-row tcgen05 tiles, partial tiles,
+    SwiGLU, against the oracle."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    gs = [300, 0, 200, 170, 129]
+    m = sum(gs) + 7
+    lhs, packed, scales, gs = _case(13, m, 256, 512, 5, gs=gs, lo=118, hi=121)
+    raw = torch.from_numpy(packed).cuda()
+    codes = dw.fp4_weight_to_codes(raw) if layout == "b200" else raw
+    sc = torch.from_numpy(scales).cuda()
+    g = torch.from_numpy(gs).cuda()
+    for act, kind, n_out in ((L.ACT_NONE, None, 512), (L.ACT_SWIGLU, "swiglu", 256)):
+        r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind)
+        r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
+        for variant in ((0, 1, 5) if layout == "b200" else (0,)):
+            out = torch.full((m, n_out), 5.0, dtype=torch.bfloat16, device="cuda")
+            ops.gmm_fp4_out(np_to_bf16(lhs), codes, sc, g, out, act=act, zero_init=True,
+                            layout=layout, variant=variant)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            got = bf16_to_np(out)
+            assert_gemm_close(got, r, r32, 256, rows=v)
+            assert np.all(got[~v] == 0), variant
 
 
 def test_gmm_deterministic(dw):
