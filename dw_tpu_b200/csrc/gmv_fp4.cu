@@ -9,27 +9,28 @@
 // word per lane per 16x16 block, one PRMT per bf16 pair), token rows are the
 // n8 tiles, and nothing decoded touches shared or tensor memory.
 //
-// The kernel is bound by instruction issue, not by the MMA: at the HBM
+// The kernel is bound by the integer (ALU) pipe, not by the MMA: at the HBM
 // roofline an SM must retire one 32-bit code word (8 weights) per lane every
-// ~23 issue slots. So the per-word work is kept to the load, the 4-PRMT
-// decode and the MMA:
-//   * E8M0 scales (the common case) are applied after the MMA, to the f32
-//     partial of each 32-deep k block (partial * 2^(c-127)), instead of to
-//     every decoded weight. The decode yields value * 2^-126 (fp4_decode.cuh);
-//     token fragments are pre-scaled by 2^64 and the k-block factor is
-//     2^(c-65), all exact powers of two, so the result equals the reference's
-//     bf16(value * scale) x bf16 token products (E0901:84-95) up to the f32
-//     summation order. Codes 1..192 take this path; a stage holding code 0
-//     (scale +0) or a code above 192 (scales >= 2^66, including the 255 = inf
-//     code) multiplies the weights in bf16 instead, exactly like the
-//     reference. The check is one SWAR test per lane per stage.
+// ~23 issue slots, and the decode alone is 9 ALU operations (2 LOP3, 3 SHF,
+// 4 PRMT). So everything else per word is kept off the ALU:
+//   * E8M0 scales (the common case) go into the weights with one bf16
+//     multiply per fragment register on the FMA pipe: the decode yields
+//     value * 2^-126 (fp4_decode.cuh) and the multiplier is 2^(c-1-4), so
+//     the product value * scale * 2^-4 is exact, and the epilogue removes
+//     the 2^-4 in f32: the reference's bf16(value * scale) x bf16 token
+//     products (E0901:84-95) up to the f32 summation order. A stage holding
+//     code 0 (scale +0) or a code above 132 multiplies in two exact steps
+//     instead (one SWAR test per lane per stage decides). Built with
+//     DWM_GMV_POST=1 the scale is instead applied to the f32 partial of each
+//     32-deep k block after the MMA (tokens pre-scaled by 2^64, factor
+//     2^(c-65)); it measured the same speed.
 //   * bf16 / f32 scales (reference: cast to bf16, one bf16 multiply) are
 //     multiplied into the decoded weights, which reproduces that rounding.
 //   * each warp streams its own tasks through a private ring of S stages,
 //     filled by five 2-D TMA copies per stage (tokens, two code tiles, two
 //     scale tiles) issued by lane 0, with prefetch running ahead across task
-//     boundaries; token tiles land 128-byte swizzled so B-fragment loads are
-//     bank-conflict free.
+//     boundaries; token rows land 144 bytes apart (a 72-k box for 64 k of
+//     data) so B-fragment loads are bank-conflict free with plain offsets.
 #include <type_traits>
 
 #include "fp4_decode.cuh"
@@ -42,6 +43,10 @@ using namespace fp4;
 constexpr int MAX_GROUPS = 1024;
 constexpr int KSTAGE = 64;        // k per ring stage
 constexpr int CODE_BYTES = 2048;  // 4 column blocks x 4 k16 blocks x 32 words
+// A token row in shared memory: 72 k of bf16, of which the stage uses 64.
+// Rows 144 bytes (36 words) apart put the 8 rows of a B-fragment load in 8
+// different bank quads.
+constexpr int TOK_ROW = 144;
 constexpr uint32_t kBf16x2_2p64 = 0x5F805F80u;   // bf16 2^64, both halves
 constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 
@@ -84,20 +89,21 @@ struct Cfg {
   // Largest E8M0 code of the post-MMA path: the k-block factor 2^(c-65)
   // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
   static constexpr uint32_t POST_MAX = POST ? (RAW ? 192u : 254u) : 128u + kDelta;
-  static constexpr int TOK = 8 * NT * KSTAGE * 2;  // token tile, 128-byte rows
+  static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of 72 k (64 used)
   // 2 scale tiles of 2 k32 rows x 32 columns, each tile 128-byte aligned.
   static constexpr int SC_TILE = 64 * es < 128 ? 128 : 64 * es;
   static constexpr int SC = 2 * SC_TILE;
-  static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 1023) & ~1023;
+  static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
   static constexpr int WARPS = SD != DWM_F32 ? DWM_GMV_WARPS1 : 12;
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int BYTES = OFF_TASKS + (MAX_GROUPS + 1) * 4;
-  static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment (128-byte swizzle)
+  static constexpr int ALLOC = BYTES + 128;  // slack for 128-byte alignment (TMA destinations)
   static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * 64 * es;
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
-  static_assert(TOK % 1024 == 0 && (S * TOK) % 1024 == 0, "token tiles need 1 KiB alignment");
+  static_assert(TOK % 128 == 0 && CODE_BYTES % 128 == 0 && SC % 128 == 0,
+                "TMA destinations need 128-byte alignment");
 };
 
 struct Args {
@@ -181,7 +187,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
   extern __shared__ uint8_t smem_raw[];
   // 1 KiB alignment by pointer arithmetic on the shared array itself, so the
   // compiler keeps every access below in the shared window (LDS, not LD).
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   int* row_start = reinterpret_cast<int*>(smem + C::OFF_ROWS);
   int* task_prefix = reinterpret_cast<int*>(smem + C::OFF_TASKS);
   const int warp = threadIdx.x >> 5;
@@ -394,11 +400,10 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
             uint32_t b[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              // token row nt*8 + gid; the 128-byte swizzle XORs the chunk with gid
-              const uint8_t* row = tok + (nt * 8 + gid) * 128 + 4 * tig;
-              uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + (((2 * kk) ^ gid) << 4));
-              uint32_t b1 =
-                  *reinterpret_cast<const uint32_t*>(row + (((2 * kk + 1) ^ gid) << 4));
+              // token row nt*8 + gid: k pairs 16 kk + 2 tig and + 8
+              const uint8_t* row = tok + (nt * 8 + gid) * TOK_ROW + kk * 32 + 4 * tig;
+              uint32_t b0 = *reinterpret_cast<const uint32_t*>(row);
+              uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + 16);
               if constexpr (C::POST) {
                 b0 = hmul2_bf16(b0, kBf16x2_2p64);
                 b1 = hmul2_bf16(b1, kBf16x2_2p64);
@@ -538,10 +543,10 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
                 cudaStream_t stream) {
   using C = Cfg<SD, NT>;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
-  // lhs [m, k] bf16: box of 64 k x 8*NT rows, 128-byte swizzle.
+  // lhs [m, k] bf16: box of 72 k (64 used) x 8*NT rows, rows 144 bytes apart.
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)a.k,
-                          (uint64_t)a.m, (uint64_t)a.k * 2, KSTAGE, 8 * NT,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+                          (uint64_t)a.m, (uint64_t)a.k * 2, TOK_ROW / 2, 8 * NT,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   // codes: rows = column blocks [n_local * n/16], each (k/16) x 32 words;
   // box of 4 k16 blocks (128 words) x 2 column blocks.
