@@ -25,12 +25,12 @@ from .gmm_v2 import (b200_to_e2m1, codes_to_e2m1, decode_codes, e2m1_to_codes,  
 from .moe_fast_combine import combine_pallas, combine_xla, fast_combine  # noqa: E402
 from .moe_fast_dispatch import (dispatch_gather, dispatch_gather_pallas,  # noqa: E402
                                 fast_dispatch_gather, moe_permute, sorted_token_indices)
-from .routing import route_topk  # noqa: E402
+from .routing import dedupe_topk, route_hash, route_topk  # noqa: E402
 
 __all__ = [
     "gmm_v2", "gmm", "gmm_wrapper", "e2m1_to_codes", "codes_to_e2m1", "decode_codes",
     "fp4_weight_to_codes", "b200_to_e2m1", "needs_fp4_emulation", "fast_dispatch_gather",
     "sorted_token_indices", "moe_permute", "dispatch_gather", "dispatch_gather_pallas",
     "fast_combine", "combine_xla", "combine_pallas", "e8m0_encode", "e8m0_decode",
-    "route_topk", "MoELayer", "FP4MoEWeights", "fused_moe_func",
+    "route_topk", "route_hash", "dedupe_topk", "MoELayer", "FP4MoEWeights", "fused_moe_func",
 ]

@@ -67,9 +67,12 @@ SIGNATURES = {
     "dwm_gmm_fp4_variant": ([_P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P,
                              _I, _P], _I),
     "dwm_fp4_codes_convert": ([_P, _P, _SZ, _I, _I, _P], _I),
+    "dwm_fp4_quantize": ([_P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P], _I),
     "dwm_e8m0_encode": ([_P, _SZ, _P, _P, _P], _I),
     "dwm_e8m0_decode": ([_P, _SZ, _P, _P], _I),
     "dwm_route_topk": ([_P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P], _I),
+    "dwm_route_hash": ([_P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P], _I),
+    "dwm_dedupe_topk": ([_P, _P, _I, _I, _I, _P, _P], _I),
     "dwm_sorted_token_indices": ([_P, _I64, _I, _P, _P], _I),
     "dwm_permute": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "dwm_dispatch_gather": ([_P, _I, _I, _P, _I64, _P, _P], _I),

@@ -18,11 +18,14 @@ __device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
   return a > b || (a == b && ia < ib);
 }
 
+// hash_ids (optional, [t, top_k]): precomputed expert ids (hash routing,
+// E0901:667-671); the weights are the scores at those ids.
 template <int LD>
 __global__ void route_topk_kernel(const void* __restrict__ logits, int t, int e, int top_k,
                                   int scoring, int renormalize, const float* __restrict__ bias,
-                                  int num_valid, int32_t* __restrict__ ids, float* __restrict__ w32,
-                                  uint16_t* __restrict__ w16) {
+                                  int num_valid, const int32_t* __restrict__ hash_ids,
+                                  int32_t* __restrict__ ids, float* __restrict__ w32,
+                                  uint16_t* __restrict__ w16, int* status) {
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* score = sm + warp * 2 * e;
@@ -67,7 +70,18 @@ __global__ void route_topk_kernel(const void* __restrict__ logits, int t, int e,
   const bool valid = num_valid < 0 || tok < num_valid;
   float wk_mine = 0.0f;  // lane k keeps the k-th weight
   int id_mine = 0;
-  for (int k = 0; k < top_k; ++k) {
+  if (hash_ids) {
+    if (lane < top_k) {
+      int id = hash_ids[(int64_t)tok * top_k + lane];
+      if (id < 0 || id >= e) {
+        report(status, DWM_DEV_BAD_INDEX);
+        id = 0;
+      }
+      id_mine = id;
+      wk_mine = score[id];
+    }
+  }
+  for (int k = 0; k < (hash_ids ? 0 : top_k); ++k) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int x = lane; x < e; x += 32) {
@@ -138,10 +152,13 @@ inline unsigned grid_for(size_t work, int threads) {
 
 using namespace dwm;
 
-extern "C" int dwm_route_topk(const void* logits, int logits_dtype, int t, int e, int top_k,
-                              int scoring, int renormalize, const float* bias,
-                              int num_valid_tokens, int32_t* topk_ids, float* topk_weights_f32,
-                              void* topk_weights_bf16, void* stream) {
+namespace dwm {
+namespace route {
+
+static int route_impl(const void* logits, int logits_dtype, int t, int e, int top_k, int scoring,
+                      int renormalize, const float* bias, const int32_t* hash_ids,
+                      int num_valid_tokens, int32_t* topk_ids, float* topk_weights_f32,
+                      void* topk_weights_bf16, void* stream) {
   DWM_CHECK_ARG(logits_dtype == DWM_BF16 || logits_dtype == DWM_F32,
                 "logits dtype must be bf16 or f32");
   DWM_CHECK_ARG(t >= 0 && e >= 1 && e <= 4096, "bad shape t=%d e=%d", t, e);
@@ -153,26 +170,95 @@ extern "C" int dwm_route_topk(const void* logits, int logits_dtype, int t, int e
   DWM_CHECK_ARG(t == 0 || (logits && topk_ids), "NULL pointer");
   if (t == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)route::WARPS * 2 * e * sizeof(float);
+  const size_t smem = (size_t)WARPS * 2 * e * sizeof(float);
   if (smem > 48 * 1024) {
-    auto fn = logits_dtype == DWM_BF16 ? route::route_topk_kernel<DWM_BF16>
-                                       : route::route_topk_kernel<DWM_F32>;
+    auto fn = logits_dtype == DWM_BF16 ? route_topk_kernel<DWM_BF16> : route_topk_kernel<DWM_F32>;
     int rc = check_cuda(
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
         "route smem attribute");
     if (rc) return rc;
   }
-  const unsigned grid = (unsigned)((t + route::WARPS - 1) / route::WARPS);
+  const unsigned grid = (unsigned)((t + WARPS - 1) / WARPS);
   auto w16 = static_cast<uint16_t*>(topk_weights_bf16);
   if (logits_dtype == DWM_BF16)
-    route::route_topk_kernel<DWM_BF16><<<grid, 32 * route::WARPS, smem, s>>>(
-        logits, t, e, top_k, scoring, renormalize, bias, num_valid_tokens, topk_ids,
-        topk_weights_f32, w16);
+    route_topk_kernel<DWM_BF16><<<grid, 32 * WARPS, smem, s>>>(
+        logits, t, e, top_k, scoring, renormalize, bias, num_valid_tokens, hash_ids, topk_ids,
+        topk_weights_f32, w16, status_ptr());
   else
-    route::route_topk_kernel<DWM_F32><<<grid, 32 * route::WARPS, smem, s>>>(
-        logits, t, e, top_k, scoring, renormalize, bias, num_valid_tokens, topk_ids,
-        topk_weights_f32, w16);
+    route_topk_kernel<DWM_F32><<<grid, 32 * WARPS, smem, s>>>(
+        logits, t, e, top_k, scoring, renormalize, bias, num_valid_tokens, hash_ids, topk_ids,
+        topk_weights_f32, w16, status_ptr());
   return check_cuda(cudaGetLastError(), "route_topk launch");
+}
+
+// dedupe_topk (E0901:98-121), one thread per token, in place: a repeated
+// expert id adds its f32 weight to the first occurrence and is re-pointed at
+// the lowest of experts 0 .. min(2k, e) - 1 the token does not use, weight 0.
+__global__ void dedupe_kernel(float* __restrict__ w, int32_t* __restrict__ ids, int t, int top_k,
+                              int e, uint16_t* __restrict__ w16) {
+  const int tok = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tok >= t) return;
+  float* wr = w + (int64_t)tok * top_k;
+  int32_t* ir = ids + (int64_t)tok * top_k;
+  const int ncand = min(2 * top_k, e);
+  for (int j = 1; j < top_k; ++j) {
+    int first = -1;
+    for (int q = 0; q < j; ++q)
+      if (ir[q] == ir[j]) {
+        first = q;
+        break;
+      }
+    if (first < 0) continue;
+    wr[first] = __fadd_rn(wr[first], wr[j]);
+    int free_id = 0;  // argmin over "used": the first unused candidate, else 0
+    for (int c = 0; c < ncand; ++c) {
+      bool used = false;
+      for (int q = 0; q < top_k; ++q) used |= ir[q] == c;
+      if (!used) {
+        free_id = c;
+        break;
+      }
+    }
+    ir[j] = free_id;
+    wr[j] = 0.0f;
+  }
+  if (w16)
+    for (int q = 0; q < top_k; ++q)
+      w16[(int64_t)tok * top_k + q] = (uint16_t)f32_to_bf16_bits(wr[q]);
+}
+
+}  // namespace route
+}  // namespace dwm
+
+extern "C" int dwm_route_topk(const void* logits, int logits_dtype, int t, int e, int top_k,
+                              int scoring, int renormalize, const float* bias,
+                              int num_valid_tokens, int32_t* topk_ids, float* topk_weights_f32,
+                              void* topk_weights_bf16, void* stream) {
+  return route::route_impl(logits, logits_dtype, t, e, top_k, scoring, renormalize, bias, nullptr,
+                           num_valid_tokens, topk_ids, topk_weights_f32, topk_weights_bf16,
+                           stream);
+}
+
+extern "C" int dwm_route_hash(const void* logits, int logits_dtype, int t, int e, int top_k,
+                              int scoring, int renormalize, const int32_t* hash_ids,
+                              int num_valid_tokens, int32_t* topk_ids, float* topk_weights_f32,
+                              void* topk_weights_bf16, void* stream) {
+  DWM_CHECK_ARG(t == 0 || hash_ids, "NULL hash_ids");
+  return route::route_impl(logits, logits_dtype, t, e, top_k, scoring, renormalize, nullptr,
+                           hash_ids, num_valid_tokens, topk_ids, topk_weights_f32,
+                           topk_weights_bf16, stream);
+}
+
+extern "C" int dwm_dedupe_topk(float* topk_weights_f32, int32_t* topk_ids, int t, int top_k,
+                               int num_experts, void* topk_weights_bf16, void* stream) {
+  DWM_CHECK_ARG(t >= 0 && top_k >= 1 && top_k <= 32 && num_experts >= 1, "bad shape");
+  DWM_CHECK_ARG(t == 0 || (topk_weights_f32 && topk_ids), "NULL pointer");
+  if (t == 0) return DWM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  route::dedupe_kernel<<<(t + 127) / 128, 128, 0, s>>>(topk_weights_f32, topk_ids, t, top_k,
+                                                       num_experts,
+                                                       static_cast<uint16_t*>(topk_weights_bf16));
+  return check_cuda(cudaGetLastError(), "dedupe_topk launch");
 }
 
 extern "C" int dwm_e8m0_encode(const float* scale, size_t n, uint8_t* codes,

@@ -44,6 +44,26 @@ class FP4MoEWeights:
         return FP4MoEWeights(ops.fp4_to_b200_out(self.w13), self.s13,
                              ops.fp4_to_b200_out(self.w2), self.s2, "b200")
 
+    @classmethod
+    def from_dense(cls, w13: torch.Tensor, w2: torch.Tensor) -> "FP4MoEWeights":
+        """Weight preparation on the device: dense (or dequantised MXFP4)
+        expert weights w13 [E, H, 2I] and w2 [E, I, H] (bf16 / f32) re-quantised
+        with quantize_tensor(float4_e2m1fn, block 32, power_of_two_scale=True)
+        (B01:319-347) into packed e2m1 codes and E8M0 scales (KE:28-40), the
+        layouts the grouped matmul reads. Raises if a scale does not fit E8M0
+        (a block whose scale is not a normal power of two)."""
+        out = []
+        for w in (w13, w2):
+            e, k, n = w.shape
+            codes = torch.empty((e, k, n // 2), dtype=torch.uint8, device=w.device)
+            scales = torch.empty((e, k // 32, n), dtype=torch.uint8, device=w.device)
+            lossless = torch.empty(1, dtype=torch.int32, device=w.device)
+            ops.fp4_quantize_out(w.contiguous(), codes, scales, lossless)
+            if int(lossless.item()) != 1:
+                raise ValueError("a block scale is not a normal power of two; keep f32 scales")
+            out += [codes, scales]
+        return cls(out[0], out[1], out[2], out[3])
+
     @property
     def num_experts(self) -> int:
         return self.s13.shape[0]

@@ -124,6 +124,29 @@ def fp4_to_b200_out(src, inverse=False, stream=None):
     return dst
 
 
+def fp4_quantize_out(w, codes, scales, lossless=None, *, power_of_two_scale=True,
+                     stream=None):
+    """quantize_tensor(float4_e2m1fn, w, block 32, power_of_two_scale)
+    (B01:319-347) of w [g, k, n] (bf16/f32) over blocks of 32 consecutive k:
+    codes uint8 [g, k, n/2] (packed e2m1), scales [g, k/32, n] as uint8 E8M0
+    codes (``lossless`` int32 [1] on the device is set to 1, cleared if a scale
+    is not a normal power of two or +0) or f32 (dwm_fp4_quantize)."""
+    L.require_cuda(w, codes, scales, lossless)
+    if w.dim() != 3 or not w.is_contiguous():
+        raise ValueError("w must be a contiguous [g, k, n] tensor")
+    g, k, n = w.shape
+    if codes.shape != (g, k, n // 2) or codes.dtype != torch.uint8:
+        raise ValueError("codes must be uint8 [g, k, n/2]")
+    if scales.shape != (g, k // 32, n):
+        raise ValueError("scales must be [g, k/32, n]")
+    rc = L.lib().dwm_fp4_quantize(w.data_ptr(), L.dtype_code(w.dtype), g, k, n,
+                                  int(bool(power_of_two_scale)), codes.data_ptr(),
+                                  scales.data_ptr(), L.dtype_code(scales.dtype), L.ptr(lossless),
+                                  L.stream_ptr() if stream is None else stream)
+    L.check(rc, "fp4_quantize")
+    return codes, scales
+
+
 def fp4_codes_convert_out(src, dst, from_format, to_format, stream=None):
     L.require_cuda(src, dst)
     src, dst = _u8view(src), _u8view(dst)
@@ -161,6 +184,35 @@ def route_topk_out(logits, top_k, ids_out, w32_out=None, w16_out=None, *,
         -1 if num_valid_tokens is None else int(num_valid_tokens), ids_out.data_ptr(),
         L.ptr(w32_out), L.ptr(w16_out), L.stream_ptr() if stream is None else stream)
     L.check(rc, "route_topk")
+
+
+def route_hash_out(logits, hash_ids, ids_out, w32_out=None, w16_out=None, *,
+                   scoring_fn="sigmoid", renormalize=True, num_valid_tokens=None, stream=None):
+    L.require_cuda(logits, hash_ids, ids_out, w32_out, w16_out)
+    if logits.dim() != 2 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous [t, e] tensor")
+    t, e = logits.shape
+    if hash_ids.dtype != torch.int32 or hash_ids.dim() != 2 or hash_ids.shape[0] != t:
+        raise ValueError("hash_ids must be int32 [t, top_k]")
+    if scoring_fn not in _SCORING:
+        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
+    rc = L.lib().dwm_route_hash(
+        logits.data_ptr(), L.dtype_code(logits.dtype), t, e, hash_ids.shape[1],
+        _SCORING[scoring_fn], int(bool(renormalize)), hash_ids.data_ptr(),
+        -1 if num_valid_tokens is None else int(num_valid_tokens), ids_out.data_ptr(),
+        L.ptr(w32_out), L.ptr(w16_out), L.stream_ptr() if stream is None else stream)
+    L.check(rc, "route_hash")
+
+
+def dedupe_topk_(w32, ids, num_experts, w16_out=None, stream=None):
+    """In place on f32 weights and int32 ids [t, top_k] (dwm_dedupe_topk)."""
+    L.require_cuda(w32, ids, w16_out)
+    if w32.dtype != torch.float32 or ids.dtype != torch.int32 or w32.shape != ids.shape:
+        raise ValueError("expected f32 weights and int32 ids of the same [t, top_k] shape")
+    t, k = ids.shape
+    rc = L.lib().dwm_dedupe_topk(w32.data_ptr(), ids.data_ptr(), t, k, int(num_experts),
+                                 L.ptr(w16_out), L.stream_ptr() if stream is None else stream)
+    L.check(rc, "dedupe_topk")
 
 
 def permute_out(topk_ids, num_experts, group_sizes, argsort=None, token_indices_sorted=None,

@@ -30,3 +30,30 @@ def route_topk(gating_output: torch.Tensor, top_k: int, renormalize: bool = True
     if dtype == torch.bfloat16:
         return w16, ids
     return w32.to(dtype), ids
+
+
+def route_hash(gating_output: torch.Tensor, hash_ids: torch.Tensor, renormalize: bool = True,
+               scoring_fn: str = "sigmoid", dtype: torch.dtype = torch.bfloat16,
+               num_valid_tokens: int | None = None):
+    """Hash routing of ``_fused_moe_fp4_routing`` (E0901:667-671): the ids
+    are ``hash_ids`` [t, top_k]; the weights are the scores at those ids,
+    renormalised, padding rows -> expert 0 with weight 0."""
+    logits = gating_output.contiguous()
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        logits = logits.float()
+    t, top_k = hash_ids.shape
+    ids = torch.empty((t, top_k), dtype=torch.int32, device=logits.device)
+    w32 = torch.empty((t, top_k), dtype=torch.float32, device=logits.device)
+    ops.route_hash_out(logits, hash_ids.to(torch.int32).contiguous(), ids, w32,
+                       scoring_fn=scoring_fn, renormalize=renormalize,
+                       num_valid_tokens=num_valid_tokens)
+    return w32.to(dtype), ids
+
+
+def dedupe_topk(topk_weights: torch.Tensor, topk_ids: torch.Tensor, num_experts: int):
+    """E0901:98-121: makes each token's expert ids distinct. Returns new
+    (f32 weights, int32 ids)."""
+    w = topk_weights.float().contiguous().clone()
+    ids = topk_ids.to(torch.int32).contiguous().clone()
+    ops.dedupe_topk_(w, ids, num_experts)
+    return w, ids

@@ -129,6 +129,18 @@ int dwm_fp4_dequant(const void* codes, int codes_format, const void* scales, int
 int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int n, int inverse,
                     void* stream);
 
+/* On-device weight preparation: quantize_tensor(float4_e2m1fn, w, block 32,
+ * power_of_two_scale) (B01:319-347) of w [groups, k, n] (bf16 or f32) over
+ * blocks of 32 consecutive k of each column -> codes uint8 [groups, k, n/2]
+ * (packed e2m1, element 2j in the low nibble) and scales [groups, k/32, n]:
+ * DWM_U8 E8M0 codes (needs pow2 = 1; *lossless_dev, int32 on the device, is
+ * set to 1 and cleared if a scale is not a positive normal power of two or
+ * +0, as e8m0_encode's flag, KE:28-34) or DWM_F32. With pow2 = 1,
+ * re-quantising MXFP4 data reproduces it exactly (B01:131-157). k % 32 == 0,
+ * n % 2 == 0. */
+int dwm_fp4_quantize(const void* w, int w_dtype, int groups, int k, int n, int pow2, void* codes,
+                     void* scales, int scale_dtype, int32_t* lossless_dev, void* stream);
+
 /* Re-encode packed nibbles between DWM_FP4_E2M1 and DWM_FP4_TOKAMAX
  * (tokamax e2m1_to_codes, TK:17-30, and its inverse); in == out allowed. */
 int dwm_fp4_codes_convert(const void* in, void* out, size_t nbytes, int from_format,
@@ -150,6 +162,22 @@ int dwm_e8m0_decode(const uint8_t* codes, size_t n, float* out, void* stream);
 int dwm_route_topk(const void* logits, int logits_dtype, int t, int e, int top_k, int scoring,
                    int renormalize, const float* bias, int num_valid_tokens, int32_t* topk_ids,
                    float* topk_weights_f32, void* topk_weights_bf16, void* stream);
+
+/* Hash routing (E0901:667-671): the ids come precomputed (hash_ids int32
+ * [t, top_k], e.g. DeepSeek-V4's hash layers) and the weights are the scores
+ * at those ids; renormalisation and padding as dwm_route_topk. Ids outside
+ * [0, e) are reported (DWM_DEV_BAD_INDEX) and read as expert 0. */
+int dwm_route_hash(const void* logits, int logits_dtype, int t, int e, int top_k, int scoring,
+                   int renormalize, const int32_t* hash_ids, int num_valid_tokens,
+                   int32_t* topk_ids, float* topk_weights_f32, void* topk_weights_bf16,
+                   void* stream);
+
+/* dedupe_topk (E0901:98-121), in place: a repeated expert id within a token
+ * adds its f32 weight to the first occurrence and is re-pointed at the lowest
+ * of experts 0 .. min(2*top_k, num_experts)-1 the token does not use, with
+ * weight 0. topk_weights_bf16 (may be NULL) receives the bf16 cast. */
+int dwm_dedupe_topk(float* topk_weights_f32, int32_t* topk_ids, int t, int top_k,
+                    int num_experts, void* topk_weights_bf16, void* stream);
 
 /* ---- permute / dispatch (KD, X0405:70-98) -------------------------------- */
 /* KD:41-44: out[j] = argsort[j] / topk. */

@@ -45,7 +45,7 @@ __all__ = [
     "dequantize_fp4_block32", "apply_scoring_fn", "route_topk",
     "sorted_token_indices", "permute", "dispatch_gather", "combine",
     "fused_moe", "ep_dispatch", "ep_combine_korder", "ep_combine_rankorder",
-    "all_gather", "reduce_scatter_rank_order", "dedupe_topk",
+    "all_gather", "reduce_scatter_rank_order", "dedupe_topk", "route_hash",
 ]
 
 # e2m1 magnitudes by 3-bit magnitude code (exponent<<1 | mantissa), TK:35-36.
@@ -428,6 +428,22 @@ def route_topk(logits, top_k: int, scoring_fn: str = "sigmoid",
     order = np.argsort(-sel, axis=-1, kind="stable")[:, :top_k]
     ids = order.astype(np.int32)
     w = np.take_along_axis(s, order, axis=-1).astype(np.float32)
+    if renormalize:
+        w = (w / w.sum(axis=-1, keepdims=True)).astype(np.float32)
+    if num_valid_tokens is not None:
+        valid = (np.arange(s.shape[0]) < num_valid_tokens)[:, None]
+        ids = np.where(valid, ids, 0).astype(np.int32)
+        w = np.where(valid, w, 0.0).astype(np.float32)
+    return ids, w
+
+
+def route_hash(logits, hash_ids, scoring_fn: str = "sigmoid", renormalize: bool = True,
+               num_valid_tokens=None):
+    """E0901:667-671 (hash routing): ids = hash_ids, weights = the scores at
+    those ids; then renormalise and pad like ``route_topk``."""
+    s = apply_scoring_fn(scoring_fn, logits)
+    ids = np.asarray(hash_ids, np.int32)
+    w = np.take_along_axis(s, ids, axis=-1).astype(np.float32)
     if renormalize:
         w = (w / w.sum(axis=-1, keepdims=True)).astype(np.float32)
     if num_valid_tokens is not None:

@@ -139,6 +139,36 @@ def test_route_topk_bias_and_padding(dw):
     assert np.all(ids.cpu().numpy()[33:] == 0) and np.all(w.cpu().numpy()[33:] == 0)
 
 
+@pytest.mark.parametrize("fn", ["sigmoid", "sqrtsoftplus", "softmax"])
+def test_route_hash(dw, fn):
+    """Hash routing (E0901:667-671): given ids, weights = scores at them."""
+    rng = np.random.default_rng(4)
+    t, e, k = 37, 64, 6
+    logits = O.round_bf16(rng.standard_normal((t, e)).astype(np.float32))
+    hid = rng.integers(0, e, (t, k)).astype(np.int32)   # repeats allowed
+    w, ids = dw.route_hash(np_to_bf16(logits), torch.from_numpy(hid).cuda(), scoring_fn=fn,
+                           num_valid_tokens=30, dtype=torch.float32)
+    rid, rw = O.route_hash(logits, hid, fn, True, num_valid_tokens=30)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
+def test_dedupe_topk_bit_exact(dw):
+    """E0901:98-121: repeated ids fold their weight into the first occurrence
+    and move to the lowest unused expert with weight 0."""
+    rng = np.random.default_rng(5)
+    t, e, k = 200, 16, 8
+    ids = rng.integers(0, 6, (t, k)).astype(np.int32)   # many repeats
+    ids[0] = [3, 3, 3, 3, 3, 3, 3, 3]
+    ids[1] = np.arange(8)                                 # already distinct
+    w = rng.random((t, k)).astype(np.float32)
+    gw, gi = dw.dedupe_topk(torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), e)
+    rw, ri = O.dedupe_topk(w, ids, e)
+    assert np.array_equal(gi.cpu().numpy(), ri)
+    assert np.array_equal(gw.cpu().numpy(), rw)
+    assert all(len(set(r)) == k for r in gi.cpu().numpy().tolist())
+
+
 def test_route_ties_go_to_lower_index(dw):
     logits = torch.zeros((2, 64), dtype=torch.float32, device="cuda")
     w, ids = dw.route_topk(logits, 4, scoring_fn="softmax", dtype=torch.float32)

@@ -201,6 +201,19 @@ def test_oneshot_collectives():
         assert np.array_equal(outs[r], exp)
 
 
+def test_route_hash_matches_take_along_scores():
+    rng = np.random.default_rng(6)
+    logits = rng.standard_normal((5, 16)).astype(np.float32)
+    hid = rng.integers(0, 16, (5, 4)).astype(np.int32)
+    ids, w = O.route_hash(logits, hid, "sigmoid", renormalize=False)
+    s = 1.0 / (1.0 + np.exp(-logits.astype(np.float64)))
+    assert np.array_equal(ids, hid)
+    np.testing.assert_allclose(w, np.take_along_axis(s, hid, axis=-1), rtol=1e-6)
+    ids2, w2 = O.route_hash(logits, hid, "sigmoid", num_valid_tokens=3)
+    assert np.all(ids2[3:] == 0) and np.all(w2[3:] == 0)
+    np.testing.assert_allclose(w2[:3].sum(-1), 1.0, rtol=1e-6)
+
+
 def test_dedupe_topk():
     w = np.array([[0.5, 0.3, 0.2]], np.float32)
     ids = np.array([[3, 3, 1]], np.int32)
