@@ -87,6 +87,7 @@ SIGNATURES = {
     "dwm_ep_connect": ([_P, _P], _I),
     "dwm_ep_connect_local": ([_P, _c.POINTER(_P)], _I),
     "dwm_ep_recv_buffer": ([_P, _c.POINTER(_P), _c.POINTER(_I64)], _I),
+    "dwm_ep_output_buffer": ([_P, _c.POINTER(_P), _c.POINTER(_I64)], _I),
     "dwm_ep_dispatch": ([_P, _P, _P, _I, _P, _I, _P], _I),
     "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
     "dwm_ep_destroy": ([_P], _I),

@@ -5,24 +5,30 @@
 //
 // One process per GPU. Every rank owns one device allocation with the same
 // layout (the "symmetric" buffer), exports it as a CUDA IPC handle, and maps
-// every peer's; kernels then store straight into peer memory over NVLink.
+// every peer's; kernels then load and store peer memory over NVLink.
 //
-//   dispatch  COUNTS  one CTA stably sorts the rank's (token, k) pairs by
-//                     expert (the counting sort of the single-device permute),
-//                     then stores its per-expert counts into every peer's count
-//                     matrix and raises a per-source flag there.
-//             ROWS    each CTA waits for all sources' counts, derives where
-//                     each local pair lands in its owner's receive buffer, and
-//                     copies the token row there (16-byte stores, a warp per
-//                     row) with a (source rank, pair) tag; then it bumps every
-//                     peer's arrival counter.
-//             WAIT    one thread waits until all CTAs of all sources arrived.
-//   combine   PUSH    each CTA copies expert-output rows back to the pair's
-//                     source, into that rank's combine buffer at the pair's
-//                     slot, then bumps every peer's arrival counter.
-//             REDUCE  every CTA waits for all arrivals, then forms the k-order
-//                     f32 weighted sum of each token (the single-device
-//                     combine's arithmetic, bit for bit).
+//   dispatch  one kernel of XFER_CTAS CTAs. Every CTA histograms all of the
+//             rank's (token, k) expert ids in shared memory (so no CTA waits
+//             on another CTA of its grid). The first CTA to start publishes
+//             the per-expert counts into every peer's count table as 64-bit
+//             (epoch << 32 | count) words, which need no fence or flag.
+//             Each CTA then waits for the peers' counts of this epoch, forms
+//             the receive offsets, and stores the rows of its own slice of
+//             pairs straight into the owners' receive buffers (the whole CTA
+//             on a few rows, loads batched ahead of the stores). The CTA that
+//             finishes last (a ticket) bumps every peer's arrival counter
+//             once and waits until all ranks have bumped its own.
+//   combine   one kernel. The first CTA to start announces that this rank's
+//             expert outputs (the symmetric output buffer, written by the
+//             preceding grouped matmul) are ready; every CTA waits for the
+//             peers' announcements, then forms each token's k-order f32
+//             weighted sum, loading each (token, k) row straight from the
+//             owner's output buffer at the row the dispatch sent it to (the
+//             single-device combine's arithmetic, bit for bit).
+//
+// The phases can also be issued as separate launches (DWM_EP_COUNTS, _ROWS,
+// _WAIT; DWM_EP_PUSH, _REDUCE), which the single-GPU emulation of several
+// ranks needs: there every rank's earlier phase runs before any later one.
 //
 // Receive order: rank r's rows are expert-major over its experts
 // [r*E/n, (r+1)*E/n), and inside an expert ordered by (source rank, source
@@ -33,11 +39,18 @@
 //   + its rank among the source's own pairs of that expert (stable).
 //
 // Waits are bounded (2 s, then DWM_DEV_TIMEOUT in the status word and the
-// kernel returns). Every wait depends only on kernels of other ranks (or of
-// earlier launches), never on a CTA of the same grid, so a grid that is not
-// fully resident cannot deadlock. Flags and counters are monotonic (epoch
-// numbered), so nothing is reset between steps; the count matrix is double
-// buffered by epoch parity.
+// kernel winds down). Every wait depends only on kernels of other ranks or of
+// earlier launches, never on a particular CTA of the same grid: the counts are
+// published by whichever CTA starts first, and only the last CTA to finish
+// waits for the arrivals. Counters are monotonic and tagged with a
+// per-rank epoch that lives in device memory (the dispatch advances it), so
+// nothing is reset between steps and a captured CUDA graph of the exchange
+// replays with a fresh epoch each time.
+//
+// Reuse across steps is safe without extra barriers: a rank starts its next
+// dispatch only after its combine has read every peer's outputs, and a peer
+// overwrites its receive rows, counts or outputs only after that next
+// dispatch's counts from this rank have reached it.
 #include <cstring>
 #include <new>
 
@@ -47,30 +60,38 @@ namespace dwm {
 namespace ep {
 
 constexpr int MAX_WORLD = 8;
-constexpr int XFER_CTAS = 128;  // grid of the ROWS and PUSH kernels (the same on every rank)
+constexpr int XFER_CTAS = 128;  // grid of the dispatch kernel
 constexpr int XFER_THREADS = 512;
-constexpr int XFER_WARPS = XFER_THREADS / 32;
+constexpr int COMBINE_THREADS = 64;
+constexpr int ROW_BITS = 28;    // sent-row code: owner << ROW_BITS | row
+constexpr int64_t MAX_CAP = 1LL << ROW_BITS;
 
 struct Layout {  // byte offsets inside every rank's symmetric buffer
-  size_t flags;   // uint32 [MAX_WORLD]: epoch of the counts source s stored here
-  size_t arrive;  // uint64 [2]: dispatch / combine CTA arrivals (monotonic)
-  size_t counts;  // int32 [2][MAX_WORLD][E]: per-source expert counts, by epoch parity
-  size_t meta;    // int32 [cap]: source rank * max_pairs + pair of each received row
+  size_t ready;   // uint32 [MAX_WORLD]: epoch whose outputs source s has made readable
+  size_t arrive;  // uint64: dispatch arrivals (one per rank and epoch, monotonic)
+  size_t counts;  // uint64 [MAX_WORLD][E]: (epoch << 32) | count of expert x from source s
   size_t recv;    // bf16 [cap][H]: received rows, expert-major
-  size_t cbuf;    // [max_pairs][H] (4-byte capacity): combine buffer, one row per own pair
+  size_t outb;    // [cap][H], 4-byte capacity: expert outputs of the received rows
   size_t total;
 };
+
+// Per-rank control words (ordinary device memory, not shared with peers).
+enum Ctl { CTL_EPOCH = 0, CTL_FIRST = 1, CTL_DONE = 2, CTL_RECV_ROWS = 3, CTL_WORDS = 4 };
 
 struct Params {
   uint8_t* peer[MAX_WORLD];
   Layout L;
-  int rank, world, E, LE, H, topk, T, max_pairs;
+  int rank, world, E, LE, H, topk, T;
   int64_t cap;
-  uint32_t epoch;
+  int32_t* sent;  // [max_pairs]: owner << ROW_BITS | row of each own pair, -1 if dropped
+  uint32_t* ctl;  // [CTL_WORDS]
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -82,8 +103,19 @@ __device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
 }
 
 // Bounded spin until *p >= target (32-bit epoch flag).
@@ -91,7 +123,7 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t target, in
   if (ld_acquire_sys(p) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    __nanosleep(64);
+    __nanosleep(32);
     if (ld_acquire_sys(p) >= target) return true;
     if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       report(status, DWM_DEV_TIMEOUT);
@@ -104,7 +136,7 @@ __device__ __forceinline__ bool wait_count(const uint64_t* p, uint64_t target, i
   if (ld_acquire_sys64(p) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    __nanosleep(64);
+    __nanosleep(32);
     if (ld_acquire_sys64(p) >= target) return true;
     if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       report(status, DWM_DEV_TIMEOUT);
@@ -113,165 +145,291 @@ __device__ __forceinline__ bool wait_count(const uint64_t* p, uint64_t target, i
   }
 }
 
-__device__ __forceinline__ int* counts_of(const Params& P, int rank_mem, int src) {
-  return reinterpret_cast<int*>(P.peer[rank_mem] + P.L.counts) +
-         ((size_t)(P.epoch & 1) * MAX_WORLD + src) * P.E;
-}
-
-// COUNTS: local stable sort + publish counts to every rank.
-__global__ void __launch_bounds__(moe::SORT_THREADS, 1)
-    ep_count_kernel(const __grid_constant__ Params P, const int32_t* __restrict__ ids, int32_t* revert,
-                    int32_t* counts, int32_t* prefix, int* status) {
-  extern __shared__ int sm[];
-  moe::counting_sort_block(ids, P.T * P.topk, P.topk, P.E, nullptr, nullptr, revert, counts,
-                           prefix, status, sm);
-  __syncthreads();
-  for (int i = threadIdx.x; i < P.world * P.E; i += blockDim.x) {
-    const int p = i / P.E, x = i - p * P.E;
-    counts_of(P, p, P.rank)[x] = counts[x];
-  }
-  __threadfence_system();
-  __syncthreads();
-  if ((int)threadIdx.x < P.world)
-    st_release_sys(reinterpret_cast<uint32_t*>(P.peer[threadIdx.x] + P.L.flags) + P.rank,
-                   P.epoch);
-}
-
-// ROWS: place every local pair in its owner's receive buffer.
-// smem: colsum [E], before [E], dest [E] ints.
-__global__ void __launch_bounds__(XFER_THREADS)
-    ep_send_kernel(const __grid_constant__ Params P, const uint4* __restrict__ hidden,
-                   const int32_t* __restrict__ ids, const int32_t* __restrict__ revert,
-                   const int32_t* __restrict__ prefix, int32_t* recv_group_sizes, int* status) {
-  extern __shared__ int sm[];
-  int* colsum = sm;
-  int* before = sm + P.E;
-  int* dest = sm + 2 * P.E;
-  __shared__ int s_fail;
-  if (threadIdx.x == 0) s_fail = 0;
-  __syncthreads();
-  if ((int)threadIdx.x < P.world) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(P.peer[P.rank] + P.L.flags) + threadIdx.x;
-    if (!wait_flag(f, P.epoch, status)) s_fail = 1;
-  }
-  __syncthreads();
-  if (s_fail) return;
-  for (int x = threadIdx.x; x < P.E; x += blockDim.x) {
-    int col = 0, bef = 0;
-    for (int s = 0; s < P.world; ++s) {
-      const int v = __ldcg(counts_of(P, P.rank, s) + x);
-      col += v;
-      if (s < P.rank) bef += v;
+// Bounded spin until the tagged count word carries `epoch`; its count or -1.
+__device__ __forceinline__ int wait_tagged(const uint64_t* p, uint32_t epoch, int* status) {
+  uint64_t v = ld_relaxed_sys64(p);
+  if ((uint32_t)(v >> 32) == epoch) return (int)(uint32_t)v;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(32);
+    v = ld_relaxed_sys64(p);
+    if ((uint32_t)(v >> 32) == epoch) return (int)(uint32_t)v;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      report(status, DWM_DEV_TIMEOUT);
+      return -1;
     }
-    colsum[x] = col;
-    before[x] = bef;
   }
-  __syncthreads();
-  for (int x = threadIdx.x; x < P.E; x += blockDim.x) {
-    const int owner = x / P.LE;
-    int base = 0;
-    for (int x2 = owner * P.LE; x2 < x; ++x2) base += colsum[x2];
-    dest[x] = base + before[x] - prefix[x];  // + the pair's local sorted position
-    if (blockIdx.x == 0 && owner == P.rank) recv_group_sizes[x - owner * P.LE] = colsum[x];
+}
+
+__device__ __forceinline__ uint64_t* count_word(const Params& P, int rank_mem, int src, int x) {
+  return reinterpret_cast<uint64_t*>(P.peer[rank_mem] + P.L.counts) + (size_t)src * P.E + x;
+}
+
+// Dynamic shared memory of the dispatch kernel (ints): tot, run, col, scan,
+// dest [E] each, then the chunk's experts and rows [XFER_THREADS] each.
+inline size_t dispatch_smem_bytes(int e) { return (size_t)(5 * e + 2 * XFER_THREADS) * 4; }
+
+// Exclusive scan of in[0, n) into out by warp 0 (chunked per lane).
+__device__ __forceinline__ void warp0_exclusive_scan(const int* in, int* out, int n) {
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x >= 32) return;
+  const int per = (n + 31) / 32;
+  int sum = 0;
+  for (int i = 0; i < per; ++i) {
+    const int x = lane * per + i;
+    if (x < n) sum += in[x];
   }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h16 = P.H / 8;
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int run = incl - sum;
+  for (int i = 0; i < per; ++i) {
+    const int x = lane * per + i;
+    if (x < n) {
+      out[x] = run;
+      run += in[x];
+    }
+  }
+}
+
+// The dispatch (phases: DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_WAIT).
+__global__ void __launch_bounds__(XFER_THREADS)
+    ep_dispatch_kernel(const __grid_constant__ Params P, const uint4* __restrict__ hidden,
+                       const int32_t* __restrict__ ids, int32_t* recv_group_sizes, int ph,
+                       int* status) {
+  extern __shared__ int sm[];
+  int* tot = sm;                 // this rank's count of each expert
+  int* run = sm + P.E;           // count of each expert in pairs before the chunk
+  int* col = sm + 2 * P.E;       // all ranks' count of each expert
+  int* scan = sm + 3 * P.E;      // exclusive scan of col
+  int* dest = sm + 4 * P.E;      // first receive row of this rank's pairs of each expert
+  int* cx = sm + 5 * P.E;        // chunk: expert of each pair (-1: dropped)
+  int* crow = cx + XFER_THREADS; // chunk: receive row of each pair (-1: dropped)
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_first, s_last, s_fail;
+  const int tid = threadIdx.x;
   const int n = P.T * P.topk;
-  for (int j = blockIdx.x * XFER_WARPS + warp; j < n; j += gridDim.x * XFER_WARPS) {
-    const int pos = revert[j];
-    if (pos < 0) continue;  // invalid id, reported by the sort
-    const int e = ids[j];
-    const int owner = e / P.LE;
-    const int64_t row = (int64_t)dest[e] + pos;
-    if (row < 0 || row >= P.cap) {
-      if (lane == 0) report(status, DWM_DEV_OVERFLOW);
-      continue;
-    }
-    const uint4* src = hidden + (int64_t)(j / P.topk) * h16;
-    uint4* dst = reinterpret_cast<uint4*>(P.peer[owner] + P.L.recv) + row * h16;
-    for (int c = lane; c < h16; c += 32) dst[c] = src[c];
-    if (lane == 0)
-      reinterpret_cast<int32_t*>(P.peer[owner] + P.L.meta)[row] = P.rank * P.max_pairs + j;
+  const bool counts = ph & DWM_EP_COUNTS, rows = ph & DWM_EP_ROWS;
+  if (tid == 0) {
+    s_epoch = P.ctl[CTL_EPOCH] + (counts ? 1u : 0u);
+    s_first = counts ? atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u : 0;
+    s_fail = 0;
   }
-  __threadfence_system();
+  for (int x = tid; x < 2 * P.E; x += blockDim.x) sm[x] = 0;
   __syncthreads();
-  if ((int)threadIdx.x < P.world)
-    red_release_sys_add(reinterpret_cast<uint64_t*>(P.peer[threadIdx.x] + P.L.arrive), 1);
-}
+  const uint32_t epoch = s_epoch;
+  const int slice = (n + gridDim.x - 1) / gridDim.x;
+  const int j0 = min(n, (int)blockIdx.x * slice), j1 = min(n, j0 + slice);
 
-// WAIT (dispatch: which = 0) — one thread.
-__global__ void ep_wait_kernel(const __grid_constant__ Params P, int which, uint64_t target, int* status) {
-  if (threadIdx.x == 0)
-    wait_count(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.arrive) + which, target,
-               status);
-}
-
-// PUSH: return every received row's expert output to the pair's source.
-// y_es: bytes per element of y (2 or 4).
-__global__ void __launch_bounds__(XFER_THREADS)
-    ep_push_kernel(const __grid_constant__ Params P, const uint8_t* __restrict__ y, int y_es, int* status) {
-  __shared__ int s_rows;
-  if (threadIdx.x == 0) s_rows = 0;
-  __syncthreads();
-  int part = 0;
-  for (int x = threadIdx.x; x < P.LE; x += blockDim.x)
-    for (int s = 0; s < P.world; ++s) part += __ldcg(counts_of(P, P.rank, s) + P.rank * P.LE + x);
-  if (part) atomicAdd(&s_rows, part);
-  __syncthreads();
-  const int rows = s_rows;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row_bytes = (int64_t)P.H * y_es;
-  const int n16 = (int)(row_bytes / 16);
-  const int32_t* meta = reinterpret_cast<const int32_t*>(P.peer[P.rank] + P.L.meta);
-  for (int r = blockIdx.x * XFER_WARPS + warp; r < rows && r < P.cap;
-       r += gridDim.x * XFER_WARPS) {
-    const int tag = __ldcg(meta + r);
-    const int src = tag / P.max_pairs, pair = tag - src * P.max_pairs;
-    if (src < 0 || src >= P.world) {
-      if (lane == 0) report(status, DWM_DEV_BAD_INDEX);
-      continue;
+  if (counts || rows) {
+    for (int j = tid; j < n; j += blockDim.x) {
+      const int x = ids[j];
+      if (x < 0 || x >= P.E) {
+        if (blockIdx.x == 0) report(status, DWM_DEV_BAD_INDEX);
+        continue;
+      }
+      atomicAdd(&tot[x], 1);
+      if (j < j0) atomicAdd(&run[x], 1);
     }
-    const uint4* from = reinterpret_cast<const uint4*>(y + r * row_bytes);
-    uint4* to = reinterpret_cast<uint4*>(P.peer[src] + P.L.cbuf + pair * row_bytes);
-    for (int c = lane; c < n16; c += 32) to[c] = from[c];
+    __syncthreads();
   }
-  __threadfence_system();
+  if (s_first) {  // publish this rank's counts to every rank (itself included)
+    for (int i = tid; i < P.world * P.E; i += blockDim.x) {
+      const int p = i / P.E, x = i - p * P.E;
+      st_relaxed_sys64(count_word(P, p, P.rank, x), ((uint64_t)epoch << 32) | (uint32_t)tot[x]);
+    }
+  }
+  if (rows) {
+    for (int x = tid; x < P.E; x += blockDim.x) {
+      int c = 0, b = 0;
+      for (int s = 0; s < P.world; ++s) {
+        int v = tot[x];
+        if (s != P.rank) {
+          v = wait_tagged(count_word(P, P.rank, s, x), epoch, status);
+          if (v < 0) {
+            s_fail = 1;
+            v = 0;
+          }
+        }
+        c += v;
+        if (s < P.rank) b += v;
+      }
+      col[x] = c;
+      dest[x] = b;
+    }
+    __syncthreads();
+    warp0_exclusive_scan(col, scan, P.E);
+    __syncthreads();
+    for (int x = tid; x < P.E; x += blockDim.x) {
+      const int owner = x / P.LE;
+      dest[x] += scan[x] - scan[owner * P.LE];
+      if (blockIdx.x == 0 && owner == P.rank) recv_group_sizes[x - owner * P.LE] = col[x];
+    }
+    if (blockIdx.x == 0 && tid == 0) {
+      const int last = (P.rank + 1) * P.LE - 1;
+      P.ctl[CTL_RECV_ROWS] = (uint32_t)(scan[last] + col[last] - scan[P.rank * P.LE]);
+    }
+    __syncthreads();
+    const int h16 = P.H / 8;
+    for (int c0 = j0; c0 < j1 && !s_fail; c0 += blockDim.x) {
+      const int cn = min((int)blockDim.x, j1 - c0);
+      if (tid < cn) {
+        const int x = ids[c0 + tid];
+        cx[tid] = (x < 0 || x >= P.E) ? -1 : x;
+      }
+      __syncthreads();
+      if (tid < cn) {
+        const int x = cx[tid];
+        int row = -1;
+        if (x >= 0) {
+          int r = run[x];
+          for (int u = 0; u < tid; ++u) r += cx[u] == x;
+          row = dest[x] + r;
+          if (row >= P.cap) {
+            report(status, DWM_DEV_OVERFLOW);
+            row = -1;
+          }
+        }
+        crow[tid] = row;
+        P.sent[c0 + tid] = row < 0 ? -1 : ((x / P.LE) << ROW_BITS) | row;
+      }
+      __syncthreads();
+      if (tid < cn && cx[tid] >= 0) atomicAdd(&run[cx[tid]], 1);
+      // Copy the chunk's rows: 16-byte units, four loads in flight per thread.
+      const int units = cn * h16;
+      for (int u0 = tid; u0 < units; u0 += 4 * blockDim.x) {
+        uint4 v[4];
+        uint4* to[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u = u0 + q * blockDim.x;
+          to[q] = nullptr;
+          if (u < units) {
+            const int p = u / h16, c = u - p * h16;
+            const int row = crow[p];
+            if (row >= 0) {
+              v[q] = __ldg(hidden + (int64_t)((c0 + p) / P.topk) * h16 + c);
+              to[q] = reinterpret_cast<uint4*>(P.peer[cx[p] / P.LE] + P.L.recv) +
+                      (int64_t)row * h16 + c;
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (to[q]) *to[q] = v[q];
+      }
+      __syncthreads();
+    }
+    if (s_fail)  // counts never came: this slice's pairs are dropped
+      for (int j = j0 + tid; j < j1; j += blockDim.x) P.sent[j] = -1;
+  }
   __syncthreads();
-  if ((int)threadIdx.x < P.world)
-    red_release_sys_add(reinterpret_cast<uint64_t*>(P.peer[threadIdx.x] + P.L.arrive) + 1, 1);
+  // The last CTA to finish: reset the tickets, advance the epoch, signal the
+  // peers once, and wait for all of them. Ordering: every CTA's row stores
+  // precede (bar.sync, then an acq_rel ticket at gpu scope) the last CTA's
+  // ticket, which precedes its release at system scope, which the peers'
+  // acquire observes; causality order is transitive across the two scopes,
+  // so one system-scope release per rank covers all CTAs' stores.
+  if (tid == 0) {
+    s_last = atom_add_acq_rel_gpu(&P.ctl[CTL_DONE], 1u) == gridDim.x - 1;
+    if (s_last) {
+      P.ctl[CTL_DONE] = 0;
+      P.ctl[CTL_FIRST] = 0;
+      if (counts) P.ctl[CTL_EPOCH] = epoch;
+      if (rows)
+        for (int p = 0; p < P.world; ++p)
+          red_release_sys_add(reinterpret_cast<uint64_t*>(P.peer[p] + P.L.arrive), 1);
+      if (ph & DWM_EP_WAIT)
+        wait_count(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.arrive),
+                   (uint64_t)epoch * P.world, status);
+    }
+  }
 }
 
-// REDUCE: out[t] = sum_k y(t, k) * w[t, k] in k order (f32, from +0.0).
+// Copy the received rows' outputs y -> the symmetric output buffer (only when
+// the caller's y is not that buffer).
+__global__ void ep_stage_kernel(const __grid_constant__ Params P, const uint4* __restrict__ y,
+                                int row_bytes) {
+  uint4* to = reinterpret_cast<uint4*>(P.peer[P.rank] + P.L.outb);
+  const int64_t units = (int64_t)P.ctl[CTL_RECV_ROWS] * (row_bytes / 16);
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units;
+       u += (int64_t)gridDim.x * blockDim.x)
+    to[u] = __ldg(y + u);
+}
+
+// The combine (phases: DWM_EP_PUSH = announce outputs, DWM_EP_REDUCE):
+// out[t] = sum_k y(t, k) * w[t, k] in k order (f32, from +0.0). A thread owns
+// 8 consecutive elements of one token and keeps up to KB of its rows' loads in
+// flight: the rows on this rank are loaded before the wait for the peers'
+// announcements, the peers' rows after it.
 template <int XD, int WD, int OD>
-__global__ void ep_reduce_kernel(const __grid_constant__ Params P, const void* __restrict__ w,
-                                 const int32_t* __restrict__ revert, void* __restrict__ out,
-                                 uint64_t target, int* status) {
+__global__ void __launch_bounds__(COMBINE_THREADS)
+    ep_combine_kernel(const __grid_constant__ Params P, const void* __restrict__ w,
+                      void* __restrict__ out, int ph, int* status) {
+  constexpr int KB = 8;
+  constexpr int ROW_MASK = (1 << ROW_BITS) - 1;
+  __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
-  if (threadIdx.x == 0)
-    s_ok = wait_count(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.arrive) + 1, target,
-                      status);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_epoch = P.ctl[CTL_EPOCH];
+    s_ok = 1;
+    // The outputs were written by earlier kernels on this stream: a release
+    // store at system scope publishes them.
+    if ((ph & DWM_EP_PUSH) && atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u)
+      for (int p = 0; p < P.world; ++p)
+        st_release_sys(reinterpret_cast<uint32_t*>(P.peer[p] + P.L.ready) + P.rank, P.ctl[CTL_EPOCH]);
+  }
   __syncthreads();
-  if (!s_ok) return;
-  const void* cbuf = P.peer[P.rank] + P.L.cbuf;
-  const int h8 = P.H / 8;
-  const int64_t total = (int64_t)P.T * h8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  if (ph & DWM_EP_REDUCE) {
+    const int h8 = P.H / 8;
+    const int64_t total = (int64_t)P.T * h8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + tid;
     const int64_t t = i / h8;
     const int c = (int)(i - t * h8);
+    const bool mine = i < total;
     float acc[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
-    for (int k = 0; k < P.topk; ++k) {
-      const int64_t j = t * P.topk + k;
-      const float wk = moe::load_weight<WD>(w, j);
-      if (revert[j] < 0) continue;  // invalid id (reported at dispatch)
-      float v[8];
-      moe::load8_cg<XD>(cbuf, j * P.H + (int64_t)c * 8, v);
-      moe::mul_add8(acc, v, wk);
+    for (int k0 = 0; k0 < P.topk || k0 == 0; k0 += KB) {
+      float v[KB][8];
+      int code[KB];
+#pragma unroll
+      for (int q = 0; q < KB; ++q)
+        code[q] = mine && k0 + q < P.topk ? __ldg(P.sent + t * P.topk + k0 + q) : -1;
+#pragma unroll
+      for (int q = 0; q < KB; ++q)
+        if (code[q] >= 0 && (code[q] >> ROW_BITS) == P.rank)
+          moe::load8_cg<XD>(P.peer[P.rank] + P.L.outb,
+                            (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8, v[q]);
+      if (k0 == 0) {  // the peers' outputs: wait once for their announcements
+        if (tid < P.world && tid != P.rank &&
+            !wait_flag(reinterpret_cast<const uint32_t*>(P.peer[P.rank] + P.L.ready) + tid,
+                       s_epoch, status))
+          s_ok = 0;
+        __syncthreads();
+      }
+      if (!s_ok) break;
+#pragma unroll
+      for (int q = 0; q < KB; ++q)
+        if (code[q] >= 0 && (code[q] >> ROW_BITS) != P.rank)
+          moe::load8_cg<XD>(P.peer[code[q] >> ROW_BITS] + P.L.outb,
+                            (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8, v[q]);
+#pragma unroll
+      for (int q = 0; q < KB; ++q)
+        if (code[q] >= 0)
+          moe::mul_add8(acc, v[q], moe::load_weight<WD>(w, t * P.topk + k0 + q));
     }
-    moe::store8<OD>(out, t * P.H + (int64_t)c * 8, acc);
+    if (mine && s_ok) moe::store8<OD>(out, t * P.H + (int64_t)c * 8, acc);
+  }
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&P.ctl[CTL_DONE], 1u) == gridDim.x - 1) {
+    __threadfence();
+    P.ctl[CTL_DONE] = 0;
+    P.ctl[CTL_FIRST] = 0;
   }
 }
 
@@ -286,12 +444,12 @@ struct dwm_ep {
   int64_t cap, max_pairs;
   ep::Layout L;
   uint8_t* base = nullptr;     // own symmetric buffer
-  int32_t* scratch = nullptr;  // revert [max_pairs], counts [E], prefix [E]
+  int32_t* scratch = nullptr;  // sent [max_pairs], then the control words
   uint8_t* peer[MAX_WORLD] = {};
   bool peer_ipc[MAX_WORLD] = {};
   bool connected = false;
-  uint32_t epoch = 0;  // dispatches started
-  int last_t = -1;     // tokens of the current dispatch
+  bool dispatched = false;  // a COUNTS phase was issued (host-side state check only)
+  int last_t = -1;          // tokens of the current dispatch
 };
 
 namespace {
@@ -309,9 +467,9 @@ ep::Params make_params(const dwm_ep* c) {
   P.H = c->hidden;
   P.topk = c->topk;
   P.T = c->last_t < 0 ? 0 : c->last_t;
-  P.max_pairs = (int)c->max_pairs;
   P.cap = c->cap;
-  P.epoch = c->epoch;
+  P.sent = c->scratch;
+  P.ctl = reinterpret_cast<uint32_t*>(c->scratch + c->max_pairs);
   return P;
 }
 
@@ -342,7 +500,8 @@ extern "C" int dwm_ep_create(int rank, int world, int max_tokens, int hidden, in
   DWM_CHECK_ARG(topk >= 1 && max_tokens >= 1, "bad topk=%d / max_tokens=%d", topk, max_tokens);
   const int64_t max_pairs = (int64_t)max_tokens * topk;
   const int64_t cap = max_pairs * world;
-  DWM_CHECK_ARG(cap < (1LL << 31) / 2, "max_tokens * topk * world too large");
+  DWM_CHECK_ARG(cap <= ep::MAX_CAP, "max_tokens * topk * world above %lld",
+                (long long)ep::MAX_CAP);
   dwm_ep* c = new (std::nothrow) dwm_ep();
   if (!c) return set_error(DWM_ERR_INVALID, "out of host memory");
   c->rank = rank;
@@ -356,18 +515,19 @@ extern "C" int dwm_ep_create(int rank, int world, int max_tokens, int hidden, in
   c->cap = cap;
   cudaGetDevice(&c->device);
   ep::Layout& L = c->L;
-  L.flags = 0;
+  L.ready = 0;
   L.arrive = 64;
   L.counts = 128;
-  L.meta = align_up(L.counts + (size_t)2 * MAX_WORLD * num_experts * 4, 256);
-  L.recv = align_up(L.meta + (size_t)cap * 4, 256);
-  L.cbuf = align_up(L.recv + (size_t)cap * hidden * 2, 256);
-  L.total = align_up(L.cbuf + (size_t)max_pairs * hidden * 4, 256);
+  L.recv = align_up(L.counts + (size_t)MAX_WORLD * num_experts * 8, 256);
+  L.outb = align_up(L.recv + (size_t)cap * hidden * 2, 256);
+  L.total = align_up(L.outb + (size_t)cap * hidden * 4, 256);
   int rc = check_cuda(cudaMalloc(&c->base, L.total), "ep symmetric buffer");
-  if (!rc) rc = check_cuda(cudaMemset(c->base, 0, L.meta), "ep header clear");
+  if (!rc) rc = check_cuda(cudaMemset(c->base, 0, L.recv), "ep header clear");
   if (!rc)
-    rc = check_cuda(cudaMalloc(&c->scratch, (size_t)(max_pairs + 2 * num_experts) * 4),
+    rc = check_cuda(cudaMalloc(&c->scratch, (size_t)(max_pairs + ep::CTL_WORDS) * 4),
                     "ep scratch");
+  if (!rc)
+    rc = check_cuda(cudaMemset(c->scratch + max_pairs, 0, ep::CTL_WORDS * 4), "ep control clear");
   if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "ep create");
   if (rc) {
     if (c->base) cudaFree(c->base);
@@ -439,6 +599,13 @@ extern "C" int dwm_ep_recv_buffer(dwm_ep* c, void** recv, int64_t* capacity_rows
   return DWM_OK;
 }
 
+extern "C" int dwm_ep_output_buffer(dwm_ep* c, void** y, int64_t* capacity_rows) {
+  DWM_CHECK_ARG(c && y && capacity_rows, "NULL pointer");
+  *y = c->base + c->L.outb;
+  *capacity_rows = c->cap;
+  return DWM_OK;
+}
+
 extern "C" int dwm_ep_dispatch(dwm_ep* c, const void* hidden, const int32_t* topk_ids,
                                int num_tokens, int32_t* recv_group_sizes, int phases,
                                void* stream) {
@@ -449,46 +616,22 @@ extern "C" int dwm_ep_dispatch(dwm_ep* c, const void* hidden, const int32_t* top
                 "num_tokens=%d out of [0, max_tokens=%d]", num_tokens, c->max_tokens);
   DWM_CHECK_ARG(num_tokens == 0 || (hidden && topk_ids), "NULL input");
   DWM_CHECK_ARG(moe::aligned16(hidden), "hidden must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int32_t* revert = c->scratch;
-  int32_t* counts = c->scratch + c->max_pairs;
-  int32_t* prefix = counts + c->num_experts;
   if (phases & DWM_EP_COUNTS) {
-    ++c->epoch;
+    c->dispatched = true;
     c->last_t = num_tokens;
-    const size_t smem = moe::sort_smem_bytes(c->num_experts);
-    static bool attr_set[64] = {};
-    if (c->device < 64 && !attr_set[c->device]) {
-      rc = check_cuda(cudaFuncSetAttribute(ep::ep_count_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)moe::sort_smem_bytes(1024)),
-                      "ep count smem attribute");
-      if (rc) return rc;
-      attr_set[c->device] = true;
-    }
-    ep::ep_count_kernel<<<1, moe::SORT_THREADS, smem, s>>>(make_params(c), topk_ids, revert,
-                                                           counts, prefix, status_ptr());
-    rc = check_cuda(cudaGetLastError(), "ep count launch");
-    if (rc) return rc;
   }
-  if (c->epoch == 0) return set_error(DWM_ERR_STATE, "dispatch phases before COUNTS");
+  if (!c->dispatched) return set_error(DWM_ERR_STATE, "dispatch phases before COUNTS");
   if (phases & DWM_EP_ROWS) {
     DWM_CHECK_ARG(num_tokens == c->last_t, "num_tokens=%d differs from the COUNTS phase (%d)",
                   num_tokens, c->last_t);
     DWM_CHECK_ARG(recv_group_sizes, "NULL recv_group_sizes");
-    ep::ep_send_kernel<<<ep::XFER_CTAS, ep::XFER_THREADS, 3 * c->num_experts * sizeof(int), s>>>(
-        make_params(c), static_cast<const uint4*>(hidden), topk_ids, revert, prefix,
-        recv_group_sizes, status_ptr());
-    rc = check_cuda(cudaGetLastError(), "ep send launch");
-    if (rc) return rc;
   }
-  if (phases & DWM_EP_WAIT) {
-    const uint64_t target = (uint64_t)c->epoch * c->world * ep::XFER_CTAS;
-    ep::ep_wait_kernel<<<1, 32, 0, s>>>(make_params(c), 0, target, status_ptr());
-    rc = check_cuda(cudaGetLastError(), "ep wait launch");
-    if (rc) return rc;
-  }
-  return DWM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (phases & DWM_EP_ROWS) ? ep::XFER_CTAS : 1;
+  ep::ep_dispatch_kernel<<<grid, ep::XFER_THREADS, ep::dispatch_smem_bytes(c->num_experts), s>>>(
+      make_params(c), static_cast<const uint4*>(hidden), topk_ids, recv_group_sizes, phases,
+      status_ptr());
+  return check_cuda(cudaGetLastError(), "ep dispatch launch");
 }
 
 extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void* topk_weights,
@@ -496,42 +639,48 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
   int rc = check_ctx(c);
   if (rc) return rc;
   DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_PUSH | DWM_EP_REDUCE), "phases=%d", phases);
-  DWM_CHECK_ARG(c->epoch > 0, "combine before any dispatch");
+  DWM_CHECK_ARG(c->dispatched, "combine before any dispatch");
   DWM_CHECK_ARG(y_dtype == DWM_BF16 || y_dtype == DWM_F32, "y dtype must be bf16 or f32");
   DWM_CHECK_ARG(w_dtype == DWM_BF16 || w_dtype == DWM_F32, "weight dtype must be bf16 or f32");
   DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const ep::Params P = make_params(c);
+  const bool reduce = phases & DWM_EP_REDUCE;
   if (phases & DWM_EP_PUSH) {
     DWM_CHECK_ARG(y && moe::aligned16(y), "y must be a 16-byte aligned device pointer");
-    ep::ep_push_kernel<<<ep::XFER_CTAS, ep::XFER_THREADS, 0, s>>>(
-        P, static_cast<const uint8_t*>(y), y_dtype == DWM_F32 ? 4 : 2, status_ptr());
-    rc = check_cuda(cudaGetLastError(), "ep push launch");
-    if (rc) return rc;
+    if (y != c->base + c->L.outb) {
+      const int row_bytes = c->hidden * (y_dtype == DWM_F32 ? 4 : 2);
+      const unsigned g = moe::grid_for(c->cap * (row_bytes / 16), 256, 4);
+      ep::ep_stage_kernel<<<g, 256, 0, s>>>(P, static_cast<const uint4*>(y), row_bytes);
+      rc = check_cuda(cudaGetLastError(), "ep stage launch");
+      if (rc) return rc;
+    }
   }
-  if (phases & DWM_EP_REDUCE) {
+  if (reduce) {
     DWM_CHECK_ARG(P.T == 0 || (topk_weights && out), "NULL weights or out");
     DWM_CHECK_ARG(moe::aligned16(out), "out must be 16-byte aligned");
-    const uint64_t target = (uint64_t)c->epoch * c->world * ep::XFER_CTAS;
-    const unsigned grid = moe::grid_for((int64_t)P.T * (c->hidden / 8), 256, 4);
-    int* st = status_ptr();
-    const int32_t* revert = c->scratch;
-#define DWM_EP_REDUCE_CASE(XD, WD, OD)                                                      \
-  if (y_dtype == XD && w_dtype == WD && out_dtype == OD) {                                  \
-    ep::ep_reduce_kernel<XD, WD, OD><<<grid, 256, 0, s>>>(P, topk_weights, revert, out,     \
-                                                          target, st);                      \
-    return check_cuda(cudaGetLastError(), "ep reduce launch");                              \
   }
-    DWM_EP_REDUCE_CASE(DWM_BF16, DWM_BF16, DWM_BF16)
-    DWM_EP_REDUCE_CASE(DWM_BF16, DWM_F32, DWM_BF16)
-    DWM_EP_REDUCE_CASE(DWM_F32, DWM_BF16, DWM_BF16)
-    DWM_EP_REDUCE_CASE(DWM_F32, DWM_F32, DWM_BF16)
-    DWM_EP_REDUCE_CASE(DWM_BF16, DWM_BF16, DWM_F32)
-    DWM_EP_REDUCE_CASE(DWM_BF16, DWM_F32, DWM_F32)
-    DWM_EP_REDUCE_CASE(DWM_F32, DWM_BF16, DWM_F32)
-    DWM_EP_REDUCE_CASE(DWM_F32, DWM_F32, DWM_F32)
-#undef DWM_EP_REDUCE_CASE
+  // One thread per 8 elements of a token (no grid-stride loop).
+  const int64_t threads = (int64_t)P.T * (c->hidden / 8);
+  const unsigned grid =
+      reduce && threads > 0 ? (unsigned)((threads + ep::COMBINE_THREADS - 1) / ep::COMBINE_THREADS)
+                            : 1;
+  int* st = status_ptr();
+#define DWM_EP_COMBINE_CASE(XD, WD, OD)                                                        \
+  if (y_dtype == XD && w_dtype == WD && out_dtype == OD) {                                     \
+    ep::ep_combine_kernel<XD, WD, OD><<<grid, ep::COMBINE_THREADS, 0, s>>>(P, topk_weights,    \
+                                                                           out, phases, st);   \
+    return check_cuda(cudaGetLastError(), "ep combine launch");                                \
   }
+  DWM_EP_COMBINE_CASE(DWM_BF16, DWM_BF16, DWM_BF16)
+  DWM_EP_COMBINE_CASE(DWM_BF16, DWM_F32, DWM_BF16)
+  DWM_EP_COMBINE_CASE(DWM_F32, DWM_BF16, DWM_BF16)
+  DWM_EP_COMBINE_CASE(DWM_F32, DWM_F32, DWM_BF16)
+  DWM_EP_COMBINE_CASE(DWM_BF16, DWM_BF16, DWM_F32)
+  DWM_EP_COMBINE_CASE(DWM_BF16, DWM_F32, DWM_F32)
+  DWM_EP_COMBINE_CASE(DWM_F32, DWM_BF16, DWM_F32)
+  DWM_EP_COMBINE_CASE(DWM_F32, DWM_F32, DWM_F32)
+#undef DWM_EP_COMBINE_CASE
   return DWM_OK;
 }
 

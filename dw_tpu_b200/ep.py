@@ -7,10 +7,11 @@ of the rank's own experts (X0101:56-104, X0107:34-51), runs the grouped
 matmuls, then forms a masked f32 partial combine over all gathered tokens and
 reduce-scatters it (X0107:15-29, ``reduce_scatter_local`` KO:167-185). Here a
 rank instead stores each of its (token, k) rows straight into the expert
-owner's receive buffer, in the same receive order, and the owner stores each
-expert output straight back into the source's combine buffer, where the token
-owner forms the k-order combine (KC:14-21). One process per GPU; peers' buffers
-are mapped with CUDA IPC, exchanged once over ``torch.distributed``.
+owner's receive buffer, in the same receive order; the owner's grouped matmul
+writes into its output buffer, from which the token owner loads each (token,
+k) output and forms the k-order combine (KC:14-21). One kernel each way. One
+process per GPU; peers' buffers are mapped with CUDA IPC, exchanged once over
+``torch.distributed``.
 
 ``all_gather_local`` / ``reduce_scatter_local`` below are the NCCL
 comparison path (the reference's collectives on ``torch.distributed``).
@@ -42,8 +43,10 @@ class EPContext:
     buffer, the receive view and the receive group sizes.
 
     Rank ``rank`` of ``world`` owns experts [rank*E/world, (rank+1)*E/world).
-    ``recv`` is a bf16 [capacity, hidden] view of the receive buffer (owned by
-    the context: keep the context alive while it is used)."""
+    ``recv`` is a bf16 [capacity, hidden] view of the receive buffer and
+    ``output(dtype)`` a [capacity, hidden] view of the output buffer, where the
+    expert outputs should be written (both owned by the context: keep the
+    context alive while they are used)."""
 
     def __init__(self, rank: int, world: int, *, max_tokens: int, hidden: int, topk: int,
                  num_experts: int):
@@ -65,9 +68,22 @@ class EPContext:
         self.capacity = cap.value
         self.recv = torch.as_tensor(_DeviceArray(recv.value, (self.capacity, self.hidden), "<i2"),
                                     device=self.device).view(torch.bfloat16)
+        outb = ctypes.c_void_p()
+        L.check(lib.dwm_ep_output_buffer(ctx, ctypes.byref(outb), ctypes.byref(cap)),
+                "dwm_ep_output_buffer")
+        self._outb = outb.value
         self.recv_group_sizes = torch.zeros(self.local_experts, dtype=torch.int32,
                                             device=self.device)
         self.num_tokens = 0
+
+    def output(self, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """[capacity, hidden] view of the output buffer (bf16 or f32)."""
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("the output buffer holds bf16 or f32")
+        typestr = "<i2" if dtype == torch.bfloat16 else "<f4"
+        t = torch.as_tensor(_DeviceArray(self._outb, (self.capacity, self.hidden), typestr),
+                            device=self.device)
+        return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
 
     # -- wiring -------------------------------------------------------------
     def ipc_handle(self) -> bytes:
@@ -110,9 +126,10 @@ class EPContext:
     def combine(self, y: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None, *, phases: int = L.EP_PUSH | L.EP_REDUCE,
                 stream: int | None = None) -> torch.Tensor | None:
-        """y [capacity (or more), H] expert outputs in receive order (bf16 or
-        f32), topk_weights [T, topk] of this rank's dispatched tokens ->
-        out [T, H] (bf16 unless ``out`` says otherwise)."""
+        """y [rows, H] expert outputs in receive order (bf16 or f32; best the
+        ``output()`` view, else they are copied there first), topk_weights
+        [T, topk] of this rank's dispatched tokens -> out [T, H] (bf16 unless
+        ``out`` says otherwise)."""
         L.require_cuda(y, topk_weights)
         if y.dim() != 2 or y.shape[1] != self.hidden or not y.is_contiguous():
             raise ValueError(f"y must be a contiguous [rows, {self.hidden}] tensor")
@@ -259,13 +276,12 @@ class EPMoELayer:
         self.w16 = torch.empty((t, k), dtype=torch.bfloat16, device=dev)
         cap, i, h = ctx.capacity, weights.intermediate_size, weights.hidden_size
         self.h1 = torch.empty((cap, i), dtype=torch.bfloat16, device=dev)
-        self.y = torch.empty((cap, h), dtype=torch.float32 if f32_reduce else torch.bfloat16,
-                             device=dev)
+        self.y = ctx.output(torch.float32 if f32_reduce else torch.bfloat16)
         if expected_rows is None:  # uniform routing over all experts
             expected_rows = t * k / ctx.num_experts * ctx.world
         self.variant = gemm_variant(weights.layout, expected_rows)
 
-    kernels_per_forward = 8  # route, 3 dispatch, 2 gmm, 2 combine
+    kernels_per_forward = 5  # route, dispatch, 2 gmm, combine
 
     def _route(self, logits: torch.Tensor):
         t = logits.shape[0]

@@ -247,7 +247,9 @@ int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits
  * Replaces the GMM_EP exchange: all_gather_local + the per-shard stable sort
  * (KO:152-164, X0101:56-104, X0107:34-51) on the way in, and the masked f32
  * combine + reduce_scatter_local (X0107:15-29, KO:167-185) on the way out,
- * with one-shot kernels that store rows straight into peer GPUs' buffers.
+ * with one-shot kernels over peer memory: the dispatch stores rows straight
+ * into the expert owners' receive buffers, and the combine loads each
+ * token's expert outputs straight from the owners' output buffers.
  * One context per rank (one process per GPU); rank r owns experts
  * [r*E/world, (r+1)*E/world). Receive order on rank r: expert-major over its
  * experts, then (source rank, source token, k slot), i.e. the rows the
@@ -255,22 +257,25 @@ int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits
  * on rank r. The combine is the k-order f32 weighted sum of each token's
  * expert outputs from +0.0, rounded once (KC:14-21, the combine contract of
  * the single-device path). Every rank must make the same sequence of calls
- * with the same dtypes; calls on one context are stream-ordered and must not
- * overlap. Device-side waits give up after 2 s with DWM_DEV_TIMEOUT. */
+ * with the same dtypes, one combine per dispatch; calls on one context are
+ * stream-ordered and must not overlap. The exchange keeps its step counter
+ * in device memory, so the calls can be captured in a CUDA graph and
+ * replayed. Device-side waits give up after 2 s with DWM_DEV_TIMEOUT. */
 #define DWM_EP_HANDLE_BYTES 64 /* size of one rank's IPC handle */
 #define DWM_EP_COUNTS 1        /* dispatch phases (DWM_EP_ALL = all three) */
 #define DWM_EP_ROWS 2
 #define DWM_EP_WAIT 4
 #define DWM_EP_ALL 7
-#define DWM_EP_PUSH 1          /* combine phases */
-#define DWM_EP_REDUCE 2
+#define DWM_EP_PUSH 1          /* combine phases: make this rank's outputs readable, */
+#define DWM_EP_REDUCE 2        /* then reduce every own token */
 
 typedef struct dwm_ep dwm_ep;
 
-/* Allocate this rank's symmetric buffer (receive rows for world*max_tokens*
- * topk pairs, their tags, a combine buffer of max_tokens*topk rows, counts
- * and flags) on the current device. num_experts % world == 0,
- * num_experts <= 1024, hidden % 8 == 0, world <= 8. */
+/* Allocate this rank's symmetric buffer on the current device: receive rows
+ * (bf16) and expert outputs (4-byte capacity) for world*max_tokens*topk
+ * pairs, plus counts and flags. num_experts % world == 0,
+ * num_experts <= 1024, hidden % 8 == 0, world <= 8,
+ * world*max_tokens*topk <= 2^28. */
 int dwm_ep_create(int rank, int world, int max_tokens, int hidden, int topk, int num_experts,
                   dwm_ep** ctx);
 /* This rank's CUDA IPC handle (DWM_EP_HANDLE_BYTES bytes) for the exchange. */
@@ -285,17 +290,22 @@ int dwm_ep_connect_local(dwm_ep* ctx, dwm_ep* const* ranks);
 /* The receive buffer (bf16 [capacity_rows, hidden]) inside the symmetric
  * buffer; rows [0, sum(recv_group_sizes)) are valid after a dispatch. */
 int dwm_ep_recv_buffer(dwm_ep* ctx, void** recv, int64_t* capacity_rows);
+/* The output buffer inside the symmetric buffer: room for [capacity_rows,
+ * hidden] bf16 or f32 expert outputs in receive order. A grouped matmul that
+ * writes its output here saves the combine a copy. */
+int dwm_ep_output_buffer(dwm_ep* ctx, void** y, int64_t* capacity_rows);
 /* hidden bf16 [num_tokens, hidden], topk_ids int32 [num_tokens, topk] (ids
  * outside [0, num_experts) are reported and dropped) -> the receive buffer
  * and recv_group_sizes int32 [num_experts/world] (device). Counterpart of
  * all_gather_local + sort (X0101:56-104). */
 int dwm_ep_dispatch(dwm_ep* ctx, const void* hidden, const int32_t* topk_ids, int num_tokens,
                     int32_t* recv_group_sizes, int phases, void* stream);
-/* y [capacity_rows, hidden] (bf16 or f32: expert outputs of the received
- * rows, in receive order) -> out [num_tokens, hidden] of out_dtype, with
- * topk_weights [num_tokens, topk] (bf16 or f32) of the dispatch's tokens.
- * Counterpart of the masked combine + reduce_scatter_local (X0107:15-29,
- * KO:167-185) with the k-order contract of fast_combine (KC:14-21). */
+/* y [rows, hidden] (bf16 or f32: expert outputs of the received rows, in
+ * receive order; copied into the output buffer first unless y is that
+ * buffer) -> out [num_tokens, hidden] of out_dtype, with topk_weights
+ * [num_tokens, topk] (bf16 or f32) of the dispatch's tokens. Counterpart of
+ * the masked combine + reduce_scatter_local (X0107:15-29, KO:167-185) with
+ * the k-order contract of fast_combine (KC:14-21). */
 int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                    int w_dtype, void* out, int out_dtype, int phases, void* stream);
 /* Synchronise the context's device, unmap peers and free the buffers. */

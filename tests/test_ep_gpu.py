@@ -113,6 +113,68 @@ def test_ep_repeated_steps_and_f32_outputs(ep):
             c.close()
 
 
+def test_ep_graph_replay_advances_epoch(ep):
+    """The exchange captured once in a CUDA graph and replayed with new inputs
+    copied into the captured tensors: the epoch advances on the device, so
+    every replay matches the oracle (the count parity alternates too)."""
+    world, e, k, h, t = 4, 32, 4, 256, 24
+    from dw_tpu_b200 import _lib as L
+    ctxs = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        hs = [torch.empty((t, h), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+        ids = [torch.empty((t, k), dtype=torch.int32, device="cuda") for _ in range(world)]
+        ws = [torch.empty((t, k), dtype=torch.float32, device="cuda") for _ in range(world)]
+        ys = [torch.empty((c.capacity, h), dtype=torch.bfloat16, device="cuda") for c in ctxs]
+        outs = [torch.empty((t, h), dtype=torch.float32, device="cuda") for _ in range(world)]
+
+        def load(step):
+            hid, i, w = _inputs(world, t, e, k, h, seed=300 + step, dist="zipf")
+            for r in range(world):
+                hs[r].copy_(np_to_bf16(hid[r]))
+                ids[r].copy_(torch.from_numpy(i[r]))
+                ws[r].copy_(torch.from_numpy(w[r]))
+                ys[r].copy_(np_to_bf16(O.round_bf16(np.random.default_rng(step * 8 + r)
+                                                    .standard_normal((ctxs[r].capacity, h))
+                                                    .astype(np.float32))))
+            return hid, i, w
+
+        def step():
+            ep.emulated_dispatch(ctxs, hs, ids)
+            ep.emulated_combine(ctxs, ys, ws, outs)
+
+        def check(hid, i, w):
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            ref = O.ep_dispatch(hid, i, e)
+            yn = [bf16_to_np(y) for y in ys]
+            for r in range(world):
+                n = int(ref[r][1].sum())
+                assert np.array_equal(ctxs[r].recv_group_sizes.cpu().numpy(), ref[r][1])
+                assert np.array_equal(_bits(ctxs[r].recv[:n]), O.f32_to_bf16_bits(ref[r][0]))
+            want = O.ep_combine_korder([y[:int(g[1].sum())] for y, g in zip(yn, ref)],
+                                       [g[2] for g in ref], w, out_dtype="f32")
+            for r in range(world):
+                assert np.array_equal(outs[r].cpu().numpy(), want[r]), r
+
+        inputs = load(0)
+        step()                                             # eager step: epoch 1
+        check(*inputs)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        for s in range(1, 5):                              # replays: epochs 2..5
+            inputs = load(s)
+            g.replay()
+            check(*inputs)
+        del g
+    finally:
+        for c in ctxs:
+            c.close()
+
+
 def test_ep_invalid_ids_reported_and_dropped(ep):
     world, e, k, h = 2, 16, 2, 64
     ctxs = ep.create_local_contexts(world, max_tokens=8, hidden=h, topk=k, num_experts=e)
