@@ -41,18 +41,16 @@ namespace gmv {
 using namespace fp4;
 
 constexpr int MAX_GROUPS = 1024;
-constexpr int KSTAGE = 64;        // k per ring stage
-constexpr int CODE_BYTES = 2048;  // 4 column blocks x 4 k16 blocks x 32 words
-// A token row in shared memory: 72 k of bf16, of which the stage uses 64.
-// Rows 144 bytes (36 words) apart put the 8 rows of a B-fragment load in 8
-// different bank quads.
-constexpr int TOK_ROW = 144;
 constexpr uint32_t kBf16x2_2p64 = 0x5F805F80u;   // bf16 2^64, both halves
 constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 
 // Ring depth per warp (stages of 64 k) for 1 and 2 n8 token tiles.
 #ifndef DWM_GMV_STAGES1
 #define DWM_GMV_STAGES1 4
+#endif
+// Ring depth per warp for stages of 128 k (one n8 token tile).
+#ifndef DWM_GMV_STAGES1_K128
+#define DWM_GMV_STAGES1_K128 2
 #endif
 #ifndef DWM_GMV_STAGES2
 #define DWM_GMV_STAGES2 3
@@ -73,25 +71,40 @@ constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 #ifndef DWM_GMV_POST
 #define DWM_GMV_POST 0
 #endif
+// 1: one-tile tasks on k % 128 == 0 take stages of 128 k.
+#ifndef DWM_GMV_K128
+#define DWM_GMV_K128 1
+#endif
 // 1: waiting warps sleep between mbarrier polls (leaving issue slots to the
 // warps that have data).
 #ifndef DWM_GMV_BACKOFF
 #define DWM_GMV_BACKOFF 0
 #endif
 
-template <int SD, int NT>
+// KS: k per ring stage (64 or 128).
+template <int SD, int NT, int KS>
 struct Cfg {
+  static constexpr int KSTAGE = KS;
+  static constexpr int KS16 = KS / 16, KS32 = KS / 32;
+  // 4 column blocks x KS16 k16 blocks x 32 words; two TMA tiles of 2 blocks.
+  static constexpr int CODE_BYTES = 4 * KS16 * 128;
+  static constexpr int CODE_TILE = CODE_BYTES / 2;
+  // A token row in shared memory: KS + 8 k of bf16, of which the stage uses
+  // KS. Rows KS/2 + 4 words apart put the 8 rows of a B-fragment load in 8
+  // different bank quads.
+  static constexpr int TOK_ROW = 2 * KS + 16;
   static constexpr bool POST = SD == DWM_U8 && DWM_GMV_POST;  // E8M0: scale f32 partials
   static constexpr int DELTA = (SD == DWM_U8 && !POST) ? kDelta : 0;  // weight-side bias
   static constexpr int es = ScaleTraits<SD>::bytes;
-  static constexpr int S = NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2;
+  static constexpr int S =
+      KS == 128 ? DWM_GMV_STAGES1_K128 : (NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2);
   static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
   // Largest E8M0 code of the post-MMA path: the k-block factor 2^(c-65)
   // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
   static constexpr uint32_t POST_MAX = POST ? (RAW ? 192u : 254u) : 128u + kDelta;
-  static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of 72 k (64 used)
-  // 2 scale tiles of 2 k32 rows x 32 columns, each tile 128-byte aligned.
-  static constexpr int SC_TILE = 64 * es < 128 ? 128 : 64 * es;
+  static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of KS + 8 k (KS used)
+  // 2 scale tiles of KS32 k32 rows x 32 columns, each tile 128-byte aligned.
+  static constexpr int SC_TILE = KS32 * 32 * es < 128 ? 128 : KS32 * 32 * es;
   static constexpr int SC = 2 * SC_TILE;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
   static constexpr int WARPS = SD != DWM_F32 ? DWM_GMV_WARPS1 : 12;
@@ -100,7 +113,7 @@ struct Cfg {
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int BYTES = OFF_TASKS + (MAX_GROUPS + 1) * 4;
   static constexpr int ALLOC = BYTES + 128;  // slack for 128-byte alignment (TMA destinations)
-  static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * 64 * es;
+  static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * KS32 * 32 * es;
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
   static_assert(TOK % 128 == 0 && CODE_BYTES % 128 == 0 && SC % 128 == 0,
                 "TMA destinations need 128-byte alignment");
@@ -176,14 +189,15 @@ __device__ __forceinline__ void task_blocks(const Task& t, const Args& a, int& c
   }
 }
 
-template <int SD, int NT>
-__global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
+template <int SD, int NT, int KS>
+__global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     gmv_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
-  using C = Cfg<SD, NT>;
+  using C = Cfg<SD, NT, KS>;
   constexpr int S = C::S;
   constexpr int es = C::es;
+  constexpr int KSTAGE = C::KSTAGE, CODE_BYTES = C::CODE_BYTES, TOK_ROW = C::TOK_ROW;
   extern __shared__ uint8_t smem_raw[];
   // 1 KiB alignment by pointer arithmetic on the shared array itself, so the
   // compiler keeps every access below in the shared window (LDS, not LD).
@@ -284,7 +298,10 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
   const int gid = lane >> 2, tig = lane & 3;
   const int NSTAGE = a.k / KSTAGE;
   const int wstride = gridDim.x * C::WARPS;
-  const int first = blockIdx.x * C::WARPS + warp;
+  // Warps numbered SM-minor: the last, partial round of tasks lands on one
+  // warp per SM (which then runs with the SM nearly to itself) instead of
+  // on every warp of a few SMs.
+  const int first = warp * gridDim.x + blockIdx.x;
 
   // ---- producer state (lane 0): the next (task, stage) to fetch ----
   uint64_t pol_stream = 0, pol_keep = 0;
@@ -308,13 +325,13 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
     const int slot = (int)(issued % S);
     uint64_t* bar = &bars[slot];
     mbar_arrive_expect_tx(bar, C::TX);
-    const int xc = iss_st * 4 * 32;
+    const int xc = iss_st * C::KS16 * 32;
     tma_load_2d(tok_s + slot * C::TOK, &tm_lhs, bar, iss_st * KSTAGE, y_tok, pol_keep);
     tma_load_2d(code_s + slot * CODE_BYTES, &tm_codes, bar, xc, y_c0, pol_stream);
-    tma_load_2d(code_s + slot * CODE_BYTES + 1024, &tm_codes, bar, xc, y_c1, pol_stream);
+    tma_load_2d(code_s + slot * CODE_BYTES + C::CODE_TILE, &tm_codes, bar, xc, y_c1, pol_stream);
     uint8_t* sdst = sc_s + slot * C::SC;
-    tma_load_2d(sdst, &tm_scales, bar, x_s0, y_s + 2 * iss_st, pol_stream);
-    tma_load_2d(sdst + C::SC_TILE, &tm_scales, bar, x_s1, y_s + 2 * iss_st, pol_stream);
+    tma_load_2d(sdst, &tm_scales, bar, x_s0, y_s + C::KS32 * iss_st, pol_stream);
+    tma_load_2d(sdst + C::SC_TILE, &tm_scales, bar, x_s1, y_s + C::KS32 * iss_st, pol_stream);
     ++issued;
     if (++iss_st == NSTAGE) {
       iss_st = 0;
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
         constexpr bool PRE = decltype(pre_tag)::value;
         constexpr uint32_t M1 = C::POST ? kBf16x2_2p62 : pow2_126_minus_delta_x2<C::DELTA>();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // 32-deep k block inside the stage
+        for (int h = 0; h < C::KS32; ++h) {  // 32-deep k block inside the stage
           // Scales of the lane's columns: block i, column gid (+8 for hc =
           // 1); tile i/2 holds 2 rows (k32 blocks) of 32 columns.
           uint32_t wm[4][2];
@@ -414,7 +431,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t w =
-                  *reinterpret_cast<const uint32_t*>(code + i * 512 + kk * 128 + lane * 4);
+                  *reinterpret_cast<const uint32_t*>(code + i * (C::KS16 * 128) + kk * 128 + lane * 4);
               uint32_t af[4];
               tvals<true>(w, af);
               if constexpr (PRE) {
@@ -458,20 +475,27 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
         }
       };
       if constexpr (SD == DWM_U8) {
-        // One check per stage for the whole warp: lane l tests 4 of the 128
-        // scale bytes; the fast path needs every code in [1, POST_MAX].
-        const uint32_t v =
-            *reinterpret_cast<const uint32_t*>(sc + (lane >> 4) * C::SC_TILE + (lane & 15) * 4);
-        const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
-        uint32_t high_byte;
-        if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
-          high_byte = ((v & 0x7F7F7F7Fu) + 0x3F3F3F3Fu) & v & 0x80808080u;
-        else if constexpr (C::POST_MAX == 128u + kDelta)  // a byte >= 133: low 7 bits >= 5
-          high_byte = ((v & 0x7F7F7F7Fu) + (0x80808080u - (1u + kDelta) * 0x01010101u)) & v &
-                      0x80808080u;
-        else  // a byte == 255
-          high_byte = (~v - 0x01010101u) & v & 0x80808080u;
-        if (__any_sync(0xffffffffu, (zero_byte | high_byte) != 0u))
+        // One check per stage for the whole warp: each lane tests KS32 x 4 of
+        // the stage's scale bytes; the fast path needs every code in
+        // [1, POST_MAX].
+        uint32_t bad = 0;
+#pragma unroll
+        for (int q = 0; q < C::KS32; ++q) {
+          const int wi = q * 32 + lane;  // word of the stage's 2 x KS32 x 8 scale words
+          const int tile = wi / (C::KS32 * 8), off = wi - tile * (C::KS32 * 8);
+          const uint32_t v = *reinterpret_cast<const uint32_t*>(sc + tile * C::SC_TILE + off * 4);
+          const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
+          uint32_t high_byte;
+          if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
+            high_byte = ((v & 0x7F7F7F7Fu) + 0x3F3F3F3Fu) & v & 0x80808080u;
+          else if constexpr (C::POST_MAX == 128u + kDelta)  // a byte >= 133: low 7 bits >= 5
+            high_byte = ((v & 0x7F7F7F7Fu) + (0x80808080u - (1u + kDelta) * 0x01010101u)) & v &
+                        0x80808080u;
+          else  // a byte == 255
+            high_byte = (~v - 0x01010101u) & v & 0x80808080u;
+          bad |= zero_byte | high_byte;
+        }
+        if (__any_sync(0xffffffffu, bad != 0u))
           stage(std::true_type{});
         else
           stage(std::false_type{});
@@ -538,39 +562,39 @@ __global__ void __launch_bounds__(Cfg<SD, NT>::WARPS * 32, 1)
   }
 }
 
-template <int SD, int NT>
+template <int SD, int NT, int KS>
 int launch_impl(const void* lhs, const void* codes, const void* scales, const Args& a,
                 cudaStream_t stream) {
-  using C = Cfg<SD, NT>;
+  using C = Cfg<SD, NT, KS>;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
-  // lhs [m, k] bf16: box of 72 k (64 used) x 8*NT rows, rows 144 bytes apart.
+  // lhs [m, k] bf16: box of KS + 8 k (KS used) x 8*NT rows, rows TOK_ROW bytes apart.
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)a.k,
-                          (uint64_t)a.m, (uint64_t)a.k * 2, TOK_ROW / 2, 8 * NT,
+                          (uint64_t)a.m, (uint64_t)a.k * 2, C::TOK_ROW / 2, 8 * NT,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   // codes: rows = column blocks [n_local * n/16], each (k/16) x 32 words;
-  // box of 4 k16 blocks (128 words) x 2 column blocks.
+  // box of KS16 k16 blocks (KS16 x 32 words) x 2 column blocks.
   rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes, (uint64_t)(a.k / 16) * 32,
-                      (uint64_t)a.n_local * (a.n / 16), (uint64_t)(a.k / 16) * 128, 4 * 32, 2,
+                      (uint64_t)a.n_local * (a.n / 16), (uint64_t)(a.k / 16) * 128, C::KS16 * 32, 2,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  // scales [n_local * k/32, n]: box of 32 columns x 2 k32 rows.
+  // scales [n_local * k/32, n]: box of 32 columns x KS32 k32 rows.
   rc = encode_tmap_2d(&tm_scales, ScaleTraits<SD>::tma, scales, (uint64_t)a.n,
                       (uint64_t)a.n_local * (a.k / 32), (uint64_t)a.n * ScaleTraits<SD>::bytes, 32,
-                      2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                      C::KS32, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmv_fp4_kernel<SD, NT>,
+    rc = check_cuda(cudaFuncSetAttribute(gmv_fp4_kernel<SD, NT, KS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::ALLOC),
                     "gmv smem attribute");
     if (rc) return rc;
     attr_set[dev] = true;
   }
-  gmv_fp4_kernel<SD, NT><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(tm_lhs, tm_codes,
-                                                                         tm_scales, a);
+  gmv_fp4_kernel<SD, NT, KS><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(
+      tm_lhs, tm_codes, tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmv_fp4 launch");
 }
 
@@ -599,7 +623,13 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.quads = n / 64;
   a.status = status_ptr();
-#define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT>(lhs, codes, scales, a, stream)
+#define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
+  if (nt <= 1 && k % 128 == 0 && DWM_GMV_K128) {
+    if (scale_dtype == DWM_U8) return gmv::launch_impl<DWM_U8, 1, 128>(lhs, codes, scales, a, stream);
+    if (scale_dtype == DWM_BF16)
+      return gmv::launch_impl<DWM_BF16, 1, 128>(lhs, codes, scales, a, stream);
+    return gmv::launch_impl<DWM_F32, 1, 128>(lhs, codes, scales, a, stream);
+  }
   if (nt <= 1) {
     if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 1);
     if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 1);
