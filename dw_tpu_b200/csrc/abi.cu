@@ -64,9 +64,8 @@ int num_sms() {
   return n;
 }
 
-int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
-                   uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                   uint32_t box_outer, CUtensorMapSwizzle swz) {
+namespace {
+int resolve_encode() {
   if (!g_encode) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_encode) {
@@ -79,6 +78,38 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   }
+  return DWM_OK;
+}
+}  // namespace
+
+int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                   const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                   CUtensorMapSwizzle swz) {
+  if (rank < 1 || rank > 5) return set_error(DWM_ERR_INVALID, "tensor map rank %d", rank);
+  int rc = resolve_encode();
+  if (rc) return rc;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), d, st, b, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(DWM_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): rank %d", (int)r,
+                     rank);
+  return DWM_OK;
+}
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                   uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_outer, CUtensorMapSwizzle swz) {
+  int rc = resolve_encode();
+  if (rc) return rc;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};

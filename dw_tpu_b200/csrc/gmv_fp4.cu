@@ -26,11 +26,14 @@
 //     2^(c-65)); it measured the same speed.
 //   * bf16 / f32 scales (reference: cast to bf16, one bf16 multiply) are
 //     multiplied into the decoded weights, which reproduces that rounding.
-//   * each warp streams its own tasks through a private ring of S stages,
-//     filled by five 2-D TMA copies per stage (tokens, two code tiles, two
-//     scale tiles) issued by lane 0, with prefetch running ahead across task
-//     boundaries; token rows land 144 bytes apart (a 72-k box for 64 k of
-//     data) so B-fragment loads are bank-conflict free with plain offsets.
+//   * each warp streams its own tasks through a private ring of S stages of
+//     64 or 128 k, filled by three TMA copies per stage issued by lane 0
+//     (tokens; the task's 4 column blocks of codes as one 5-D box; their
+//     scales as one 3-D box), with prefetch running ahead across task
+//     boundaries; token rows land KS/2 + 4 words apart (a box KS + 8 k wide)
+//     so B-fragment loads are bank-conflict free with plain offsets.
+//   * warps are numbered SM-minor, so the last partial round of tasks is
+//     spread one warp per SM.
 #include <type_traits>
 
 #include "fp4_decode.cuh"
@@ -86,9 +89,8 @@ template <int SD, int NT, int KS>
 struct Cfg {
   static constexpr int KSTAGE = KS;
   static constexpr int KS16 = KS / 16, KS32 = KS / 32;
-  // 4 column blocks x KS16 k16 blocks x 32 words; two TMA tiles of 2 blocks.
+  // [2 halves][2 column blocks][KS16 k16 blocks][32 words], one TMA copy.
   static constexpr int CODE_BYTES = 4 * KS16 * 128;
-  static constexpr int CODE_TILE = CODE_BYTES / 2;
   // A token row in shared memory: KS + 8 k of bf16, of which the stage uses
   // KS. Rows KS/2 + 4 words apart put the 8 rows of a B-fragment load in 8
   // different bank quads.
@@ -103,9 +105,9 @@ struct Cfg {
   // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
   static constexpr uint32_t POST_MAX = POST ? (RAW ? 192u : 254u) : 128u + kDelta;
   static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of KS + 8 k (KS used)
-  // 2 scale tiles of KS32 k32 rows x 32 columns, each tile 128-byte aligned.
-  static constexpr int SC_TILE = KS32 * 32 * es < 128 ? 128 : KS32 * 32 * es;
-  static constexpr int SC = 2 * SC_TILE;
+  // Scales of a stage: [KS32 k32 rows][2 tiles][32 columns], one TMA copy.
+  static constexpr int SC_ROW = 64 * es;
+  static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
   static constexpr int WARPS = SD != DWM_F32 ? DWM_GMV_WARPS1 : 12;
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
@@ -115,7 +117,7 @@ struct Cfg {
   static constexpr int ALLOC = BYTES + 128;  // slack for 128-byte alignment (TMA destinations)
   static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * KS32 * 32 * es;
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
-  static_assert(TOK % 128 == 0 && CODE_BYTES % 128 == 0 && SC % 128 == 0,
+  static_assert(TOK % 128 == 0 && CODE_BYTES % 128 == 0 && SC % 128 == 0 && KS32 % 2 == 0,
                 "TMA destinations need 128-byte alignment");
 };
 
@@ -306,18 +308,20 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
   // ---- producer state (lane 0): the next (task, stage) to fetch ----
   uint64_t pol_stream = 0, pol_keep = 0;
   int iss_idx = first, iss_st = 0;
-  // Per-task TMA coordinates: token row, the two code-tile rows, the two
-  // scale-tile columns and the task's first scale row.
-  int y_tok = 0, y_c0 = 0, y_c1 = 0, x_s0 = 0, x_s1 = 0, y_s = 0;
+  // Per-task TMA coordinates: token row, the group and the two quad
+  // coordinates of the code map (the map's dimensions differ with the
+  // activation; the task's quad goes into one of them), the scale map's two
+  // column coordinates and the task's first scale row.
+  int y_tok = 0, c_g = 0, c_a = 0, c_b = 0, s_x = 0, s_y = 0, y_s = 0;
   auto set_task = [&](int idx) {
     const Task t = get_task<NT>(idx, row_start, task_prefix, a);
-    int cb0, cb1;
-    task_blocks(t, a, cb0, cb1);
+    const bool act = a.act != DWM_ACT_NONE;
     y_tok = t.row0;
-    y_c0 = t.g * (a.n / 16) + cb0;
-    y_c1 = t.g * (a.n / 16) + cb1;
-    x_s0 = 16 * cb0;
-    x_s1 = 16 * cb1;
+    c_g = t.g;
+    c_a = act ? t.quad : 0;
+    c_b = act ? 0 : t.quad;
+    s_x = act ? 32 * t.quad : 0;
+    s_y = act ? 0 : 2 * t.quad;
     y_s = t.g * (a.k / 32);
   };
   uint32_t issued = 0;  // stages issued so far (ring sequence)
@@ -327,11 +331,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     mbar_arrive_expect_tx(bar, C::TX);
     const int xc = iss_st * C::KS16 * 32;
     tma_load_2d(tok_s + slot * C::TOK, &tm_lhs, bar, iss_st * KSTAGE, y_tok, pol_keep);
-    tma_load_2d(code_s + slot * CODE_BYTES, &tm_codes, bar, xc, y_c0, pol_stream);
-    tma_load_2d(code_s + slot * CODE_BYTES + C::CODE_TILE, &tm_codes, bar, xc, y_c1, pol_stream);
-    uint8_t* sdst = sc_s + slot * C::SC;
-    tma_load_2d(sdst, &tm_scales, bar, x_s0, y_s + C::KS32 * iss_st, pol_stream);
-    tma_load_2d(sdst + C::SC_TILE, &tm_scales, bar, x_s1, y_s + C::KS32 * iss_st, pol_stream);
+    tma_load_5d(code_s + slot * CODE_BYTES, &tm_codes, bar, xc, 0, c_a, c_b, c_g, pol_stream);
+    tma_load_3d(sc_s + slot * C::SC, &tm_scales, bar, s_x, s_y, y_s + C::KS32 * iss_st,
+                pol_stream);
     ++issued;
     if (++iss_st == NSTAGE) {
       iss_st = 0;
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
               const uint8_t* p =
-                  sc + (i >> 1) * C::SC_TILE + (h * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
+                  sc + h * C::SC_ROW + ((i >> 1) * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
               uint32_t c;
               if constexpr (SD == DWM_U8)
                 c = *p;
@@ -475,15 +477,13 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
         }
       };
       if constexpr (SD == DWM_U8) {
-        // One check per stage for the whole warp: each lane tests KS32 x 4 of
-        // the stage's scale bytes; the fast path needs every code in
+        // One check per stage for the whole warp: each lane tests KS32 / 2 of
+        // the stage's KS32 x 16 scale words; the fast path needs every code in
         // [1, POST_MAX].
         uint32_t bad = 0;
 #pragma unroll
-        for (int q = 0; q < C::KS32; ++q) {
-          const int wi = q * 32 + lane;  // word of the stage's 2 x KS32 x 8 scale words
-          const int tile = wi / (C::KS32 * 8), off = wi - tile * (C::KS32 * 8);
-          const uint32_t v = *reinterpret_cast<const uint32_t*>(sc + tile * C::SC_TILE + off * 4);
+        for (int q = 0; q < C::KS32 / 2; ++q) {
+          const uint32_t v = *reinterpret_cast<const uint32_t*>(sc + (q * 32 + lane) * 4);
           const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
           uint32_t high_byte;
           if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
@@ -572,17 +572,36 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
                           (uint64_t)a.m, (uint64_t)a.k * 2, C::TOK_ROW / 2, 8 * NT,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  // codes: rows = column blocks [n_local * n/16], each (k/16) x 32 words;
-  // box of KS16 k16 blocks (KS16 x 32 words) x 2 column blocks.
-  rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes, (uint64_t)(a.k / 16) * 32,
-                      (uint64_t)a.n_local * (a.n / 16), (uint64_t)(a.k / 16) * 128, C::KS16 * 32, 2,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  // scales [n_local * k/32, n]: box of 32 columns x KS32 k32 rows.
-  rc = encode_tmap_2d(&tm_scales, ScaleTraits<SD>::tma, scales, (uint64_t)a.n,
-                      (uint64_t)a.n_local * (a.k / 32), (uint64_t)a.n * ScaleTraits<SD>::bytes, 32,
-                      C::KS32, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
+  // codes: one row of (k/16) x 32 words per column block, n/16 rows per
+  // group (R bytes each). One 5-D box holds the task's 4 column blocks as
+  // two pairs: with SwiGLU the gate pair (blocks 2q, 2q+1) and the up pair
+  // (n/32 blocks later); otherwise blocks 4q .. 4q+3. Dimensions: word,
+  // block in pair, then (quad, half) or (half, quad), group.
+  const bool act = a.act != DWM_ACT_NONE;
+  const uint64_t R = (uint64_t)(a.k / 16) * 128;
+  const uint64_t cw = (uint64_t)(a.k / 16) * 32, q64 = (uint64_t)a.n / 64, G = a.n_local;
+  {
+    const uint64_t dims[5] = {cw, 2, act ? q64 : 2, act ? 2 : q64, G};
+    const uint64_t strides[4] = {R, 2 * R, act ? (uint64_t)(a.n / 32) * R : 4 * R,
+                                 (uint64_t)(a.n / 16) * R};
+    const uint32_t box[5] = {(uint32_t)(C::KS16 * 32), 2, act ? 1u : 2u, act ? 2u : 1u, 1};
+    rc = encode_tmap_nd(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 5, codes, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  // scales [n_local * k/32, n]: one 3-D box of 32 columns x 2 tiles x KS32
+  // k32 rows; the tiles are the gate and up halves (n/2 apart) with SwiGLU,
+  // else two adjacent 32-column groups.
+  {
+    constexpr uint64_t es = ScaleTraits<SD>::bytes;
+    const uint64_t dims[3] = {act ? (uint64_t)a.n / 2 : 32, act ? 2 : (uint64_t)a.n / 32,
+                              G * (a.k / 32)};
+    const uint64_t strides[2] = {act ? (uint64_t)a.n / 2 * es : 32 * es, (uint64_t)a.n * es};
+    const uint32_t box[3] = {32, 2, (uint32_t)C::KS32};
+    rc = encode_tmap_nd(&tm_scales, ScaleTraits<SD>::tma, 3, scales, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
