@@ -75,6 +75,33 @@ __device__ __forceinline__ void tvals(uint32_t w, uint32_t (&t)[4]) {
   }
 }
 
+// The B200 decode with its constants held in registers. pin() hides a value
+// from the compiler, so the four constants are materialised once per kernel
+// and stay in registers, and each selector is one LOP3 ((w & m33) | c40).
+__device__ __forceinline__ uint32_t pin(uint32_t v) {
+  asm volatile("mov.b32 %0, %0;" : "+r"(v));
+  return v;
+}
+struct DecodeRegs {
+  uint32_t lut_lo, lut_hi, m33, c40;
+  __device__ __forceinline__ static DecodeRegs make() {
+    return {pin(kLutLo), pin(kLutHi), pin(0x33333333u), pin(0x40404040u)};
+  }
+};
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+  return d;
+}
+__device__ __forceinline__ void tvals_b200(uint32_t w, const DecodeRegs& R, uint32_t (&t)[4]) {
+  const uint32_t x = lop3_and_or(w, R.m33, R.c40);
+  const uint32_t y = lop3_and_or(w >> 2, R.m33, R.c40);
+  t[0] = prmt(R.lut_lo, R.lut_hi, x);
+  t[1] = prmt(R.lut_lo, R.lut_hi, y);
+  t[2] = prmt(R.lut_lo, R.lut_hi, x >> 16);
+  t[3] = prmt(R.lut_lo, R.lut_hi, y >> 16);
+}
+
 template <bool B200, bool TWO>
 __device__ __forceinline__ uint4 decode8(uint32_t w, const uint32_t (&m1)[4],
                                          const uint32_t (&m2)[4]) {

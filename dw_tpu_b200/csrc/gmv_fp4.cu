@@ -9,21 +9,22 @@
 // word per lane per 16x16 block, one PRMT per bf16 pair), token rows are the
 // n8 tiles, and nothing decoded touches shared or tensor memory.
 //
-// The kernel is bound by the integer (ALU) pipe, not by the MMA: at the HBM
-// roofline an SM must retire one 32-bit code word (8 weights) per lane every
-// ~23 issue slots, and the decode alone is 9 ALU operations (2 LOP3, 3 SHF,
-// 4 PRMT). So everything else per word is kept off the ALU:
-//   * E8M0 scales (the common case) go into the weights with one bf16
-//     multiply per fragment register on the FMA pipe: the decode yields
-//     value * 2^-126 (fp4_decode.cuh) and the multiplier is 2^(c-1-4), so
-//     the product value * scale * 2^-4 is exact, and the epilogue removes
-//     the 2^-4 in f32: the reference's bf16(value * scale) x bf16 token
-//     products (E0901:84-95) up to the f32 summation order. A stage holding
-//     code 0 (scale +0) or a code above 132 multiplies in two exact steps
-//     instead (one SWAR test per lane per stage decides). Built with
-//     DWM_GMV_POST=1 the scale is instead applied to the f32 partial of each
-//     32-deep k block after the MMA (tokens pre-scaled by 2^64, factor
-//     2^(c-65)); it measured the same speed.
+// The kernel is bound by instruction issue and the integer (ALU) pipe, not
+// by the MMA: at the HBM roofline an SM must retire one 32-bit code word (8
+// weights) per lane every ~22 issue slots, and the decode alone is 9 ALU
+// operations (2 LOP3, 3 SHF, 4 PRMT, with its four constants held in
+// registers). So everything else per word is kept off the ALU and small:
+//   * E8M0 scales (the common case) are applied to the f32 partial of each
+//     32-deep k block after the MMA: the decode yields value * 2^-126
+//     (fp4_decode.cuh), the tokens are pre-scaled by 2^64 (exact), and the
+//     partial is multiplied by 2^(c-65) (one mad builds the factor): the
+//     reference's bf16(value * scale) x bf16 token products (E0901:84-95),
+//     exactly, up to the f32 summation order. A stage holding code 0 (scale
+//     +0) or a code above 192 instead multiplies the decoded weights in two
+//     exact bf16 steps (one SWAR test per lane per stage decides). Built with
+//     DWM_GMV_POST=0 the fast path instead multiplies each decoded weight
+//     register by 2^(c-1-4) in bf16 (exact for codes 1..132; the epilogue
+//     removes the 2^-4), about 3% slower.
 //   * bf16 / f32 scales (reference: cast to bf16, one bf16 multiply) are
 //     multiplied into the decoded weights, which reproduces that rounding.
 //   * each warp streams its own tasks through a private ring of S stages of
@@ -72,7 +73,7 @@ constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 // 0 = multiply each decoded weight register by 2^(c-1-4) in bf16 (exact for
 // codes 1..132; the 2^-4 is removed in the epilogue).
 #ifndef DWM_GMV_POST
-#define DWM_GMV_POST 0
+#define DWM_GMV_POST 1
 #endif
 // 1: one-tile tasks on k % 128 == 0 take stages of 128 k.
 #ifndef DWM_GMV_K128
@@ -299,6 +300,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
 
   const int gid = lane >> 2, tig = lane & 3;
   const int NSTAGE = a.k / KSTAGE;
+  const DecodeRegs dregs = DecodeRegs::make();
+  // 2^(c-1-delta) for E8M0 code c, both bf16 halves: c * 0x00800080 + bias.
+  const uint32_t wm_bias = pin((126u - C::DELTA) * 0x00800080u);
   const int wstride = gridDim.x * C::WARPS;
   // Warps numbered SM-minor: the last, partial round of tasks lands on one
   // warp per SM (which then runs with the SM nearly to itself) instead of
@@ -404,10 +408,12 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
                 wm[i][hc] = SD == DWM_U8 ? (c << 7) * 0x10001u  // bf16 2^(c-127), 0 -> +0
                                          : c * 0x10001u;        // the bf16 scale
               } else if constexpr (!C::POST) {
-                wm[i][hc] = ((c + 126u - C::DELTA) << 7) * 0x10001u;  // 2^(c-1-delta)
+                asm("mad.lo.u32 %0, %1, 8388736, %2;"  // c * 0x00800080 + bias
+                    : "=r"(wm[i][hc])
+                    : "r"(c), "r"(wm_bias));
               } else {
-                post[i][hc] = C::RAW ? __uint_as_float((c + 62u) << 23)  // 2^(c-65)
-                                     : __uint_as_float(c << 23);         // 2^(c-127)
+                post[i][hc] = C::RAW ? __uint_as_float(c * 0x00800000u + (62u << 23))  // 2^(c-65)
+                                     : __uint_as_float(c << 23);                       // 2^(c-127)
               }
             }
           float part[4][NT][4];
@@ -435,7 +441,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
               const uint32_t w =
                   *reinterpret_cast<const uint32_t*>(code + i * (C::KS16 * 128) + kk * 128 + lane * 4);
               uint32_t af[4];
-              tvals<true>(w, af);
+              tvals_b200(w, dregs, af);
               if constexpr (PRE) {
                 af[0] = hmul2_bf16(hmul2_bf16(af[0], M1), wm[i][0]);
                 af[1] = hmul2_bf16(hmul2_bf16(af[1], M1), wm[i][1]);
