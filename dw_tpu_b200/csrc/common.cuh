@@ -153,15 +153,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // false so the kernel can wind down instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// kBackoff: sleep between polls (for waits that span a whole tile, so the
-// waiting warps leave issue slots to the decode warps).
-template <bool kBackoff = false>
+// kSleepNs: sleep between polls, so that waiting warps leave issue slots to
+// the working ones (each poll is a handful of warp instructions).
+template <int kSleepNs = 0>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (kBackoff) __nanosleep(256);
+    if (kSleepNs > 0) __nanosleep(kSleepNs);
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;

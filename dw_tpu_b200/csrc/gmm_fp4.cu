@@ -66,6 +66,22 @@ constexpr int C_SUB_BYTES = BK * (BW / 2);        // 4 KiB of packed nibbles per
 constexpr int C_STAGE = NSUB * C_SUB_BYTES;       // TMA writes 128-byte aligned addresses
 static_assert(C_SUB_BYTES % 128 == 0, "TMA needs 128 B alignment");
 
+// Sleep (ns) between mbarrier polls per role: the epilogue waits a whole
+// tile, the producers and the decode warps wait for ring slots, the MMA
+// issuer waits for decoded stages (latency-critical).
+#ifndef DWM_GMM_EPI_SLEEP
+#define DWM_GMM_EPI_SLEEP 256
+#endif
+#ifndef DWM_GMM_PROD_SLEEP
+#define DWM_GMM_PROD_SLEEP 0
+#endif
+#ifndef DWM_GMM_DEC_SLEEP
+#define DWM_GMM_DEC_SLEEP 0
+#endif
+#ifndef DWM_GMM_MMA_SLEEP
+#define DWM_GMM_MMA_SLEEP 0
+#endif
+
 // Pipeline depths (build-time tunables).
 #ifndef DWM_GMM_TS
 #define DWM_GMM_TS 3
@@ -308,7 +324,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
       const int buf = it % NBUF;
       const uint32_t ph = (it / NBUF) & 1;
-      const bool got = mbar_wait<true>(&acc_full[buf], ph, abort_flag, a.status);
+      const bool got = mbar_wait<DWM_GMM_EPI_SLEEP>(&acc_full[buf], ph, abort_flag, a.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NSUB * BT);
@@ -378,7 +394,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           col[1] = half + t.n_idx * BW;
         }
         for (int kk = 0; kk < KT; ++kk) {
-          if (!mbar_wait(&cs_empty[cs], cs_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
+          if (!mbar_wait<DWM_GMM_PROD_SLEEP>(&cs_empty[cs], cs_ph ^ 1, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(&cs_full[cs], cs_bytes);
           cs_armed |= 1u << cs;
           cs_par = (cs_par & ~(1u << cs)) | (cs_ph << cs);
@@ -418,7 +437,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int kspan = token_span<BT>(nb, nbp);
         for (int k0 = 0; k0 < KT; k0 += kspan) {
           const int kn = min(kspan, KT - k0);
-          if (!mbar_wait(&tk_empty[ts], ts_ph ^ 1, abort_flag, a.status)) { ok = false; break; }
+          if (!mbar_wait<DWM_GMM_PROD_SLEEP>(&tk_empty[ts], ts_ph ^ 1, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(&tk_full[ts], kn * nb * T_BOX_BYTES);
           ts_armed |= 1u << ts;
           ts_par = (ts_par & ~(1u << ts)) | (ts_ph << ts);
@@ -449,16 +471,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t idesc = idesc_bf16(128, nmma, /*a_mn=*/VAR == kMN, /*b_mn=*/false);
         const int buf = it % NBUF;
         const uint32_t ph = (it / NBUF) & 1;
-        if (!mbar_wait(&acc_empty[buf], ph ^ 1, abort_flag, a.status)) break;
+        if (!mbar_wait<DWM_GMM_MMA_SLEEP>(&acc_empty[buf], ph ^ 1, abort_flag, a.status)) break;
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * NSUB * BT);
         for (int kk = 0; kk < KT; ++kk) {
           const int kl = kk % kspan;
-          if (kl == 0 && !mbar_wait(&tk_full[ts], ts_ph, abort_flag, a.status)) {
+          if (kl == 0 && !mbar_wait<DWM_GMM_MMA_SLEEP>(&tk_full[ts], ts_ph, abort_flag, a.status)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&a_full[as], as_ph, abort_flag, a.status)) {
+          if (!mbar_wait<DWM_GMM_MMA_SLEEP>(&a_full[as], as_ph, abort_flag, a.status)) {
             ok = false;
             break;
           }
@@ -529,8 +551,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t cs_ph = (step / CS) & 1;
           const int as = (int)(step % AS);
           const uint32_t as_ph = (step / AS) & 1;
-          bool got = mbar_wait(&cs_full[cs], cs_ph, abort_flag, a.status);
-          got = got && mbar_wait(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
+          bool got = mbar_wait<DWM_GMM_DEC_SLEEP>(&cs_full[cs], cs_ph, abort_flag, a.status);
+          got = got && mbar_wait<DWM_GMM_DEC_SLEEP>(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
           if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
@@ -585,8 +607,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t cs_ph = (step / CS) & 1;
           const int as = (int)(step % AS);
           const uint32_t as_ph = (step / AS) & 1;
-          bool got = mbar_wait(&cs_full[cs], cs_ph, abort_flag, a.status);
-          got = got && mbar_wait(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
+          bool got = mbar_wait<DWM_GMM_DEC_SLEEP>(&cs_full[cs], cs_ph, abort_flag, a.status);
+          got = got && mbar_wait<DWM_GMM_DEC_SLEEP>(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
           if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;

@@ -79,8 +79,8 @@ constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 #ifndef DWM_GMV_K128
 #define DWM_GMV_K128 1
 #endif
-// 1: waiting warps sleep between mbarrier polls (leaving issue slots to the
-// warps that have data).
+// Sleep (ns) of a waiting warp between mbarrier polls (leaving issue slots to
+// the warps that have data); 0 = poll.
 #ifndef DWM_GMV_BACKOFF
 #define DWM_GMV_BACKOFF 0
 #endif
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     for (int st = 0; st < NSTAGE; ++st, ++seq) {
       const int slot = (int)(seq % S);
       const bool got =
-          mbar_wait<DWM_GMV_BACKOFF != 0>(&bars[slot], (seq / S) & 1, nullptr, a.status);
+          mbar_wait<DWM_GMV_BACKOFF>(&bars[slot], (seq / S) & 1, nullptr, a.status);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
