@@ -22,7 +22,8 @@ from .e8m0_scale import e8m0_decode, e8m0_encode  # noqa: E402
 from .fused_moe import FP4MoEWeights, MoELayer, fused_moe_func  # noqa: E402
 from .gmm_v2 import (b200_to_e2m1, codes_to_e2m1, decode_codes, e2m1_to_codes,  # noqa: E402
                      fp4_weight_to_codes, gmm, gmm_v2, gmm_wrapper, needs_fp4_emulation)
-from .moe_fast_combine import combine_pallas, combine_xla, fast_combine  # noqa: E402
+from .moe_fast_combine import (combine_pallas, combine_shared, combine_xla,  # noqa: E402
+                               fast_combine)
 from .moe_fast_dispatch import (dispatch_gather, dispatch_gather_pallas,  # noqa: E402
                                 fast_dispatch_gather, moe_permute, sorted_token_indices)
 from .routing import dedupe_topk, route_hash, route_topk  # noqa: E402
@@ -31,6 +32,6 @@ __all__ = [
     "gmm_v2", "gmm", "gmm_wrapper", "e2m1_to_codes", "codes_to_e2m1", "decode_codes",
     "fp4_weight_to_codes", "b200_to_e2m1", "needs_fp4_emulation", "fast_dispatch_gather",
     "sorted_token_indices", "moe_permute", "dispatch_gather", "dispatch_gather_pallas",
-    "fast_combine", "combine_xla", "combine_pallas", "e8m0_encode", "e8m0_decode",
+    "fast_combine", "combine_xla", "combine_pallas", "combine_shared", "e8m0_encode", "e8m0_decode",
     "route_topk", "route_hash", "dedupe_topk", "MoELayer", "FP4MoEWeights", "fused_moe_func",
 ]

@@ -77,6 +77,7 @@ SIGNATURES = {
     "dwm_permute": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "dwm_dispatch_gather": ([_P, _I, _I, _P, _I64, _P, _P], _I),
     "dwm_combine": ([_P, _I, _I64, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
+    "dwm_combine_shared": ([_P, _I, _I64, _P, _P, _I, _I, _I, _I, _P, _I, _F, _I, _P, _I, _P], _I),
     "dwm_moe_layer_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
     "dwm_moe_layer_fp4": ([_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I,
                            _F, _I, _P, _SZ, _P, _P], _I),
@@ -90,6 +91,7 @@ SIGNATURES = {
     "dwm_ep_output_buffer": ([_P, _c.POINTER(_P), _c.POINTER(_I64)], _I),
     "dwm_ep_dispatch": ([_P, _P, _P, _I, _P, _I, _P], _I),
     "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
+    "dwm_ep_combine_shared": ([_P, _P, _I, _P, _I, _P, _I, _F, _I, _P, _I, _I, _P], _I),
     "dwm_ep_destroy": ([_P], _I),
 }
 

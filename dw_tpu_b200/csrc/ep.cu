@@ -368,7 +368,7 @@ __global__ void ep_stage_kernel(const __grid_constant__ Params P, const uint4* _
 template <int XD, int WD, int OD>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     ep_combine_kernel(const __grid_constant__ Params P, const void* __restrict__ w,
-                      void* __restrict__ out, int ph, int* status) {
+                      void* __restrict__ out, const moe::SharedAdd sa, int ph, int* status) {
   constexpr int KB = 8;
   constexpr int ROW_MASK = (1 << ROW_BITS) - 1;
   __shared__ uint32_t s_epoch;
@@ -423,7 +423,10 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
         if (code[q] >= 0)
           moe::mul_add8(acc, v[q], moe::load_weight<WD>(w, t * P.topk + k0 + q));
     }
-    if (mine && s_ok) moe::store8<OD>(out, t * P.H + (int64_t)c * 8, acc);
+    if (mine && s_ok) {
+      moe::shared_add8(acc, sa, t * P.H + (int64_t)c * 8);
+      moe::store8<OD>(out, t * P.H + (int64_t)c * 8, acc);
+    }
   }
   __syncthreads();
   if (tid == 0 && atomicAdd(&P.ctl[CTL_DONE], 1u) == gridDim.x - 1) {
@@ -634,8 +637,10 @@ extern "C" int dwm_ep_dispatch(dwm_ep* c, const void* hidden, const int32_t* top
   return check_cuda(cudaGetLastError(), "ep dispatch launch");
 }
 
-extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void* topk_weights,
-                              int w_dtype, void* out, int out_dtype, int phases, void* stream) {
+extern "C" int dwm_ep_combine_shared(dwm_ep* c, const void* y, int y_dtype,
+                                     const void* topk_weights, int w_dtype, const void* shared,
+                                     int shared_dtype, float routed_scale, int mid_dtype,
+                                     void* out, int out_dtype, int phases, void* stream) {
   int rc = check_ctx(c);
   if (rc) return rc;
   DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_PUSH | DWM_EP_REDUCE), "phases=%d", phases);
@@ -659,7 +664,13 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
   if (reduce) {
     DWM_CHECK_ARG(P.T == 0 || (topk_weights && out), "NULL weights or out");
     DWM_CHECK_ARG(moe::aligned16(out), "out must be 16-byte aligned");
+    DWM_CHECK_ARG(shared == nullptr || ((shared_dtype == DWM_BF16 || shared_dtype == DWM_F32) &&
+                                        (mid_dtype == DWM_BF16 || mid_dtype == DWM_F32) &&
+                                        moe::aligned16(shared)),
+                  "shared partial: bf16/f32, 16-byte aligned; mid dtype bf16/f32");
   }
+  const moe::SharedAdd sa{reduce ? shared : nullptr, shared_dtype == DWM_F32, routed_scale,
+                          mid_dtype == DWM_BF16};
   // One thread per 8 elements of a token (no grid-stride loop).
   const int64_t threads = (int64_t)P.T * (c->hidden / 8);
   const unsigned grid =
@@ -669,7 +680,7 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
 #define DWM_EP_COMBINE_CASE(XD, WD, OD)                                                        \
   if (y_dtype == XD && w_dtype == WD && out_dtype == OD) {                                     \
     ep::ep_combine_kernel<XD, WD, OD><<<grid, ep::COMBINE_THREADS, 0, s>>>(P, topk_weights,    \
-                                                                           out, phases, st);   \
+                                                                           out, sa, phases, st); \
     return check_cuda(cudaGetLastError(), "ep combine launch");                                \
   }
   DWM_EP_COMBINE_CASE(DWM_BF16, DWM_BF16, DWM_BF16)
@@ -682,6 +693,12 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
   DWM_EP_COMBINE_CASE(DWM_F32, DWM_F32, DWM_F32)
 #undef DWM_EP_COMBINE_CASE
   return DWM_OK;
+}
+
+extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void* topk_weights,
+                              int w_dtype, void* out, int out_dtype, int phases, void* stream) {
+  return dwm_ep_combine_shared(c, y, y_dtype, topk_weights, w_dtype, nullptr, DWM_F32, 1.0f,
+                               DWM_BF16, out, out_dtype, phases, stream);
 }
 
 extern "C" int dwm_ep_destroy(dwm_ep* c) {

@@ -188,6 +188,33 @@ __device__ __forceinline__ void store8(void* out, int64_t off, const float (&acc
   }
 }
 
+// The shared expert summed into the routed combine (MOE_SHARED_EXPERT_TP,
+// X0104:80-87 of the patch): out = f32(mid(routed)) * scale + shared, where
+// mid rounds the routed k-order sum to bf16 (the combine's own output dtype)
+// or keeps it f32 (MOE_F32_REDUCE); each step is rounded to f32 on its own.
+// p == nullptr: no shared expert (the plain combine).
+struct SharedAdd {
+  const void* p;
+  int f32;       // shared partial dtype: 1 = f32, 0 = bf16
+  float scale;   // routed_scale
+  int mid_bf16;  // 1: round the routed sum to bf16 first
+};
+
+__device__ __forceinline__ void shared_add8(float (&acc)[8], const SharedAdd& s, int64_t off) {
+  if (s.p == nullptr) return;
+  float sh[8];
+  if (s.f32)
+    load8<DWM_F32>(s.p, off, sh);
+  else
+    load8<DWM_BF16>(s.p, off, sh);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float v = acc[q];
+    if (s.mid_bf16) v = __uint_as_float(f32_to_bf16_bits(v) << 16);
+    acc[q] = __fadd_rn(__fmul_rn(v, s.scale), sh[q]);
+  }
+}
+
 inline unsigned grid_for(int64_t work, int threads, int per_sm = 16) {
   const int64_t b = (work + threads - 1) / threads;
   const int64_t cap = (int64_t)num_sms() * per_sm;

@@ -58,7 +58,8 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ hidden, int t, int6
 template <int XD, int WD, int OD>
 __global__ void combine_kernel(const void* __restrict__ x, int64_t x_rows,
                                const int32_t* __restrict__ idx, const void* __restrict__ w,
-                               int t, int h, int topk, void* __restrict__ out, int* status) {
+                               int t, int h, int topk, void* __restrict__ out,
+                               const moe::SharedAdd sa, int* status) {
   const int h8 = h / 8;
   const int64_t total = (int64_t)t * h8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -79,6 +80,7 @@ __global__ void combine_kernel(const void* __restrict__ x, int64_t x_rows,
       load8<XD>(x, r * h + (int64_t)c * 8, v);
       mul_add8(acc, v, wk);
     }
+    moe::shared_add8(acc, sa, tt * h + (int64_t)c * 8);
     store8<OD>(out, tt * h + (int64_t)c * 8, acc);
   }
 }
@@ -143,9 +145,11 @@ extern "C" int dwm_dispatch_gather(const void* hidden, int t, int h,
   return check_cuda(cudaGetLastError(), "gather launch");
 }
 
-extern "C" int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int32_t* indices,
-                           const void* w, int w_dtype, int t, int h, int topk, void* out,
-                           int out_dtype, void* stream) {
+extern "C" int dwm_combine_shared(const void* x, int x_dtype, int64_t x_rows,
+                                  const int32_t* indices, const void* w, int w_dtype, int t, int h,
+                                  int topk, const void* shared, int shared_dtype,
+                                  float routed_scale, int mid_dtype, void* out, int out_dtype,
+                                  void* stream) {
   DWM_CHECK_ARG(t >= 0 && h > 0 && topk >= 1 && x_rows >= 0, "bad shape");
   DWM_CHECK_ARG(h % 8 == 0, "h=%d must be a multiple of 8", h);
   DWM_CHECK_ARG(x_dtype == DWM_BF16 || x_dtype == DWM_F32, "x dtype must be bf16 or f32");
@@ -153,14 +157,19 @@ extern "C" int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int
   DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
   DWM_CHECK_ARG(t == 0 || (x && indices && w && out), "NULL pointer");
   DWM_CHECK_ARG(moe::aligned16(x) && moe::aligned16(out), "pointers must be 16-byte aligned");
+  DWM_CHECK_ARG(shared == nullptr || ((shared_dtype == DWM_BF16 || shared_dtype == DWM_F32) &&
+                                      (mid_dtype == DWM_BF16 || mid_dtype == DWM_F32) &&
+                                      moe::aligned16(shared)),
+                "shared partial: bf16/f32, 16-byte aligned; mid dtype bf16/f32");
   if (t == 0) return DWM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned grid = moe::grid_for((int64_t)t * (h / 8), 256);
+  const moe::SharedAdd sa{shared, shared_dtype == DWM_F32, routed_scale, mid_dtype == DWM_BF16};
   int* st = status_ptr();
 #define DWM_COMBINE(XD, WD, OD)                                                             \
   if (x_dtype == XD && w_dtype == WD && out_dtype == OD) {                                  \
     perm::combine_kernel<XD, WD, OD><<<grid, 256, 0, s>>>(x, x_rows, indices, w, t, h, topk, \
-                                                          out, st);                          \
+                                                          out, sa, st);                      \
     return check_cuda(cudaGetLastError(), "combine launch");                                \
   }
   DWM_COMBINE(DWM_BF16, DWM_BF16, DWM_BF16)
@@ -173,4 +182,11 @@ extern "C" int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int
   DWM_COMBINE(DWM_F32, DWM_F32, DWM_F32)
 #undef DWM_COMBINE
   return set_error(DWM_ERR_UNSUPPORTED, "combine dtype combination");
+}
+
+extern "C" int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int32_t* indices,
+                           const void* w, int w_dtype, int t, int h, int topk, void* out,
+                           int out_dtype, void* stream) {
+  return dwm_combine_shared(x, x_dtype, x_rows, indices, w, w_dtype, t, h, topk, nullptr, DWM_F32,
+                            1.0f, DWM_BF16, out, out_dtype, stream);
 }

@@ -125,11 +125,13 @@ class EPContext:
 
     def combine(self, y: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None, *, phases: int = L.EP_PUSH | L.EP_REDUCE,
-                stream: int | None = None) -> torch.Tensor | None:
+                stream: int | None = None, shared: torch.Tensor | None = None,
+                routed_scale: float = 1.0, f32_reduce: bool = False) -> torch.Tensor | None:
         """y [rows, H] expert outputs in receive order (bf16 or f32; best the
         ``output()`` view, else they are copied there first), topk_weights
         [T, topk] of this rank's dispatched tokens -> out [T, H] (bf16 unless
-        ``out`` says otherwise)."""
+        ``out`` says otherwise). ``shared`` [T, H] (bf16/f32): the shared
+        expert summed in as ``combine_shared`` does (X0104:80-87)."""
         L.require_cuda(y, topk_weights)
         if y.dim() != 2 or y.shape[1] != self.hidden or not y.is_contiguous():
             raise ValueError(f"y must be a contiguous [rows, {self.hidden}] tensor")
@@ -138,13 +140,19 @@ class EPContext:
             raise ValueError(f"topk_weights must be [{t}, {self.topk}]")
         if out is None and phases & L.EP_REDUCE:
             out = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=y.device)
-        L.check(L.lib().dwm_ep_combine(self._ctx, y.data_ptr(), L.dtype_code(y.dtype),
-                                       topk_weights.contiguous().data_ptr(),
-                                       L.dtype_code(topk_weights.dtype),
-                                       L.ptr(out), L.dtype_code(out.dtype) if out is not None
-                                       else L.BF16, phases,
-                                       L.stream_ptr() if stream is None else stream),
-                "dwm_ep_combine")
+        if shared is not None:
+            L.require_cuda(shared)
+            if shared.shape != (t, self.hidden) or shared.dtype not in (torch.bfloat16,
+                                                                       torch.float32):
+                raise ValueError(f"shared must be bf16/f32 [{t}, {self.hidden}]")
+            shared = shared.contiguous()
+        L.check(L.lib().dwm_ep_combine_shared(
+            self._ctx, y.data_ptr(), L.dtype_code(y.dtype), topk_weights.contiguous().data_ptr(),
+            L.dtype_code(topk_weights.dtype), L.ptr(shared),
+            L.dtype_code(shared.dtype) if shared is not None else L.F32, float(routed_scale),
+            L.F32 if f32_reduce else L.BF16, L.ptr(out),
+            L.dtype_code(out.dtype) if out is not None else L.BF16, phases,
+            L.stream_ptr() if stream is None else stream), "dwm_ep_combine_shared")
         return out
 
     def close(self) -> None:

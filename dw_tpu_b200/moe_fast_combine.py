@@ -49,3 +49,27 @@ def fast_combine(x: torch.Tensor, indices: torch.Tensor, topk_weights: torch.Ten
     if mode not in (1, 2):
         raise ValueError(f"MOE_FAST_COMBINE mode must be 1 or 2, got {mode}")
     return _combine(x, indices, topk_weights, topk, out_dtype)
+
+
+def combine_shared(x: torch.Tensor, indices: torch.Tensor, topk_weights: torch.Tensor, topk: int,
+                   shared_partial: torch.Tensor, routed_scale: float = 1.0,
+                   f32_reduce: bool = False, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """The combine with the shared expert's output (or this shard's partial
+    of it) summed in, as MOE_SHARED_EXPERT_TP does before its reduce
+    (X0104:80-87): out = dtype(f32(routed) * routed_scale + shared_partial),
+    the routed k-order sum first rounded to bf16 unless ``f32_reduce``
+    (MOE_F32_REDUCE keeps it f32)."""
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"out_dtype {out_dtype} not supported")
+    w = topk_weights
+    if w.dtype not in (torch.bfloat16, torch.float32):
+        w = w.to(torch.float32)
+    sh = shared_partial
+    if sh.dtype not in (torch.bfloat16, torch.float32):
+        sh = sh.to(torch.float32)
+    t = w.shape[0]
+    out = torch.empty((t, x.shape[1]), dtype=out_dtype, device=x.device)
+    return ops.combine_shared_out(x.contiguous(), indices.to(torch.int32).reshape(-1),
+                                  w.contiguous(), int(topk), sh.contiguous(), out,
+                                  routed_scale=routed_scale,
+                                  mid_dtype=torch.float32 if f32_reduce else torch.bfloat16)

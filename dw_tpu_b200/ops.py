@@ -273,6 +273,34 @@ def combine_out(x, indices, topk_weights, topk, out, stream=None):
     return out
 
 
+def combine_shared_out(x, indices, topk_weights, topk, shared, out, *, routed_scale=1.0,
+                       mid_dtype=torch.bfloat16, stream=None):
+    """out <- combine (as ``combine_out``) with the shared expert summed in:
+    out = round(f32(mid(routed)) * routed_scale + shared) (dwm_combine_shared,
+    MOE_SHARED_EXPERT_TP X0104:80-87)."""
+    L.require_cuda(x, indices, topk_weights, out, shared)
+    if x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous [rows, h] tensor")
+    t = topk_weights.shape[0]
+    h = x.shape[1]
+    if topk_weights.shape != (t, topk) or not topk_weights.is_contiguous():
+        raise ValueError("topk_weights must be contiguous [t, topk]")
+    if indices.numel() != t * topk or indices.dtype != torch.int32:
+        raise ValueError("indices must be int32 [t * topk]")
+    if out.shape != (t, h) or shared.shape != (t, h) or not shared.is_contiguous():
+        raise ValueError("out and shared must be [t, h] (shared contiguous)")
+    if mid_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("mid_dtype must be bf16 or f32")
+    rc = L.lib().dwm_combine_shared(
+        x.data_ptr(), L.dtype_code(x.dtype), x.shape[0], indices.data_ptr(),
+        topk_weights.data_ptr(), L.dtype_code(topk_weights.dtype), t, h, int(topk),
+        shared.data_ptr(), L.dtype_code(shared.dtype), float(routed_scale),
+        L.dtype_code(mid_dtype), out.data_ptr(), L.dtype_code(out.dtype),
+        L.stream_ptr() if stream is None else stream)
+    L.check(rc, "combine_shared")
+    return out
+
+
 def moe_layer_workspace_bytes(num_tokens, hidden, inter, topk, num_experts, y_f32=False):
     return int(L.lib().dwm_moe_layer_workspace_bytes(int(num_tokens), int(hidden), int(inter),
                                                      int(topk), int(num_experts), int(y_f32)))

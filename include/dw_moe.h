@@ -205,6 +205,18 @@ int dwm_combine(const void* x, int x_dtype, int64_t x_rows, const int32_t* indic
                 const void* w, int w_dtype, int t, int h, int topk, void* out, int out_dtype,
                 void* stream);
 
+/* The combine with the shared expert summed in (MOE_SHARED_EXPERT_TP,
+ * X0104:80-87): out[t] = round(f32(mid(routed[t])) * routed_scale + shared[t])
+ * where routed[t] is dwm_combine's k-order f32 sum, mid rounds it to bf16
+ * (mid_dtype DWM_BF16, the combine's own output dtype) or keeps it
+ * (DWM_F32, MOE_F32_REDUCE), and each step is rounded to f32. shared [t, h]
+ * (DWM_BF16 or DWM_F32) is the shared expert's output (or this shard's
+ * partial of it); NULL gives dwm_combine. */
+int dwm_combine_shared(const void* x, int x_dtype, int64_t x_rows, const int32_t* indices,
+                       const void* w, int w_dtype, int t, int h, int topk, const void* shared,
+                       int shared_dtype, float routed_scale, int mid_dtype, void* out,
+                       int out_dtype, void* stream);
+
 /* ---- the single-device layer in one call ---------------------------------
  * fused_moe_func's GMM path (X0104:88-98, X0405, X0404 on one device):
  * dwm_route_topk -> dwm_permute -> dwm_dispatch_gather -> dwm_gmm_fp4 (gmm1,
@@ -308,6 +320,12 @@ int dwm_ep_dispatch(dwm_ep* ctx, const void* hidden, const int32_t* topk_ids, in
  * the k-order contract of fast_combine (KC:14-21). */
 int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                    int w_dtype, void* out, int out_dtype, int phases, void* stream);
+/* dwm_ep_combine with the shared expert summed into each own token's sum
+ * (MOE_SHARED_EXPERT_TP, X0104:80-87), as dwm_combine_shared does; shared
+ * [num_tokens, hidden] is read in the REDUCE phase. */
+int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
+                          int w_dtype, const void* shared, int shared_dtype, float routed_scale,
+                          int mid_dtype, void* out, int out_dtype, int phases, void* stream);
 /* Synchronise the context's device, unmap peers and free the buffers. */
 int dwm_ep_destroy(dwm_ep* ctx);
 

@@ -41,7 +41,7 @@ __all__ = [
     "codes_to_e2m1", "decode_codes", "round_to_e2m1", "b200_swizzle",
     "b200_unswizzle", "to_b200_layout", "from_b200_layout", "e8m0_encode",
     "e8m0_decode", "scales_to_f32", "dequant_fp4_block", "dequant_fp4_f32",
-    "gmm_f32", "gmm_ref", "silu_and_mul", "quantize_fp4_block32",
+    "gmm_f32", "gmm_ref", "silu_and_mul", "combine_shared", "quantize_fp4_block32",
     "dequantize_fp4_block32", "apply_scoring_fn", "route_topk",
     "sorted_token_indices", "permute", "dispatch_gather", "combine",
     "fused_moe", "ep_dispatch", "ep_combine_korder", "ep_combine_rankorder",
@@ -522,6 +522,21 @@ def combine(x: np.ndarray, indices, topk_weights, topk: int,
         prod = (xf[idx[:, k]] * w[:, k:k + 1]).astype(np.float32)
         acc = (acc + prod).astype(np.float32)
     return round_bf16(acc) if out_dtype == "bf16" else acc
+
+
+def combine_shared(x, indices, topk_weights, topk: int, shared, routed_scale: float = 1.0,
+                   mid_dtype: str = "bf16", out_dtype: str = "bf16") -> np.ndarray:
+    """The routed combine with the shared expert's partial summed in
+    (MOE_SHARED_EXPERT_TP, X0104:80-87 of the patch): the routed k-order sum
+    in the combine's dtype (bf16, or f32 under MOE_F32_REDUCE), widened to
+    f32, times routed_scale, plus the f32 shared partial, each step rounded
+    to f32, then one rounding to the output dtype:
+        out = dtype(f32(combine_out) * routed_scale + shared_partial)."""
+    routed = combine(x, indices, topk_weights, topk, out_dtype=mid_dtype)
+    sh = np.asarray(shared, np.float32)
+    v = (np.asarray(routed, np.float32) * np.float32(routed_scale)).astype(np.float32)
+    v = (v + sh).astype(np.float32)
+    return round_bf16(v) if out_dtype == "bf16" else v
 
 
 # ----------------------------------------------------------------------------

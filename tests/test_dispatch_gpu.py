@@ -117,6 +117,38 @@ def test_combine_bit_exact(dw, xdt, wdt):
     assert np.array_equal(bf16_to_np(out), O.combine(y, idx, w, k))
 
 
+@pytest.mark.parametrize("f32_reduce", [False, True])
+@pytest.mark.parametrize("shdt,odt", [("f32", "bf16"), ("bf16", "bf16"), ("f32", "f32")])
+def test_combine_shared_bit_exact(dw, f32_reduce, shdt, odt):
+    """The shared expert summed into the combine (X0104:80-87): bit-exact
+    against the oracle's f32(mid(routed)) * routed_scale + shared."""
+    rng = np.random.default_rng(9)
+    t, k, h = 129, 6, 1024
+    y = O.round_bf16(rng.standard_normal((t * k, h)).astype(np.float32))
+    w = rng.dirichlet(np.ones(k), size=t).astype(np.float32)
+    idx = rng.permutation(t * k).astype(np.int32)
+    sh = (rng.standard_normal((t, h)) * 0.5).astype(np.float32)
+    if shdt == "bf16":
+        sh = O.round_bf16(sh)
+        sh_t = np_to_bf16(sh)
+    else:
+        sh_t = torch.from_numpy(sh).cuda()
+    odtype = torch.bfloat16 if odt == "bf16" else torch.float32
+    out = dw.combine_shared(np_to_bf16(y), torch.from_numpy(idx).cuda(),
+                            torch.from_numpy(w).cuda(), k, sh_t, routed_scale=2.5,
+                            f32_reduce=f32_reduce, out_dtype=odtype)
+    want = O.combine_shared(y, idx, w, k, sh, 2.5, mid_dtype="f32" if f32_reduce else "bf16",
+                            out_dtype=odt)
+    got = bf16_to_np(out) if odt == "bf16" else out.cpu().numpy()
+    assert np.array_equal(got, want)
+    # routed_scale 1 and a zero shared partial give back the plain combine
+    # (up to the mid rounding, which the bf16 output repeats).
+    zero = torch.zeros((t, h), dtype=torch.float32, device="cuda")
+    out0 = dw.combine_shared(np_to_bf16(y), torch.from_numpy(idx).cuda(),
+                             torch.from_numpy(w).cuda(), k, zero)
+    assert np.array_equal(bf16_to_np(out0), O.combine(y, idx, w, k))
+
+
 @pytest.mark.parametrize("fn", ["sigmoid", "softmax", "sqrtsoftplus"])
 def test_route_topk_golden(dw, golden, fn):
     d = golden("route_small")

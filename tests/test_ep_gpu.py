@@ -175,6 +175,42 @@ def test_ep_graph_replay_advances_epoch(ep):
             c.close()
 
 
+def test_ep_combine_with_shared_expert(ep):
+    """The EP combine with a shared expert summed in (X0104:80-87): each
+    rank's k-order routed sum, rounded to bf16, times routed_scale, plus its
+    shared partial, bit-exact."""
+    world, e, k, h = 4, 32, 4, 256
+    from dw_tpu_b200 import _lib as L
+    t = [24, 3, 17, 0]
+    hid, ids, w = _inputs(world, t, e, k, h, seed=41, dist="zipf")
+    ctxs = ep.create_local_contexts(world, max_tokens=24, hidden=h, topk=k, num_experts=e)
+    try:
+        ep.emulated_dispatch(ctxs, [np_to_bf16(x) for x in hid],
+                             [torch.from_numpy(i).cuda() for i in ids])
+        ref = O.ep_dispatch(hid, ids, e)
+        ys = [O.round_bf16(np.random.default_rng(r).standard_normal(
+            (ctxs[r].capacity, h)).astype(np.float32)) for r in range(world)]
+        shs = [np.random.default_rng(50 + r).standard_normal((t[r], h)).astype(np.float32)
+               for r in range(world)]
+        for c, y in zip(ctxs, ys):
+            c.combine(np_to_bf16(y), torch.zeros((c.num_tokens, k), device="cuda"),
+                      phases=L.EP_PUSH)
+        outs = [c.combine(np_to_bf16(y), torch.from_numpy(ww).cuda(), phases=L.EP_REDUCE,
+                          shared=torch.from_numpy(sh).cuda(), routed_scale=1.5)
+                for c, y, ww, sh in zip(ctxs, ys, w, shs)]
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        routed = O.ep_combine_korder([y[:int(g[1].sum())] for y, g in zip(ys, ref)],
+                                     [g[2] for g in ref], w, out_dtype="bf16")
+        for r in range(world):
+            want = O.round_bf16((np.asarray(routed[r], np.float32) * np.float32(1.5)
+                                 ).astype(np.float32) + shs[r])
+            assert np.array_equal(bf16_to_np(outs[r]), want), r
+    finally:
+        for c in ctxs:
+            c.close()
+
+
 def test_ep_invalid_ids_reported_and_dropped(ep):
     world, e, k, h = 2, 16, 2, 64
     ctxs = ep.create_local_contexts(world, max_tokens=8, hidden=h, topk=k, num_experts=e)

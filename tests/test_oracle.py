@@ -150,6 +150,21 @@ def test_combine_matches_explicit_k_loop():
         assert np.array_equal(got[tt], acc)
 
 
+def test_combine_shared_follows_x0104_order():
+    rng = np.random.default_rng(12)
+    t, k, h = 5, 3, 8
+    x = O.round_bf16(rng.standard_normal((t * k, h)).astype(np.float32))
+    idx = rng.permutation(t * k).astype(np.int32)
+    w = rng.random((t, k)).astype(np.float32)
+    sh = rng.standard_normal((t, h)).astype(np.float32)
+    got = O.combine_shared(x, idx, w, k, sh, 0.75, mid_dtype="bf16", out_dtype="f32")
+    routed = O.round_bf16(O.combine(x, idx, w, k, out_dtype="f32"))
+    for tt in range(t):
+        for c in range(h):
+            v = np.float32(np.float32(routed[tt, c]) * np.float32(0.75))
+            assert got[tt, c] == np.float32(v + sh[tt, c])
+
+
 def test_gmm_ref_close_to_f32_oracle():
     d = make_golden.gmm_small(seed=1)
     lhs = O.bf16_bits_to_f32(d["lhs_bits"])
