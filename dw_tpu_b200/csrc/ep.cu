@@ -7,7 +7,7 @@
 // layout (the "symmetric" buffer), exports it as a CUDA IPC handle, and maps
 // every peer's; kernels then load and store peer memory over NVLink.
 //
-//   dispatch  one kernel of XFER_CTAS CTAs. Every CTA histograms all of the
+//   dispatch  one kernel of one CTA per SM. Every CTA histograms all of the
 //             rank's (token, k) expert ids in shared memory (so no CTA waits
 //             on another CTA of its grid). The first CTA to start publishes
 //             the per-expert counts into every peer's count table as 64-bit
@@ -52,6 +52,7 @@
 // overwrites its receive rows, counts or outputs only after that next
 // dispatch's counts from this rank have reached it.
 #include <cstring>
+#include <type_traits>
 #include <new>
 
 #include "moe_common.cuh"
@@ -60,9 +61,9 @@ namespace dwm {
 namespace ep {
 
 constexpr int MAX_WORLD = 8;
-constexpr int XFER_CTAS = 128;  // grid of the dispatch kernel
-constexpr int XFER_THREADS = 512;
-constexpr int COMBINE_THREADS = 64;
+constexpr int XFER_THREADS = 512;  // dispatch CTA size (one CTA per SM)
+constexpr int COPY_DEPTH = 8;      // 16-byte row loads in flight per dispatch thread
+constexpr int COMBINE_THREADS = 128;
 constexpr int ROW_BITS = 28;    // sent-row code: owner << ROW_BITS | row
 constexpr int64_t MAX_CAP = 1LL << ROW_BITS;
 
@@ -298,13 +299,14 @@ __global__ void __launch_bounds__(XFER_THREADS)
       }
       __syncthreads();
       if (tid < cn && cx[tid] >= 0) atomicAdd(&run[cx[tid]], 1);
-      // Copy the chunk's rows: 16-byte units, four loads in flight per thread.
+      // Copy the chunk's rows: 16-byte units, COPY_DEPTH loads in flight per
+      // thread ahead of the stores.
       const int units = cn * h16;
-      for (int u0 = tid; u0 < units; u0 += 4 * blockDim.x) {
-        uint4 v[4];
-        uint4* to[4];
+      for (int u0 = tid; u0 < units; u0 += COPY_DEPTH * blockDim.x) {
+        uint4 v[COPY_DEPTH];
+        uint4* to[COPY_DEPTH];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < COPY_DEPTH; ++q) {
           const int u = u0 + q * blockDim.x;
           to[q] = nullptr;
           if (u < units) {
@@ -318,7 +320,7 @@ __global__ void __launch_bounds__(XFER_THREADS)
           }
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < COPY_DEPTH; ++q)
           if (to[q]) *to[q] = v[q];
       }
       __syncthreads();
@@ -395,16 +397,24 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
     for (int k0 = 0; k0 < P.topk || k0 == 0; k0 += KB) {
-      float v[KB][8];
+      // Rows in flight: packed bf16 (4 registers each) or f32 (8).
+      using Row = std::conditional_t<XD == DWM_BF16, uint4, float[8]>;
+      Row v[KB];
       int code[KB];
+      auto load = [&](int q) {
+        const uint8_t* base = P.peer[code[q] >> ROW_BITS] + P.L.outb;
+        const int64_t off = (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8;
+        if constexpr (XD == DWM_BF16)
+          v[q] = moe::load8_bf16_raw_cg(base, off);
+        else
+          moe::load8_cg<XD>(base, off, v[q]);
+      };
 #pragma unroll
       for (int q = 0; q < KB; ++q)
         code[q] = mine && k0 + q < P.topk ? __ldg(P.sent + t * P.topk + k0 + q) : -1;
 #pragma unroll
       for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0 && (code[q] >> ROW_BITS) == P.rank)
-          moe::load8_cg<XD>(P.peer[P.rank] + P.L.outb,
-                            (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8, v[q]);
+        if (code[q] >= 0 && (code[q] >> ROW_BITS) == P.rank) load(q);
       if (k0 == 0) {  // the peers' outputs: wait once for their announcements
         if (tid < P.world && tid != P.rank &&
             !wait_flag(reinterpret_cast<const uint32_t*>(P.peer[P.rank] + P.L.ready) + tid,
@@ -415,13 +425,16 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
       if (!s_ok) break;
 #pragma unroll
       for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0 && (code[q] >> ROW_BITS) != P.rank)
-          moe::load8_cg<XD>(P.peer[code[q] >> ROW_BITS] + P.L.outb,
-                            (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8, v[q]);
+        if (code[q] >= 0 && (code[q] >> ROW_BITS) != P.rank) load(q);
 #pragma unroll
       for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0)
-          moe::mul_add8(acc, v[q], moe::load_weight<WD>(w, t * P.topk + k0 + q));
+        if (code[q] >= 0) {
+          const float wk = moe::load_weight<WD>(w, t * P.topk + k0 + q);
+          if constexpr (XD == DWM_BF16)
+            moe::mul_add8_bf16raw(acc, v[q], wk);
+          else
+            moe::mul_add8(acc, v[q], wk);
+        }
     }
     if (mine && s_ok) {
       moe::shared_add8(acc, sa, t * P.H + (int64_t)c * 8);
@@ -630,7 +643,7 @@ extern "C" int dwm_ep_dispatch(dwm_ep* c, const void* hidden, const int32_t* top
     DWM_CHECK_ARG(recv_group_sizes, "NULL recv_group_sizes");
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned grid = (phases & DWM_EP_ROWS) ? ep::XFER_CTAS : 1;
+  const unsigned grid = (phases & DWM_EP_ROWS) ? (unsigned)num_sms() : 1;
   ep::ep_dispatch_kernel<<<grid, ep::XFER_THREADS, ep::dispatch_smem_bytes(c->num_experts), s>>>(
       make_params(c), static_cast<const uint4*>(hidden), topk_ids, recv_group_sizes, phases,
       status_ptr());

@@ -157,6 +157,21 @@ __device__ __forceinline__ void load8_cg(const void* x, int64_t off, float (&v)[
   }
 }
 
+// 8 consecutive bf16 elements kept packed (4 registers), bypassing L1.
+__device__ __forceinline__ uint4 load8_bf16_raw_cg(const void* x, int64_t off) {
+  return __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
+}
+
+// acc <- acc + bf16x8(q) * w, as mul_add8 on the unpacked values.
+__device__ __forceinline__ void mul_add8_bf16raw(float (&acc)[8], const uint4& q, float w) {
+  const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(__uint_as_float(u[i] << 16), w));
+    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(__uint_as_float(u[i] & 0xFFFF0000u), w));
+  }
+}
+
 template <int WD>
 __device__ __forceinline__ float load_weight(const void* w, int64_t i) {
   if constexpr (WD == DWM_BF16)
