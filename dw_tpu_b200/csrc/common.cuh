@@ -79,8 +79,29 @@ __device__ __forceinline__ float lds_f32(uint32_t a) {
 __device__ __forceinline__ void sts_u32(uint32_t a, uint32_t v) {
   asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
+__device__ __forceinline__ void sts_u16(uint32_t a, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(v) : "memory");
+}
+__device__ __forceinline__ uint4 lds_u128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ void sts_f32(uint32_t a, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+// sigmoid for the SwiGLU epilogues: exp and reciprocal on the MUFU pipe
+// (__expf, __fdividef: a few ulp, within the GEMM's ~1e-3 tolerance) in a
+// handful of instructions. A correctly rounded division or reciprocal
+// measured ~300 cycles per value in the tcgen05 epilogue, where it made a
+// 256-row tile's epilogue longer than its main loop. Large -g: __fdividef
+// returns 0 for a denominator above 2^126, the right limit.
+__device__ __forceinline__ float sigmoid_fast(float g) {
+  return __fdividef(1.0f, 1.0f + __expf(-g));
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

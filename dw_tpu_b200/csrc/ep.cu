@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
       // Rows in flight: packed bf16 (4 registers each) or f32 (8).
       using Row = std::conditional_t<XD == DWM_BF16, uint4, float[8]>;
       Row v[KB];
-      int code[KB];
+      int code[KB] = {};
       auto load = [&](int q) {
         const uint8_t* base = P.peer[code[q] >> ROW_BITS] + P.L.outb;
         const int64_t off = (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8;

@@ -82,6 +82,11 @@ static_assert(C_SUB_BYTES % 128 == 0, "TMA needs 128 B alignment");
 #define DWM_GMM_MMA_SLEEP 0
 #endif
 
+// Epilogue staging: each epilogue warp turns its 32 columns x 8 token rows
+// into 16-byte row vectors through 1 KiB of shared memory (8 x 32 x 4 bytes).
+constexpr int EPI_ROWS = 8;
+constexpr int EPI_WARP_BYTES = EPI_ROWS * 32 * 4;
+
 // Pipeline depths (build-time tunables).
 #ifndef DWM_GMM_TS
 #define DWM_GMM_TS 3
@@ -101,7 +106,11 @@ struct Smem {
   static constexpr int AS = BT == 128 ? DWM_GMM_AS : 2;
   static constexpr int T_STAGE = BT * BK * 2;  // BT/16 boxes of 16 rows x 64 k
   static constexpr int NBUF = TMEM_COLS / (NSUB * BT);
-  static constexpr int CS = ScaleTraits<SD>::bytes == 4 ? (DWM_GMM_CS * 3) / 4 : DWM_GMM_CS;
+  // Code ring: 8 stages (6 with f32 scales, 7 with bf16 scales, to fit the
+  // epilogue's staging tiles in shared memory).
+  static constexpr int CS = ScaleTraits<SD>::bytes == 4   ? (DWM_GMM_CS * 3) / 4
+                            : ScaleTraits<SD>::bytes == 2 ? DWM_GMM_CS - 1
+                                                          : DWM_GMM_CS;
   static constexpr int S_STAGE = NSUB * 2 * BW * ScaleTraits<SD>::bytes;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_T = OFF_A + AS * A_STAGE;
@@ -110,9 +119,10 @@ struct Smem {
   static constexpr int OFF_BAR = OFF_S + CS * S_STAGE;
   static constexpr int NUM_BARS = 2 * CS + 2 * TS + 2 * AS + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int OFF_ROWS = OFF_MISC + 16;
+  static constexpr int OFF_ROWS = OFF_MISC + 32;
   static constexpr int OFF_TILES = OFF_ROWS + (MAX_GROUPS + 1) * 4;
-  static constexpr int BYTES = OFF_TILES + (MAX_GROUPS + 1) * 4;
+  static constexpr int OFF_EPI = (OFF_TILES + (MAX_GROUPS + 1) * 4 + 15) & ~15;
+  static constexpr int BYTES = OFF_EPI + 4 * EPI_WARP_BYTES;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
   static_assert(CS <= 32 && TS <= 32, "ring masks are 32-bit");
@@ -170,6 +180,33 @@ __device__ __forceinline__ int token_span(int nb, int& nbp) {
   return (BT / T_BOX_ROWS) / nbp;
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// A decode group's wait for its next stage: the group's first warp polls the
+// two mbarriers (codes landed, A slot free) and publishes the outcome; the
+// other seven warps wait on named barrier 1 + grp, which holds them in
+// hardware instead of letting them spin and take issue slots from the warps
+// with work (the epilogue, above all). The outcome is double-buffered by the
+// group's step parity, so the first warp can publish the next step's value
+// while a slow warp still reads this one.
+template <int SLEEP>
+__device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint64_t* full,
+                                           uint32_t full_ph, uint64_t* empty, uint32_t empty_ph,
+                                           volatile int* abort_flag, volatile int* go,
+                                           int* status) {
+  volatile int* slot = go + grp * 2 + ((step >> 1) & 1);
+  if (dw == 0) {
+    bool got = mbar_wait<SLEEP>(full, full_ph, abort_flag, status);
+    got = got && mbar_wait<SLEEP>(empty, empty_ph, abort_flag, status);
+    got = __all_sync(0xffffffffu, got);
+    if ((threadIdx.x & 31) == 0) *slot = got ? 1 : 0;
+  }
+  named_bar_sync(1 + grp, NUM_DEC_WARPS * 32);
+  return *slot != 0;
+}
+
 template <int SD, int VAR, int BT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
@@ -197,6 +234,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  volatile int* group_go = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 16);  // [2][2]
   int* row_start = reinterpret_cast<int*>(smem + L::OFF_ROWS);
   int* tile_prefix = reinterpret_cast<int*>(smem + L::OFF_TILES);
 
@@ -317,6 +355,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int64_t i = (int64_t)hi * n16 + tid; i < (int64_t)a.m * n16; i += stride) o[i] = z;
     }
     const int mrow = warp * 32 + lane;  // TMEM lane = A row = weight column slot
+    const uint32_t epi_s = smem_u32(smem + L::OFF_EPI + warp * EPI_WARP_BYTES);
     const int col = VAR == kMN ? (mrow & ~7) + perm8(mrow & 7) : mrow;
     constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
     int it = 0;
@@ -329,44 +368,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NSUB * BT);
       const int nchunks = (t.rows + 15) >> 4;
+      // The warp's 32 output columns (per part): SwiGLU gives one part
+      // (columns n_idx*BW + 32 warp ..), a plain GEMM two (sub-tile 0 and
+      // sub-tile 1, BW apart).
+      const bool act = a.act != DWM_ACT_NONE;
+      const int nparts = act ? 1 : 2;
+      const int64_t colw = act ? (int64_t)t.n_idx * BW + warp * 32
+                               : (int64_t)t.n_idx * (NSUB * BW) + warp * 32;
+      const int lcol = col - warp * 32;  // this lane's column inside the warp's 32
+      const int row_bytes = 32 * es;     // one staged row: 64 or 128 bytes
+      const int vec_per_row = row_bytes / 16;
       for (int c = 0; c < nchunks; ++c) {
         uint32_t r0[16], r1[16];
         tmem_ld16(tbase + c * 16, r0);
         tmem_ld16(tbase + BT + c * 16, r1);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int r = c * 16 + e;
-          if (r < t.rows) {
-            const int64_t row = t.row0 + r;
-            const float v0 = __uint_as_float(r0[e]) * acc_scale;
-            const float v1 = __uint_as_float(r1[e]) * acc_scale;
-            if (a.act == DWM_ACT_NONE) {
-              const int64_t base = row * a.ldo + (int64_t)t.n_idx * (NSUB * BW) + col;
-              if (a.out_f32) {
-                float* o = reinterpret_cast<float*>(a.out);
-                o[base] = v0;
-                o[base + BW] = v1;
+        for (int half = 0; half < 2; ++half) {
+          const int rb = c * 16 + half * EPI_ROWS;  // first token row of this round
+          if (rb >= t.rows) break;
+          for (int part = 0; part < nparts; ++part) {
+            // Stage: lane lcol writes its value of each of the round's rows.
+#pragma unroll
+            for (int e = 0; e < EPI_ROWS; ++e) {
+              const int ee = half * EPI_ROWS + e;
+              const float v0 = __uint_as_float(r0[ee]) * acc_scale;
+              const float v1 = __uint_as_float(r1[ee]) * acc_scale;
+              float v;
+              if (act) {
+                float g = v0, u = v1;
+                if (a.act == DWM_ACT_SWIGLU_CLAMP) {
+                  g = fminf(g, a.limit);
+                  u = fminf(fmaxf(u, -a.limit), a.limit);
+                }
+                v = g * sigmoid_fast(g) * u;
               } else {
-                uint16_t* o = reinterpret_cast<uint16_t*>(a.out);
-                o[base] = (uint16_t)f32_to_bf16_bits(v0);
-                o[base + BW] = (uint16_t)f32_to_bf16_bits(v1);
+                v = part == 0 ? v0 : v1;
               }
-            } else {
-              float g = v0, u = v1;
-              if (a.act == DWM_ACT_SWIGLU_CLAMP) {
-                g = fminf(g, a.limit);
-                u = fminf(fmaxf(u, -a.limit), a.limit);
-              }
-              const float sg = 1.0f / (1.0f + expf(-g));
-              const float h = g * sg * u;
-              const int64_t base = row * a.ldo + (int64_t)t.n_idx * BW + col;
-              if (a.out_f32) {
-                reinterpret_cast<float*>(a.out)[base] = h;
-              } else {
-                reinterpret_cast<uint16_t*>(a.out)[base] = (uint16_t)f32_to_bf16_bits(h);
+              if (a.out_f32)
+                sts_f32(epi_s + (uint32_t)(e * row_bytes + lcol * 4), v);
+              else
+                sts_u16(epi_s + (uint32_t)(e * row_bytes + lcol * 2),
+                        (uint16_t)f32_to_bf16_bits(v));
+            }
+            __syncwarp();
+            // Copy out: 16-byte vectors of consecutive columns, one row each.
+            for (int q = lane; q < EPI_ROWS * vec_per_row; q += 32) {
+              const int e = q / vec_per_row, j = q - e * vec_per_row;
+              const int r = rb + e;
+              if (r < t.rows) {
+                const uint4 v = lds_u128(epi_s + (uint32_t)(e * row_bytes + j * 16));
+                const int64_t off = ((t.row0 + r) * (int64_t)a.ldo + colw + part * BW) * es +
+                                    j * 16;
+                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
               }
             }
+            __syncwarp();
           }
         }
       }
@@ -551,9 +608,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t cs_ph = (step / CS) & 1;
           const int as = (int)(step % AS);
           const uint32_t as_ph = (step / AS) & 1;
-          bool got = mbar_wait<DWM_GMM_DEC_SLEEP>(&cs_full[cs], cs_ph, abort_flag, a.status);
-          got = got && mbar_wait<DWM_GMM_DEC_SLEEP>(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
-          if (!__all_sync(0xffffffffu, got)) {
+          if (!group_wait<DWM_GMM_DEC_SLEEP>(grp, dw, step, &cs_full[cs], cs_ph, &a_empty[as],
+                                             as_ph ^ 1, abort_flag, group_go, a.status)) {
             ok = false;
             break;
           }
@@ -607,9 +663,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t cs_ph = (step / CS) & 1;
           const int as = (int)(step % AS);
           const uint32_t as_ph = (step / AS) & 1;
-          bool got = mbar_wait<DWM_GMM_DEC_SLEEP>(&cs_full[cs], cs_ph, abort_flag, a.status);
-          got = got && mbar_wait<DWM_GMM_DEC_SLEEP>(&a_empty[as], as_ph ^ 1, abort_flag, a.status);
-          if (!__all_sync(0xffffffffu, got)) {
+          if (!group_wait<DWM_GMM_DEC_SLEEP>(grp, dw, step, &cs_full[cs], cs_ph, &a_empty[as],
+                                             as_ph ^ 1, abort_flag, group_go, a.status)) {
             ok = false;
             break;
           }

@@ -549,7 +549,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
                 g = fminf(g, a.limit);
                 u = fminf(fmaxf(u, -a.limit), a.limit);
               }
-              const float hv = g * (1.0f / (1.0f + expf(-g))) * u;
+              const float hv = g * sigmoid_fast(g) * u;
               const int64_t off = row * a.ldo + colbase[i] + gid + 8 * hc;
               if (a.out_f32)
                 reinterpret_cast<float*>(a.out)[off] = hv;
