@@ -87,30 +87,47 @@ static_assert(C_SUB_BYTES % 128 == 0, "TMA needs 128 B alignment");
 constexpr int EPI_ROWS = 8;
 constexpr int EPI_WARP_BYTES = EPI_ROWS * 32 * 4;
 
-// Pipeline depths (build-time tunables).
+// Pipeline depths (build-time tunables). Measured on cfg3-sized groups (256
+// rows per expert): the token ring is the one that matters. A token stage
+// reaches shared memory from L2 only after the UMMAs of the stage it
+// replaces have completed, so its latency has to be covered by the stages
+// ahead of it: 4 stages of 128 rows (2 A stages, 8 code stages) measured
+// 599 TFLOP/s against 562 with 3 (3 A stages); 256-row tiles take 3 token
+// stages of 32 KiB at the cost of the code ring.
 #ifndef DWM_GMM_TS
-#define DWM_GMM_TS 3
+#define DWM_GMM_TS 4
 #endif
 #ifndef DWM_GMM_AS
-#define DWM_GMM_AS 3
+#define DWM_GMM_AS 2
 #endif
 #ifndef DWM_GMM_CS
 #define DWM_GMM_CS 8
+#endif
+// The same for 256-row tiles.
+#ifndef DWM_GMM_TS256
+#define DWM_GMM_TS256 3
+#endif
+#ifndef DWM_GMM_AS256
+#define DWM_GMM_AS256 2
+#endif
+#ifndef DWM_GMM_CS256
+#define DWM_GMM_CS256 3
 #endif
 // BT = token rows per tile (the UMMA N): 128 (two TMEM accumulator buffers,
 // the epilogue overlaps the next tile) or 256 (one buffer; every weight
 // column is decoded once per 256 rows and each UMMA does twice the work).
 template <int SD, int BT>
 struct Smem {
-  static constexpr int TS = BT == 128 ? DWM_GMM_TS : 2;
-  static constexpr int AS = BT == 128 ? DWM_GMM_AS : 2;
+  static constexpr int TS = BT == 128 ? DWM_GMM_TS : DWM_GMM_TS256;
+  static constexpr int AS = BT == 128 ? DWM_GMM_AS : DWM_GMM_AS256;
   static constexpr int T_STAGE = BT * BK * 2;  // BT/16 boxes of 16 rows x 64 k
   static constexpr int NBUF = TMEM_COLS / (NSUB * BT);
   // Code ring: 8 stages (6 with f32 scales, 7 with bf16 scales, to fit the
   // epilogue's staging tiles in shared memory).
-  static constexpr int CS = ScaleTraits<SD>::bytes == 4   ? (DWM_GMM_CS * 3) / 4
-                            : ScaleTraits<SD>::bytes == 2 ? DWM_GMM_CS - 1
-                                                          : DWM_GMM_CS;
+  static constexpr int CS_BASE = BT == 128 ? DWM_GMM_CS : DWM_GMM_CS256;
+  static constexpr int CS = ScaleTraits<SD>::bytes == 4   ? (CS_BASE * 3 + 3) / 4
+                            : ScaleTraits<SD>::bytes == 2 ? CS_BASE - (CS_BASE > 4)
+                                                          : CS_BASE;
   static constexpr int S_STAGE = NSUB * 2 * BW * ScaleTraits<SD>::bytes;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_T = OFF_A + AS * A_STAGE;
