@@ -144,13 +144,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// d = a * b (accumulator starts at zero).
+// d = a * b + z, with z a zero quad the caller keeps in registers (the MMA
+// reads C as four registers; a literal 0 would be rebuilt for every call).
 __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                            uint32_t b1) {
+                                            uint32_t b1, const float (&z)[4]) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%10,%10,%10,%10};"
+      "{%8,%9}, {%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z[0]), "f"(z[1]),
+        "f"(z[2]), "f"(z[3]));
 }
 
 struct Task {
@@ -301,6 +303,11 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
   const int gid = lane >> 2, tig = lane & 3;
   const int NSTAGE = a.k / KSTAGE;
   const DecodeRegs dregs = DecodeRegs::make();
+  // Register-held constants of the post-MMA path: the zero quad of the
+  // partials' first MMA and the tokens' 2^64 pre-scale.
+  const float zq[4] = {__uint_as_float(pin(0u)), __uint_as_float(pin(0u)),
+                       __uint_as_float(pin(0u)), __uint_as_float(pin(0u))};
+  const uint32_t tok_2p64 = pin(kBf16x2_2p64);
   // 2^(c-1-delta) for E8M0 code c, both bf16 halves: c * 0x00800080 + bias.
   const uint32_t wm_bias = pin((126u - C::DELTA) * 0x00800080u);
   const int wstride = gridDim.x * C::WARPS;
@@ -430,8 +437,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
               uint32_t b0 = *reinterpret_cast<const uint32_t*>(row);
               uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + 16);
               if constexpr (C::POST) {
-                b0 = hmul2_bf16(b0, kBf16x2_2p64);
-                b1 = hmul2_bf16(b1, kBf16x2_2p64);
+                b0 = hmul2_bf16(b0, tok_2p64);
+                b1 = hmul2_bf16(b1, tok_2p64);
               }
               b[nt][0] = b0;
               b[nt][1] = b1;
@@ -464,7 +471,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                   if (kk2 == 0)
-                    mma_16816_z(part[i][nt], af, b[nt][0], b[nt][1]);
+                    mma_16816_z(part[i][nt], af, b[nt][0], b[nt][1], zq);
                   else
                     mma_16816(part[i][nt], af, b[nt][0], b[nt][1]);
                 }
