@@ -35,7 +35,8 @@ ACT_SWIGLU_CLAMP = 2
 FP4_E2M1 = 0
 FP4_TOKAMAX = 1
 FP4_B200 = 2
-LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200}
+FP4_CM = 3
+LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200, "cm": FP4_CM}
 SCORE_SOFTMAX = 0
 SCORE_SIGMOID = 1
 SCORE_SQRTSOFTPLUS = 2
@@ -64,6 +65,7 @@ SIGNATURES = {
                     _I),
     "dwm_fp4_dequant": ([_P, _I, _P, _I, _I, _I, _I, _P, _P], _I),
     "dwm_fp4_to_b200": ([_P, _P, _I, _I, _I, _I, _P], _I),
+    "dwm_fp4_to_cm": ([_P, _P, _I, _I, _I, _I, _P], _I),
     "dwm_gmm_fp4_variant": ([_P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P,
                              _I, _P], _I),
     "dwm_fp4_codes_convert": ([_P, _P, _SZ, _I, _I, _P], _I),

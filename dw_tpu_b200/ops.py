@@ -40,13 +40,14 @@ def _scale_view(s: torch.Tensor):
 # ----------------------------------------------------------------------------
 
 def fp4_dims(codes: torch.Tensor, layout: str):
-    """(groups, k, n) of packed FP4 weights: "e2m1" [g, k, n/2], "b200" [g, n, k/2]."""
+    """(groups, k, n) of packed FP4 weights: "e2m1" [g, k, n/2]; "b200" and
+    "cm" [g, n, k/2]."""
     if codes.dim() != 3:
         raise ValueError("FP4 weights must be 3-D packed bytes")
     g, a, b = codes.shape
     if layout == "e2m1":
         return g, a, 2 * b
-    if layout == "b200":
+    if layout in ("b200", "cm"):
         return g, 2 * b, a
     raise ValueError(f"unknown FP4 layout {layout!r}")
 
@@ -121,6 +122,28 @@ def fp4_to_b200_out(src, inverse=False, stream=None):
     rc = L.lib().dwm_fp4_to_b200(src.data_ptr(), dst.data_ptr(), g, k, n, int(inverse),
                                  L.stream_ptr() if stream is None else stream)
     L.check(rc, "fp4_to_b200")
+    return dst
+
+
+def fp4_to_cm_out(src, inverse=False, stream=None):
+    """Raw e2m1 [g, k, n/2] -> the column-major CM layout (u32 words
+    [g][n][k/8], returned as bytes shaped [g, n, k/2]), or back with
+    ``inverse``; returns a new tensor."""
+    L.require_cuda(src)
+    src = _u8view(src).contiguous()
+    if src.dim() != 3:
+        raise ValueError("expected packed FP4 weights [g, k, n/2] (or [g, n, k/2])")
+    if inverse:
+        g, n, k2 = src.shape
+        k = 2 * k2
+        dst = torch.empty((g, k, n // 2), dtype=torch.uint8, device=src.device)
+    else:
+        g, k, n2 = src.shape
+        n = 2 * n2
+        dst = torch.empty((g, n, k // 2), dtype=torch.uint8, device=src.device)
+    rc = L.lib().dwm_fp4_to_cm(src.data_ptr(), dst.data_ptr(), g, k, n, int(inverse),
+                               L.stream_ptr() if stream is None else stream)
+    L.check(rc, "fp4_to_cm")
     return dst
 
 

@@ -30,7 +30,7 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--layout", default="b200", choices=["b200", "e2m1"])
+    p.add_argument("--layout", default="b200", choices=["b200", "e2m1", "cm"])
     p.add_argument("--variant", type=int, default=0,
                    help="dwm_gmm_fp4_variant kernel choice (0 = automatic)")
     a = p.parse_args()
@@ -38,6 +38,8 @@ def main():
     w = synthetic.moe_weights(e, h, i, seed=a.seed, device="cuda")
     if a.layout == "b200":
         w = w.to_b200()
+    elif a.layout == "cm":
+        w = w.to_cm()
     x, router = synthetic.layer_inputs(t, h, e, seed=a.seed)
     x = x.cuda()
     logits = (x.float() @ router.cuda().float()).to(torch.bfloat16)

@@ -59,6 +59,12 @@ extern "C" {
                              m16n8k16 MMA for W^T, its bits permuted for a
                              one-PRMT bf16 decode */
 
+#define DWM_FP4_CM 3      /* column-major load-time layout (dwm_fp4_to_cm): u32
+                             words [groups][n][k/8], word w of column c the
+                             nibbles of k = 8w..8w+7 in order, bits permuted
+                             as in DWM_FP4_B200; taken by the tcgen05 kernel
+                             that keeps the decoded weights in TMEM */
+
 #define DWM_SCORE_SOFTMAX 0
 #define DWM_SCORE_SIGMOID 1
 #define DWM_SCORE_SQRTSOFTPLUS 2
@@ -128,6 +134,12 @@ int dwm_fp4_dequant(const void* codes, int codes_format, const void* scales, int
  * fp4_weight_to_codes (B01:276-299, TK:17-30). k % 16 == 0, n % 16 == 0. */
 int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int n, int inverse,
                     void* stream);
+
+/* Load-time re-layout of packed e2m1 weights: raw [g, k, n/2] -> DWM_FP4_CM
+ * [g, n, k/2] (inverse = 0) or back (inverse = 1); lossless, out of place.
+ * k % 8 == 0, n % 2 == 0. */
+int dwm_fp4_to_cm(const void* in, void* out, int groups, int k, int n, int inverse,
+                  void* stream);
 
 /* On-device weight preparation: quantize_tensor(float4_e2m1fn, w, block 32,
  * power_of_two_scale) (B01:319-347) of w [groups, k, n] (bf16 or f32) over

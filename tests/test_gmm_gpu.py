@@ -212,6 +212,49 @@ def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
     assert_gemm_close(bf16_to_np(out), r, r32, 128, rows=v)
 
 
+@pytest.mark.parametrize("sd", ["u8", "bf16", "f32", "u8_wide"])
+def test_cm_layout_tmem_kernel_matches_e2m1(dw, sd):
+    """The column-major CM layout (weights decoded into TMEM by the tcgen05
+    kernel, variant 6): the re-layout matches the oracle and inverts, and the
+    GEMM gives the raw e2m1 path's bits (the same decoded bf16 weights and
+    UMMA order) for plain, SwiGLU and f32 outputs, with ragged groups (one
+    empty, one above 128 rows) and E8M0 codes 0 and > 132."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    lo, hi = (0, 140) if sd == "u8_wide" else (120, 140)
+    lhs, packed, scales, gs = _case(11, 400, 128, 512, 4, gs=[3, 0, 70, 300], lo=lo, hi=hi)
+    if sd in ("u8", "u8_wide"):
+        sc = torch.from_numpy(scales)
+    elif sd == "bf16":
+        sc = torch.from_numpy(O.e8m0_decode(scales)).to(torch.bfloat16)
+    else:
+        sc = torch.from_numpy(O.e8m0_decode(scales))
+    sc = sc.cuda()
+    raw = torch.from_numpy(packed).cuda()
+    cm = ops.fp4_to_cm_out(raw)
+    assert np.array_equal(cm.cpu().numpy(), O.to_cm_layout(packed))
+    assert torch.equal(ops.fp4_to_cm_out(cm, inverse=True), raw)
+    x = np_to_bf16(lhs)
+    g = torch.from_numpy(gs).cuda()
+    for act, n_out, dt in ((L.ACT_NONE, 512, torch.bfloat16), (L.ACT_SWIGLU, 256, torch.bfloat16),
+                           (L.ACT_NONE, 512, torch.float32)):
+        ref = ops.gmm_fp4_out(x, raw, sc, g, torch.empty((400, n_out), dtype=dt, device="cuda"),
+                              act=act, zero_init=True)
+        kind = "swiglu" if act == L.ACT_SWIGLU else None
+        r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
+                         out_dtype="f32" if dt == torch.float32 else "bf16")
+        r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
+        for variant in (0, 6):
+            got = ops.gmm_fp4_out(x, cm, sc, g, torch.empty((400, n_out), dtype=dt, device="cuda"),
+                                  act=act, zero_init=True, layout="cm", variant=variant)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            assert_gemm_close(to_np(got), O.round_bf16(r) if dt == torch.bfloat16 else r, r32,
+                              128, rows=v)
+            assert np.all(to_np(got)[~v] == 0)
+            assert torch.equal(ref.view(torch.int16), got.view(torch.int16)), (act, variant)
+
+
 @pytest.mark.parametrize("gs,k,act,limit,sd,out_dt", [
     ([1, 0, 2, 3, 5, 8, 0, 7], 192, None, None, "u8", "bf16"),        # <= 8 rows: one n8 tile
     ([9, 16, 11, 0, 14, 3, 12, 15], 256, None, None, "u8", "f32"),    # 9-16 rows: two n8 tiles

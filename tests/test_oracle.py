@@ -76,6 +76,19 @@ def test_b200_swizzle_is_a_lossless_bit_permutation():
         assert got == nib[g, kk, c], (g, kk, c)
 
 
+def test_cm_layout_round_trip_and_element_order():
+    rng = np.random.default_rng(14)
+    raw = rng.integers(0, 256, (2, 64, 24), dtype=np.uint8)  # [g, k, n/2]
+    cm = O.to_cm_layout(raw)
+    assert cm.shape == (2, 48, 32)                              # [g, n, k/2]
+    assert np.array_equal(O.from_cm_layout(cm), raw)
+    nib = O.unpack_nibbles(raw)                                # [g, k, n]
+    words = O.b200_unswizzle(cm).view(np.uint32).reshape(2, 48, 8)
+    for (g, kk, c) in [(0, 0, 0), (1, 63, 47), (0, 9, 17), (1, 22, 5), (0, 40, 30)]:
+        got = (int(words[g, c, kk // 8]) >> (4 * (kk % 8))) & 0xF
+        assert got == nib[g, kk, c], (g, kk, c)
+
+
 def test_e8m0_roundtrip_and_lossless_flag():
     e = np.arange(-126, 128)
     s = np.ldexp(np.ones(e.shape, np.float32), e).astype(np.float32)
