@@ -57,6 +57,7 @@ constexpr int num_threads() { return VAR == 2 ? 896 : NUM_THREADS; }
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
 constexpr int TOKEN_WARP = 6;
+constexpr int MMA_WARP2 = 7;  // the TMEM variant's second UMMA issuer (sub-tile 1)
 constexpr int DEC_WARP0 = 8;
 constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
 constexpr int MAX_GROUPS = 1024;
@@ -252,6 +253,10 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
   using L = Smem<SD, BT, VAR>;
   static_assert(VAR != kTS || BT == 128, "kTS runs 128-row tiles");
+  // The TMEM variant issues its UMMAs from two threads (warps 5 and 7), one
+  // per sub-tile, so that one thread's barrier waits and commits (~500
+  // cycles a stage) overlap the other's UMMAs; each commits its own.
+  constexpr int MMA_ISSUERS = VAR == kTS ? 2 : 1;
   constexpr int CS = L::CS;
   constexpr int TS = L::TS;
   constexpr int AS = L::AS;
@@ -287,17 +292,17 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
     }
     for (int i = 0; i < TS; ++i) {
       mbar_init(&tk_full[i], 1);
-      mbar_init(&tk_empty[i], 1);
+      mbar_init(&tk_empty[i], MMA_ISSUERS);
     }
     for (int i = 0; i < AS; ++i) {
       mbar_init(&a_full[i], NUM_DEC_WARPS);
-      mbar_init(&a_empty[i], 1);
+      mbar_init(&a_empty[i], MMA_ISSUERS);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], MMA_ISSUERS);
       mbar_init(&acc_empty[i], L::EPI_WARPS);
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(drain_bar, MMA_ISSUERS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -558,8 +563,10 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       for (int s = 0; s < TS; ++s)
         if (ts_armed & (1u << s)) mbar_wait(&tk_full[s], (ts_par >> s) & 1, nullptr, a.status);
     }
-  } else if (warp == MMA_WARP) {
-    // ---------------- UMMA issuer ----------------
+  } else if (warp == MMA_WARP || (MMA_ISSUERS == 2 && warp == MMA_WARP2)) {
+    // ---------------- UMMA issuer(s) ----------------
+    const int s_lo = MMA_ISSUERS == 2 && warp == MMA_WARP2 ? 1 : 0;
+    const int s_hi = MMA_ISSUERS == 2 ? s_lo + 1 : NSUB;
     if (lane == 0) {
       int as = 0, ts = 0;
       uint32_t as_ph = 0, ts_ph = 0;
@@ -594,8 +601,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bdesc = smem_desc_sw128(t_base + j * 32, 16, 1024);
-#pragma unroll
-            for (int s = 0; s < NSUB; ++s) {
+            for (int s = s_lo; s < s_hi; ++s) {
               if constexpr (VAR == kTS) {
                 const uint32_t a_tm = tmem + (uint32_t)(TS_A_COL0 + (as * NSUB + s) * 32 + j * 8);
                 umma_ts_bf16(d0 + s * BT, a_tm, bdesc, idesc, (kk | j) != 0);
