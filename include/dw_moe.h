@@ -87,8 +87,9 @@ int dwm_device_status(void* stream, int* bits);
  *           [sum(group_sizes[:g]), +group_sizes[g]))
  *   codes   DWM_FP4_E2M1: uint8 [num_local_groups, k, n/2], two e2m1 nibbles
  *           per byte, element 2j in the low nibble; DWM_FP4_B200: the same
- *           values re-laid by dwm_fp4_to_b200 (faster decode); convert
- *           tokamax codes once with dwm_fp4_codes_convert
+ *           values re-laid by dwm_fp4_to_b200 (faster decode); DWM_FP4_CM:
+ *           re-laid by dwm_fp4_to_cm (decoded into TMEM, for prefill-sized
+ *           groups); convert tokamax codes once with dwm_fp4_codes_convert
  *   scales  [num_local_groups, k/32, n] of scale_dtype: DWM_U8 (E8M0 codes,
  *           KE:37-40), DWM_BF16 or DWM_F32 (cast to bf16 before use)
  *   group_sizes int32 [num_groups] on the device
@@ -109,8 +110,10 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8- or 16-row token tiles by the average rows per local group),
  * 3 / 4 = the same with 8 / 16-row token tiles (2-4: the automatic choice
- * for B200 codes whose groups average at most 16 rows). 1-5 need DWM_FP4_B200
- * codes. Every variant decodes the same bf16 weights and accumulates in f32; results
+ * for B200 codes whose groups average at most 16 rows), 6 = tcgen05 MMA with
+ * the weights decoded straight into TMEM (the A-from-TMEM UMMA form; the
+ * automatic choice for, and the only variant of, DWM_FP4_CM codes). 1-5 need
+ * DWM_FP4_B200 codes. Every variant decodes the same bf16 weights and accumulates in f32; results
  * differ between variants only by f32 summation order. Same reference
  * interface as dwm_gmm_fp4 (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
