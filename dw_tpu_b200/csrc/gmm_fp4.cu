@@ -37,6 +37,10 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
                cudaStream_t stream);
+int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+                    const int32_t* group_sizes, int num_groups, int m, int k, int n,
+                    int group_offset, int n_local, int act, float limit, int out_dtype,
+                    int zero_init, void* out, cudaStream_t stream);
 
 namespace gmm {
 
@@ -1145,10 +1149,11 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // variant: 0 = choose, 1 = tcgen05 (shared-memory decode) with 128-row
 // tiles, 5 = the same with 256-row tiles, 2 = mma.sync decode kernel (B200
 // layout only) with 8- or 16-row token tiles by the average rows per local
-// group, 3 / 4 = the same with 8 / 16-row tiles. The automatic choice sends
-// the B200 layout to mma.sync when the local groups average at most 16 rows,
-// else 128-row tiles (256-row tiles measured slower at 256 rows per group:
-// one TMEM buffer, shallower rings and fewer tiles to balance).
+// group, 3 / 4 = the same with 8 / 16-row tiles, 6 = weights decoded into
+// TMEM (CM layout), 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout). The
+// automatic choice for the B200 layout: mma.sync when the local groups
+// average at most 16 rows, CTA pairs from 128 rows (prefill), else the
+// single-CTA tcgen05 kernel with 128-row tiles.
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
                int group_offset, int num_local_groups, int act, float act_limit, int out_dtype,
@@ -1162,12 +1167,17 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     return DWM_OK;
   }
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
-  if (variant == 0) variant = codes_format == DWM_FP4_B200 && avg <= 16 ? 2 : 1;
+  if (variant == 0)
+    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 7 : 1;
   if (codes_format == DWM_FP4_CM) variant = 6;
   if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
                       variant == 3 ? 1 : variant == 4 ? 2 : (avg <= 8 ? 1 : 2), s);
+  if (variant == 7)
+    return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                           group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
+                           out, s);
 #define DWM_GMM_LAUNCH(SD, VAR, BT)                                                       \
   return launch<SD, VAR, BT>(lhs, codes, scales, group_sizes, num_groups, m, k, n,      \
                              group_offset, num_local_groups, act, act_limit, out_dtype,  \
@@ -1213,13 +1223,14 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 6,
+  DWM_CHECK_ARG(variant >= 0 && variant <= 7,
                 "variant must be 0 (auto), 1 / 5 (tcgen05, 128 / 256-row tiles), 2-4 "
-                "(mma.sync decode kernel) or 6 (tcgen05, weights decoded into TMEM)");
+                "(mma.sync decode kernel), 6 (tcgen05, weights decoded into TMEM) or 7 "
+                "(tcgen05 on CTA pairs)");
   DWM_CHECK_ARG(variant == 0 || (variant == 6) == (codes_format == DWM_FP4_CM),
                 "variant 6 takes (only) the CM layout");
   DWM_CHECK_ARG(variant == 0 || variant == 6 || codes_format == DWM_FP4_B200,
-                "variants 1-5 need the B200 layout");
+                "variants 1-5 and 7 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

@@ -1,0 +1,731 @@
+// FP4 grouped matmul on CTA pairs for prefill-sized groups: tokamax gmm_v2
+// with rhs_fp4_codes (TK:107-153), weights in the B200 layout
+// (fp4_decode.cuh), decoded on the SM and multiplied with tcgen05
+// cta_group::2 UMMAs.
+//
+// The product is computed transposed as in gmm_fp4.cu: decoded weight columns
+// are UMMA operand A (rows), token rows are operand B. Two CTAs on
+// neighbouring SMs (a cluster of 2) share one 256 x N tile:
+//   - each CTA decodes its own 128 weight columns of a 64-k stage into its
+//     shared memory (A) and loads half of the tile's N token rows (B);
+//   - the even CTA issues the M = 256 UMMAs, which take the time of a
+//     single-SM 128 x N UMMA;
+//   - each CTA's TMEM holds its 128 x N f32 accumulator, double-buffered
+//     (2 x 256 columns), so a tile's epilogue overlaps the next main loop.
+// Against one CTA with two 128-column sub-tiles and N = 128 this halves the
+// decode work per output and reaches the UMMA's full rate (N = 256).
+//
+// Tile geometry: a pair tile covers 128 SwiGLU features (their gate and up
+// columns, 64 features per CTA) or 256 plain columns (128 per CTA), and up
+// to 256 token rows of one group. A group of r rows takes ceil(r / 256) tiles
+// of equal size, N rounded up to 32 so that each CTA's half is a whole number
+// of 16-row TMA boxes. In A, each 16-feature gate block sits next to its up
+// block, so one TMEM lane quarter holds both and the SwiGLU epilogue pairs
+// them with one warp shuffle.
+//
+// Warp roles in each CTA (768 threads):
+//   warps 0-3   epilogue: TMEM lane quarter = warp
+//   warp  4     TMA: FP4 codes + scales of this CTA's columns (HBM stream)
+//   warp  5     pair TMEM allocation; UMMA issuer in the even CTA
+//   warp  6     TMA: this CTA's half of the token rows (L2-resident)
+//   warps 8-23  decode, two groups of 8 on alternate stages
+//
+// A pipeline stage holds one 64-k step of both operands (the decoded A and
+// this CTA's token rows) behind one "full" barrier in the even CTA, so the
+// single issuing thread waits once and commits once per step: both CTAs'
+// token copies complete on it (the even CTA expects the bytes of both
+// halves) and both CTAs' decode warps arrive on it remotely. The issuer's
+// commits arrive on the matching barrier of both CTAs. Every wait is bounded
+// (common.cuh). Numerics are those of gmm_fp4.cu (E0901:84-95).
+#include <algorithm>
+
+#include "fp4_decode.cuh"
+
+namespace dwm {
+namespace gmm_pair {
+
+using namespace fp4;
+
+constexpr int ROWS = 128;        // A rows (weight columns) per CTA
+constexpr int BK = 64;           // k per stage
+constexpr int BT = 256;          // token rows per tile at most (pair UMMA N)
+constexpr int HALF = BT / 2;     // token rows per CTA at most
+constexpr int NUM_THREADS = 768;
+constexpr int EPI_WARPS = 4;
+constexpr int PRODUCER_WARP = 4;
+constexpr int MMA_WARP = 5;
+constexpr int TOKEN_WARP = 6;
+constexpr int DEC_WARP0 = 8;
+constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
+constexpr int MAX_GROUPS = 1024;
+constexpr int TMEM_COLS = 512;    // two 256-column accumulator buffers
+constexpr int ACC_COLS = 256;
+constexpr int A_STAGE = ROWS * BK * 2;  // 16 KiB of bf16, 128-byte swizzled, K-major
+constexpr int T_STAGE = HALF * BK * 2;  // 16 KiB: this CTA's token rows of one k-step
+constexpr int STAGE = A_STAGE + T_STAGE;
+constexpr int C_STAGE = ROWS * BK / 2;  // 4 KiB of codes: 8 column blocks x 4 k-blocks x 32 words
+constexpr int T_BOX_ROWS = 16;
+constexpr int T_BOX_BYTES = T_BOX_ROWS * BK * 2;  // 2 KiB
+constexpr int EPI_WARP_BYTES = 16 * 32 * 4;       // 16 token rows x 32 columns of f32
+
+#ifndef DWM_PAIR_STAGES
+#define DWM_PAIR_STAGES 5
+#endif
+#ifndef DWM_PAIR_CS
+#define DWM_PAIR_CS 8
+#endif
+#ifndef DWM_PAIR_EPI_SLEEP
+#define DWM_PAIR_EPI_SLEEP 256
+#endif
+
+template <int SD>
+struct Layout {
+  static constexpr int S = DWM_PAIR_STAGES;
+  static constexpr int CS = DWM_PAIR_CS;
+  static constexpr int S_STAGE = 2 * ROWS * ScaleTraits<SD>::bytes;  // [k32 block][128 rows]
+  static constexpr int OFF_STAGE = 0;  // stage i: A at i * STAGE, tokens A_STAGE after it
+  static constexpr int OFF_C = OFF_STAGE + S * STAGE;
+  static constexpr int OFF_S = OFF_C + CS * C_STAGE;
+  static constexpr int OFF_BAR = OFF_S + CS * S_STAGE;
+  static constexpr int NUM_BARS = 2 * CS + 2 * S + 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_ROWS = OFF_MISC + 32;
+  static constexpr int OFF_TILES = OFF_ROWS + (MAX_GROUPS + 1) * 4;
+  static constexpr int OFF_EPI = (OFF_TILES + (MAX_GROUPS + 1) * 4 + 15) & ~15;
+  static constexpr int BYTES = OFF_EPI + EPI_WARPS * EPI_WARP_BYTES;
+  static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment
+  static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
+  static_assert(STAGE % 1024 == 0 && A_STAGE % 1024 == 0, "swizzled tiles need 1 KiB alignment");
+  static_assert(CS <= 32 && S <= 32, "ring masks are 32-bit");
+};
+
+struct Args {
+  const int32_t* group_sizes;
+  int num_groups, group_offset, n_local;
+  int m, k, n;
+  int act;
+  float limit;
+  int out_f32;
+  int zero_init;
+  void* out;
+  int ldo;      // output row length (n, or n/2 with SwiGLU)
+  int n_tiles;  // pair column tiles per group (n / 256)
+  int* status;
+};
+
+struct Tile {
+  int g;      // local group
+  int row0;   // first lhs row
+  int rows;   // valid rows (1..BT)
+  int n_idx;  // column tile
+};
+
+__device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
+                                         const Args& a) {
+  int lo = 0, hi = a.n_local;  // tile_prefix[lo] <= idx < tile_prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tile_prefix[mid] <= idx) lo = mid; else hi = mid;
+  }
+  Tile t;
+  t.g = lo;
+  const int local = idx - tile_prefix[lo];
+  const int t_idx = local / a.n_tiles;
+  t.n_idx = local - t_idx * a.n_tiles;
+  const int gs_start = row_start[a.group_offset + lo];
+  const int gs_rows = row_start[a.group_offset + lo + 1] - gs_start;
+  const int nt = (gs_rows + BT - 1) / BT;
+  const int r_lo = (int)(((int64_t)t_idx * gs_rows) / nt);
+  const int r_hi = (int)(((int64_t)(t_idx + 1) * gs_rows) / nt);
+  t.row0 = gs_start + r_lo;
+  t.rows = r_hi - r_lo;
+  return t;
+}
+
+// UMMA N of a tile: rows rounded up to 32 (each CTA's half a multiple of 16).
+__device__ __forceinline__ int tile_n(int rows) { return max(32, (rows + 31) & ~31); }
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// A decode group's wait for its next stage (codes landed, stage released by
+// the pair's UMMAs): the group's first warp polls, the other seven park on
+// named barrier 1 + grp. The outcome is double-buffered by step parity.
+__device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint64_t* full,
+                                           uint32_t full_ph, uint64_t* empty, uint32_t empty_ph,
+                                           volatile int* abort_flag, volatile int* go,
+                                           int* status) {
+  volatile int* slot = go + grp * 2 + ((step >> 1) & 1);
+  if (dw == 0) {
+    bool got = mbar_wait(full, full_ph, abort_flag, status);
+    got = got && mbar_wait(empty, empty_ph, abort_flag, status);
+    got = __all_sync(0xffffffffu, got);
+    if ((threadIdx.x & 31) == 0) *slot = got ? 1 : 0;
+  }
+  named_bar_sync(1 + grp, NUM_DEC_WARPS * 32);
+  return *slot != 0;
+}
+
+template <int SD>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gmm_pair_kernel(const __grid_constant__ CUtensorMap tm_lhs,
+                    const __grid_constant__ CUtensorMap tm_lhs_half,
+                    const __grid_constant__ CUtensorMap tm_codes,
+                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
+  using L = Layout<SD>;
+  constexpr int CS = L::CS;
+  constexpr int S = L::S;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* cs_full = bars;             // local: code TMA landed
+  uint64_t* cs_empty = cs_full + CS;    // local: decode group done with the codes
+  uint64_t* full = cs_empty + CS;      // even CTA: both CTAs' A decoded and tokens landed
+  uint64_t* empty = full + S;           // each CTA: the pair's UMMAs done with the stage
+  uint64_t* acc_full = empty + S;       // each CTA: accumulator buffer complete
+  uint64_t* acc_empty = acc_full + 2;   // even CTA: both CTAs drained the buffer
+  uint64_t* drain_bar = acc_empty + 2;  // each CTA: every UMMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  volatile int* group_go = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 16);  // [2][2]
+  int* row_start = reinterpret_cast<int*>(smem + L::OFF_ROWS);
+  int* tile_prefix = reinterpret_cast<int*>(smem + L::OFF_TILES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cl = (int)cluster_index();
+  const int ncl = (int)cluster_count();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < CS; ++i) {
+      mbar_init(&cs_full[i], 1);
+      mbar_init(&cs_empty[i], NUM_DEC_WARPS);
+    }
+    for (int i = 0; i < S; ++i) {
+      // Decode warps of both CTAs, plus the even CTA's expect_tx for the
+      // token bytes of both halves.
+      mbar_init(&full[i], 2 * NUM_DEC_WARPS + 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == PRODUCER_WARP && lane == 0) {
+    tma_prefetch_desc(&tm_lhs);
+    tma_prefetch_desc(&tm_lhs_half);
+    tma_prefetch_desc(&tm_codes);
+    tma_prefetch_desc(&tm_scales);
+  }
+  if (warp == 0) {
+    // Row starts over all groups (rows are sorted by group), then the tile
+    // prefix over the local groups.
+    const int G = a.num_groups;
+    const int per = (G + 31) / 32;
+    int sum = 0;
+    for (int i = 0; i < per; ++i) {
+      const int g = lane * per + i;
+      if (g < G) {
+        int v = a.group_sizes[g];
+        if (v < 0) { report(a.status, DWM_DEV_BAD_INDEX); v = 0; }
+        sum += v;
+      }
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - sum;
+    for (int i = 0; i < per; ++i) {
+      const int g = lane * per + i;
+      if (g < G) {
+        const int v = max(a.group_sizes[g], 0);
+        row_start[g] = min(run, a.m);
+        run += v;
+      }
+    }
+    if (lane == 31) {
+      row_start[G] = min(run, a.m);
+      if (run > a.m) report(a.status, DWM_DEV_BAD_INDEX);
+    }
+    __syncwarp();
+    const int NL = a.n_local;
+    const int per2 = (NL + 31) / 32;
+    int tsum = 0;
+    for (int i = 0; i < per2; ++i) {
+      const int g = lane * per2 + i;
+      if (g < NL) {
+        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        tsum += ((rows + BT - 1) / BT) * a.n_tiles;
+      }
+    }
+    int tincl = tsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, tincl, o);
+      if (lane >= o) tincl += y;
+    }
+    int trun = tincl - tsum;
+    for (int i = 0; i < per2; ++i) {
+      const int g = lane * per2 + i;
+      if (g < NL) {
+        tile_prefix[g] = trun;
+        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        trun += ((rows + BT - 1) / BT) * a.n_tiles;
+      }
+    }
+    if (lane == 31) tile_prefix[NL] = trun;
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // Barriers initialised and TMEM allocated in both CTAs before any
+  // cross-CTA arrival.
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = tile_prefix[a.n_local];
+  const int KT = a.k / BK;
+  const bool act = a.act != DWM_ACT_NONE;
+  // The even CTA's barriers, as shared::cluster addresses.
+  const uint32_t full_0 = mapa_shared(full, 0);
+  const uint32_t acc_empty_0 = mapa_shared(acc_empty, 0);
+
+  if (warp < EPI_WARPS) {
+    // ---------------- epilogue ----------------
+    const int es = a.out_f32 ? 4 : 2;
+    const int q = warp;  // TMEM lane quarter
+    if (a.zero_init) {
+      // Rows outside the local groups: [0, lo) and [hi, m).
+      const int lo = row_start[a.group_offset];
+      const int hi = row_start[a.group_offset + a.n_local];
+      const int64_t n16 = (int64_t)a.ldo * es / 16;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      const int64_t tid = (int64_t)blockIdx.x * 128 + threadIdx.x;
+      const int64_t stride = (int64_t)gridDim.x * 128;
+      uint4* o = reinterpret_cast<uint4*>(a.out);
+      for (int64_t i = tid; i < (int64_t)lo * n16; i += stride) o[i] = z;
+      for (int64_t i = (int64_t)hi * n16 + tid; i < (int64_t)a.m * n16; i += stride) o[i] = z;
+    }
+    const uint32_t epi_s = smem_u32(smem + L::OFF_EPI + q * EPI_WARP_BYTES);
+    constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
+    const bool hi_lane = lane >= 16;
+    int it = 0;
+    for (int idx = cl; idx < total; idx += ncl, ++it) {
+      const Tile t = get_tile(idx, row_start, tile_prefix, a);
+      const int buf = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const bool got = mbar_wait<DWM_PAIR_EPI_SLEEP>(&acc_full[buf], ph, abort_flag, a.status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * ACC_COLS);
+      const int nchunks = (t.rows + 15) >> 4;
+      if (act) {
+        // Lanes 0-15 hold the gate, lanes 16-31 the up column of features
+        // fcol + (lane & 15); lane < 16 forms the even tokens of a chunk,
+        // lane >= 16 the odd ones, each after one shuffle with its partner.
+        const int64_t fcol = (int64_t)t.n_idx * 128 + rank * 64 + q * 16;
+        const int row_bytes = 16 * es;  // one staged token row: 16 features
+        const int vpr = row_bytes / 16;
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float even = __uint_as_float(r[2 * e]) * acc_scale;
+            const float odd = __uint_as_float(r[2 * e + 1]) * acc_scale;
+            const float recv = __shfl_xor_sync(0xffffffffu, hi_lane ? even : odd, 16);
+            float g = hi_lane ? recv : even;
+            float u = hi_lane ? odd : recv;
+            if (a.act == DWM_ACT_SWIGLU_CLAMP) {
+              g = fminf(g, a.limit);
+              u = fminf(fmaxf(u, -a.limit), a.limit);
+            }
+            const float v = g * sigmoid_fast(g) * u;
+            const uint32_t at = (uint32_t)((2 * e + (hi_lane ? 1 : 0)) * row_bytes + (lane & 15) * es);
+            if (a.out_f32)
+              sts_f32(epi_s + at, v);
+            else
+              sts_u16(epi_s + at, (uint16_t)f32_to_bf16_bits(v));
+          }
+          __syncwarp();
+          for (int qv = lane; qv < 16 * vpr; qv += 32) {
+            const int e = qv / vpr, j = qv - e * vpr;
+            const int rr = c * 16 + e;
+            if (rr < t.rows) {
+              const uint4 v = lds_u128(epi_s + (uint32_t)(e * row_bytes + j * 16));
+              const int64_t off = ((t.row0 + rr) * (int64_t)a.ldo + fcol) * es + j * 16;
+              *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+            }
+          }
+          __syncwarp();
+        }
+      } else {
+        const int64_t ccol = (int64_t)t.n_idx * 256 + rank * 128 + q * 32;
+        const int row_bytes = 32 * es;  // one staged token row: 32 columns
+        const int vpr = row_bytes / 16;
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float v = __uint_as_float(r[e]) * acc_scale;
+            const uint32_t at = (uint32_t)(e * row_bytes + lane * es);
+            if (a.out_f32)
+              sts_f32(epi_s + at, v);
+            else
+              sts_u16(epi_s + at, (uint16_t)f32_to_bf16_bits(v));
+          }
+          __syncwarp();
+          for (int qv = lane; qv < 16 * vpr; qv += 32) {
+            const int e = qv / vpr, j = qv - e * vpr;
+            const int rr = c * 16 + e;
+            if (rr < t.rows) {
+              const uint4 v = lds_u128(epi_s + (uint32_t)(e * row_bytes + j * 16));
+              const int64_t off = ((t.row0 + rr) * (int64_t)a.ldo + ccol) * es + j * 16;
+              *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(buf * 8));
+    }
+  } else if (warp == PRODUCER_WARP) {
+    // ---------------- TMA producer: codes + scales (HBM stream) ----------------
+    if (lane == 0) {
+      const uint64_t pol_stream = policy_evict_first();
+      constexpr uint32_t cs_bytes = C_STAGE + L::S_STAGE;
+      int cs = 0;
+      uint32_t cs_ph = 0, cs_armed = 0, cs_par = 0;
+      bool ok = true;
+      for (int idx = cl; idx < total && ok; idx += ncl) {
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        // This CTA's first column: features (gate) with SwiGLU, else columns.
+        const int col0 = act ? t.n_idx * 128 + (int)rank * 64 : t.n_idx * 256 + (int)rank * 128;
+        const int blk = t.g * (a.n / 16) + col0 / 16;
+        const int srow = t.g * (a.k / 32);
+        for (int kk = 0; kk < KT; ++kk) {
+          if (!mbar_wait(&cs_empty[cs], cs_ph ^ 1, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&cs_full[cs], cs_bytes);
+          cs_armed |= 1u << cs;
+          cs_par = (cs_par & ~(1u << cs)) | (cs_ph << cs);
+          tma_load_3d(smem + L::OFF_C + cs * C_STAGE, &tm_codes, &cs_full[cs], kk * 128, blk, 0,
+                      pol_stream);
+          tma_load_3d(smem + L::OFF_S + cs * L::S_STAGE, &tm_scales, &cs_full[cs], col0, 0,
+                      srow + kk * 2, pol_stream);
+          if (++cs == CS) { cs = 0; cs_ph ^= 1; }
+        }
+      }
+      for (int s = 0; s < CS; ++s)
+        if (cs_armed & (1u << s)) mbar_wait(&cs_full[s], (cs_par >> s) & 1, nullptr, a.status);
+    }
+  } else if (warp == TOKEN_WARP) {
+    // ---------------- TMA producer: this CTA's token rows ----------------
+    // A full half (128 rows) is one box; a partial one nb boxes of 16 rows.
+    if (lane == 0) {
+      const uint64_t pol_keep = policy_evict_last();
+      int st = 0;
+      uint32_t ph = 0, armed = 0, par = 0;
+      bool ok = true;
+      for (int idx = cl; idx < total && ok; idx += ncl) {
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const int half = tile_n(t.rows) / 2;
+        const int nb = half / T_BOX_ROWS;
+        const int rbase = t.row0 + (int)rank * half;
+        for (int kk = 0; kk < KT; ++kk) {
+          if (!mbar_wait(&empty[st], ph ^ 1, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * nb * T_BOX_BYTES));
+          armed |= 1u << st;
+          par = (par & ~(1u << st)) | (ph << st);
+          const uint32_t bar0 = full_0 + (uint32_t)(st * 8);
+          uint8_t* tdst = smem + L::OFF_STAGE + st * STAGE + A_STAGE;
+          if (nb == HALF / T_BOX_ROWS) {
+            tma_load_2d_pair(tdst, &tm_lhs_half, bar0, kk * BK, rbase, pol_keep);
+          } else {
+            for (int bx = 0; bx < nb; ++bx)
+              tma_load_2d_pair(tdst + bx * T_BOX_BYTES, &tm_lhs, bar0, kk * BK,
+                               rbase + bx * T_BOX_ROWS, pol_keep);
+          }
+          if (++st == S) { st = 0; ph ^= 1; }
+        }
+      }
+      // Every stage this CTA filled is released by the pair's UMMAs (so its
+      // copies have landed) before the CTA can exit.
+      for (int i = 0; i < S; ++i)
+        if (armed & (1u << i)) mbar_wait(&empty[i], (par >> i) & 1, nullptr, a.status);
+    }
+  } else if (warp == MMA_WARP) {
+    // ---------------- UMMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      int st = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int idx = cl; idx < total && ok; idx += ncl, ++it) {
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        const uint32_t idesc = idesc_bf16(2 * ROWS, tile_n(t.rows), false, false);
+        const int buf = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag, a.status)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + (uint32_t)(buf * ACC_COLS);
+        for (int kk = 0; kk < KT; ++kk) {
+          if (!mbar_wait(&full[st], ph, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + L::OFF_STAGE + st * STAGE);
+          const uint32_t t_base = a_base + A_STAGE;
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            umma_pair_bf16(d0, smem_desc_sw128(a_base + j * 32, 16, 1024),
+                           smem_desc_sw128(t_base + j * 32, 16, 1024), idesc, (kk | j) != 0);
+          umma_commit_pair(&empty[st]);
+          if (++st == S) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[buf]);
+      }
+      umma_commit_pair(drain_bar);
+    }
+    // Both CTAs: every UMMA (which writes both TMEMs) completes before TMEM
+    // is released.
+    if (lane == 0) mbar_wait(drain_bar, 0, nullptr, a.status);
+  } else if (warp >= DEC_WARP0) {
+    // ---------------- decode ----------------
+    // Two groups of 8 warps take alternate stages. Warp dw decodes code
+    // block dw (16 weight columns) of the stage: lane l decodes word l of
+    // each of its 4 k-blocks (columns gid, gid+8 of the block, k pairs t,
+    // t+4) into A rows p*16 + gid and + 8, where the row block p puts gate
+    // block j next to up block j with SwiGLU.
+    const int grp = (warp - DEC_WARP0) / NUM_DEC_WARPS;
+    const int dw = (warp - DEC_WARP0) % NUM_DEC_WARPS;
+    constexpr int es = ScaleTraits<SD>::bytes;
+    constexpr int DELTA = decode_delta<SD>();
+    const int b = dw;
+    const int p = act ? 2 * (b & 3) + (b >> 2) : b;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int r0 = 16 * p + gid;  // A rows r0 and r0 + 8
+    const int row_a_off = (r0 >> 3) * 1024 + (r0 & 7) * 128;
+    const int row_b_off = ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
+    uint32_t step = 0;
+    bool ok = true;
+    for (int idx = cl; idx < total && ok; idx += ncl) {
+      for (int kk = 0; kk < KT; ++kk, ++step) {
+        if ((int)(step & 1) != grp) continue;
+        const int cs = (int)(step % CS);
+        const uint32_t cs_ph = (step / CS) & 1;
+        const int st = (int)(step % S);
+        const uint32_t ph = (step / S) & 1;
+        if (!group_wait(grp, dw, step, &cs_full[cs], cs_ph, &empty[st], ph ^ 1, abort_flag,
+                        group_go, a.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
+        const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE;
+        uint8_t* astage = smem + L::OFF_STAGE + st * STAGE;
+        uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
+        bool two = false;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          two |= col_mult<SD, DELTA>(sstage + (h * ROWS + 16 * b + gid) * es, m1[h][0], m2[h][0]);
+          two |= col_mult<SD, DELTA>(sstage + (h * ROWS + 16 * b + gid + 8) * es, m1[h][1],
+                                     m2[h][1]);
+        }
+        const bool two_any = __any_sync(0xffffffffu, two);
+        if (two_any && SD == DWM_U8) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
+        }
+        uint8_t* row_a = astage + row_a_off;
+        uint8_t* row_b = astage + row_b_off;
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(cstage + kb * 128 + lane * 4);
+          uint32_t tv[4];
+          tvals<true>(w, tv);
+          const int h = kb >> 1;
+          uint32_t v0 = hmul2_bf16(tv[0], m1[h][0]);
+          uint32_t v1 = hmul2_bf16(tv[1], m1[h][1]);
+          uint32_t v2 = hmul2_bf16(tv[2], m1[h][0]);
+          uint32_t v3 = hmul2_bf16(tv[3], m1[h][1]);
+          if (two_any) {
+            v0 = hmul2_bf16(v0, m2[h][0]);
+            v1 = hmul2_bf16(v1, m2[h][1]);
+            v2 = hmul2_bf16(v2, m2[h][0]);
+            v3 = hmul2_bf16(v3, m2[h][1]);
+          }
+          // k pair (16 kb + 2 tig) sits in 16-byte chunk 2 kb, k pair
+          // (16 kb + 2 tig + 8) in chunk 2 kb + 1, both at byte 4 tig.
+          const int c0 = 2 * kb, c1 = 2 * kb + 1;
+          *reinterpret_cast<uint32_t*>(row_a + ((c0 ^ (r0 & 7)) << 4) + 4 * tig) = v0;
+          *reinterpret_cast<uint32_t*>(row_b + ((c0 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v1;
+          *reinterpret_cast<uint32_t*>(row_a + ((c1 ^ (r0 & 7)) << 4) + 4 * tig) = v2;
+          *reinterpret_cast<uint32_t*>(row_b + ((c1 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v3;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&cs_empty[cs]);
+          mbar_arrive_remote(full_0 + (uint32_t)(st * 8));
+        }
+      }
+    }
+  }
+
+  // Both CTAs are done with every barrier, shared tile and TMEM column.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+  cluster_sync();
+}
+
+// Largest number of 2-CTA clusters resident at once (one CTA per SM), per
+// device.
+template <int SD>
+int max_pairs(cudaLaunchConfig_t cfg) {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  cfg.gridDim = dim3(2 * (unsigned)std::max(1, num_sms() / 2));
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gmm_pair_kernel<SD>, &cfg);
+  if (e != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = std::max(1, num_sms() / 2);
+  }
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int SD>
+int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
+           int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
+           float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
+  using L = Layout<SD>;
+  constexpr int es = ScaleTraits<SD>::bytes;
+  const bool act_on = act != DWM_ACT_NONE;
+  CUtensorMap tm_lhs, tm_lhs_half, tm_codes, tm_scales;
+  int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
+                          (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tm_lhs_half, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
+                      (uint64_t)m, (uint64_t)k * 2, BK, HALF, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  {
+    // Codes: rows = 16-column blocks ((k/16)*32 words each); a box is 4
+    // consecutive blocks x 2 halves (the up blocks I/16 rows on with SwiGLU,
+    // the next 4 blocks without) x one stage of 4 k-blocks.
+    const uint64_t row_bytes = (uint64_t)(k / 16) * 128;
+    const uint64_t dims[3] = {(uint64_t)(k / 16) * 32, (uint64_t)n_local * (n / 16), 2};
+    const uint64_t strides[2] = {row_bytes, act_on ? (uint64_t)(n / 32) * row_bytes : 4 * row_bytes};
+    const uint32_t box[3] = {128, 4, 2};
+    rc = encode_tmap_nd(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, codes, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  {
+    // Scales [n_local * k/32][n]: 64 columns x the same 2 halves x 2 k32 rows.
+    const uint64_t dims[3] = {(uint64_t)n, 2, (uint64_t)n_local * (k / 32)};
+    const uint64_t strides[2] = {act_on ? (uint64_t)(n / 2) * es : (uint64_t)64 * es,
+                                 (uint64_t)n * es};
+    const uint32_t box[3] = {64, 2, 2};
+    rc = encode_tmap_nd(&tm_scales, ScaleTraits<SD>::tma, 3, scales, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    rc = check_cuda(cudaFuncSetAttribute(gmm_pair_kernel<SD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC),
+                    "gmm pair smem attribute");
+    if (rc) return rc;
+    attr_set[dev] = true;
+  }
+  Args a;
+  a.group_sizes = group_sizes;
+  a.num_groups = num_groups;
+  a.group_offset = group_offset;
+  a.n_local = n_local;
+  a.m = m;
+  a.k = k;
+  a.n = n;
+  a.act = act;
+  a.limit = limit;
+  a.out_f32 = out_dtype == DWM_F32;
+  a.zero_init = zero_init;
+  a.out = out;
+  a.ldo = act_on ? n / 2 : n;
+  a.n_tiles = n / 256;
+  a.status = status_ptr();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2 * (unsigned)max_pairs<SD>(cfg));
+  return check_cuda(cudaLaunchKernelEx(&cfg, gmm_pair_kernel<SD>, tm_lhs, tm_lhs_half, tm_codes,
+                                       tm_scales, a),
+                    "gmm_pair launch");
+}
+
+}  // namespace gmm_pair
+
+// Entry from the grouped-matmul dispatcher (gmm_fp4.cu): B200-layout weights,
+// n a multiple of 256, k of 64; the caller has validated the arguments.
+int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+                    const int32_t* group_sizes, int num_groups, int m, int k, int n,
+                    int group_offset, int n_local, int act, float limit, int out_dtype,
+                    int zero_init, void* out, cudaStream_t stream) {
+  if (scale_dtype == DWM_U8)
+    return gmm_pair::launch<DWM_U8>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
+                                    group_offset, n_local, act, limit, out_dtype, zero_init, out,
+                                    stream);
+  if (scale_dtype == DWM_BF16)
+    return gmm_pair::launch<DWM_BF16>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
+                                      group_offset, n_local, act, limit, out_dtype, zero_init,
+                                      out, stream);
+  return gmm_pair::launch<DWM_F32>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
+                                   group_offset, n_local, act, limit, out_dtype, zero_init, out,
+                                   stream);
+}
+
+}  // namespace dwm

@@ -105,17 +105,22 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
 
 /* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4),
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
- * automatic choice above 16 rows), 5 = the same with 256-row tiles (one TMEM
- * accumulator buffer),
+ * automatic choice for groups averaging 17-127 rows), 5 = the same with
+ * 256-row tiles (one TMEM accumulator buffer),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8- or 16-row token tiles by the average rows per local group),
  * 3 / 4 = the same with 8 / 16-row token tiles (2-4: the automatic choice
  * for B200 codes whose groups average at most 16 rows), 6 = tcgen05 MMA with
  * the weights decoded straight into TMEM (the A-from-TMEM UMMA form; the
- * automatic choice for, and the only variant of, DWM_FP4_CM codes). 1-5 need
- * DWM_FP4_B200 codes. Every variant decodes the same bf16 weights and accumulates in f32; results
- * differ between variants only by f32 summation order. Same reference
- * interface as dwm_gmm_fp4 (TK:107-153). */
+ * automatic choice for, and the only variant of, DWM_FP4_CM codes),
+ * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
+ * decoding half of the weight columns, up to 256 token rows per tile and
+ * double-buffered accumulators (the automatic choice for B200 codes whose
+ * groups average 128 rows or more). 1-5 and 7 need DWM_FP4_B200 codes.
+ * Every variant decodes the same bf16 weights and accumulates in f32;
+ * results differ between variants only by f32 summation order (1, 5, 6 and
+ * 7 give identical bits). Same reference interface as dwm_gmm_fp4
+ * (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
                         int scale_dtype, const int32_t* group_sizes, int num_groups, int m,
                         int k, int n, int group_offset, int num_local_groups, int act,

@@ -255,6 +255,69 @@ def test_cm_layout_tmem_kernel_matches_e2m1(dw, sd):
             assert torch.equal(ref.view(torch.int16), got.view(torch.int16)), (act, variant)
 
 
+@pytest.mark.parametrize("sd", ["u8", "bf16", "f32", "u8_wide"])
+def test_pair_kernel_matches_single_cta(dw, sd):
+    """The CTA-pair tcgen05 kernel (variant 7: M = 256 UMMAs over two SMs,
+    double-buffered accumulators, groups above 256 rows split into equal
+    tiles) gives the single-CTA kernel's bits (the same decoded bf16 weights
+    and UMMA k order) for plain, SwiGLU, clamped SwiGLU and f32 outputs, on
+    ragged groups: empty, 1 row, below and above 128, exactly 256, 257 and
+    600 rows (2 and 3 tiles); also on a window of local groups with
+    zero_init."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    lo, hi = (0, 140) if sd == "u8_wide" else (120, 140)
+    sizes = [0, 1, 17, 129, 256, 257, 600, 31]
+    m = sum(sizes)
+    lhs, packed, scales, gs = _case(21, m, 256, 512, len(sizes), gs=sizes, lo=lo, hi=hi)
+    if sd in ("u8", "u8_wide"):
+        sc = torch.from_numpy(scales)
+    elif sd == "bf16":
+        sc = torch.from_numpy(O.e8m0_decode(scales)).to(torch.bfloat16)
+    else:
+        sc = torch.from_numpy(O.e8m0_decode(scales))
+    sc = sc.cuda()
+    b200 = ops.fp4_to_b200_out(torch.from_numpy(packed).cuda())
+    x = np_to_bf16(lhs)
+    g = torch.from_numpy(gs).cuda()
+
+    def bits(t):
+        return t.view(torch.int16 if t.dtype == torch.bfloat16 else torch.int32)
+
+    for act, n_out, dt, limit in ((L.ACT_NONE, 512, torch.bfloat16, 0.0),
+                                  (L.ACT_SWIGLU, 256, torch.bfloat16, 0.0),
+                                  (L.ACT_SWIGLU_CLAMP, 256, torch.float32, 0.5),
+                                  (L.ACT_NONE, 512, torch.float32, 0.0)):
+        outs = []
+        for variant in (1, 7):
+            o = torch.full((m, n_out), float("nan"), dtype=dt, device="cuda")
+            ops.gmm_fp4_out(x, b200, sc, g, o, act=act, act_limit=limit, layout="b200",
+                            variant=variant)
+            outs.append(o)
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        assert torch.equal(bits(outs[0]), bits(outs[1])), (act, dt)
+        if act != L.ACT_SWIGLU_CLAMP:
+            kind = "swiglu" if act == L.ACT_SWIGLU else None
+            r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
+                             out_dtype="f32" if dt == torch.float32 else "bf16")
+            r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
+            assert_gemm_close(to_np(outs[1]), O.round_bf16(r) if dt == torch.bfloat16 else r,
+                              r32, 256, rows=v)
+    # Local groups 2..5 of 8 (rows 1..659), rows outside zeroed.
+    wins = []
+    for variant in (1, 7):
+        o = torch.full((m, 256), float("nan"), dtype=torch.bfloat16, device="cuda")
+        ops.gmm_fp4_out(x, b200[2:6], sc[2:6], g, o, group_offset=2, num_local_groups=4,
+                        act=L.ACT_SWIGLU, zero_init=True, layout="b200", variant=variant)
+        wins.append(o)
+    torch.cuda.synchronize()
+    L.raise_on_device_error()
+    assert torch.equal(bits(wins[0]), bits(wins[1]))
+    w = to_np(wins[1])
+    assert np.all(w[:1] == 0) and np.all(w[660:] == 0)
+
+
 @pytest.mark.parametrize("gs,k,act,limit,sd,out_dt", [
     ([1, 0, 2, 3, 5, 8, 0, 7], 192, None, None, "u8", "bf16"),        # <= 8 rows: one n8 tile
     ([9, 16, 11, 0, 14, 3, 12, 15], 256, None, None, "u8", "f32"),    # 9-16 rows: two n8 tiles
