@@ -432,6 +432,17 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                : "memory");
 }
 
+// One lane of the (fully active) warp: true in exactly one lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(p));
+  return p != 0;
+}
+
 // Pair UMMA (issued by the even CTA): D[tmem] (+)= A[smem desc] * B[smem desc].
 __device__ __forceinline__ void umma_pair_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                                uint32_t idesc, uint32_t accumulate) {

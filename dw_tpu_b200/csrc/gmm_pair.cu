@@ -26,7 +26,9 @@
 // Warp roles in each CTA (768 threads):
 //   warps 0-3   epilogue: TMEM lane quarter = warp
 //   warp  4     TMA: FP4 codes + scales of this CTA's columns (HBM stream)
-//   warp  5     pair TMEM allocation; UMMA issuer in the even CTA
+//   warp  5     pair TMEM allocation; UMMA issuer in the even CTA (the whole
+//               warp runs the loop so its operands stay warp-uniform, one
+//               elected lane issues: a UMMA takes ~100 cycles to issue)
 //   warp  6     TMA: this CTA's half of the token rows (L2-resident)
 //   warps 8-23  decode, two groups of 8 on alternate stages
 //
@@ -477,7 +479,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == MMA_WARP) {
     // ---------------- UMMA issuer (even CTA) ----------------
-    if (lane == 0 && rank == 0) {
+    if (rank == 0) {
+      // The whole warp runs the loop (warp-uniform operands); one elected
+      // lane issues.
+      const bool issuer = elect_one();
       int st = 0;
       uint32_t ph = 0;
       int it = 0;
@@ -487,28 +492,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t idesc = idesc_bf16(2 * ROWS, tile_n(t.rows), false, false);
         const int buf = it & 1;
         const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag, a.status)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag, a.status)))
+          break;
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * ACC_COLS);
         for (int kk = 0; kk < KT; ++kk) {
-          if (!mbar_wait(&full[st], ph, abort_flag, a.status)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[st], ph, abort_flag, a.status))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + L::OFF_STAGE + st * STAGE);
           const uint32_t t_base = a_base + A_STAGE;
+          if (issuer) {
 #pragma unroll
-          for (int j = 0; j < BK / 16; ++j)
-            umma_pair_bf16(d0, smem_desc_sw128(a_base + j * 32, 16, 1024),
-                           smem_desc_sw128(t_base + j * 32, 16, 1024), idesc, (kk | j) != 0);
-          umma_commit_pair(&empty[st]);
+            for (int j = 0; j < BK / 16; ++j)
+              umma_pair_bf16(d0, smem_desc_sw128(a_base + j * 32, 16, 1024),
+                             smem_desc_sw128(t_base + j * 32, 16, 1024), idesc, (kk | j) != 0);
+            umma_commit_pair(&empty[st]);
+          }
+          __syncwarp();
           if (++st == S) { st = 0; ph ^= 1; }
         }
         if (!ok) break;
-        umma_commit_pair(&acc_full[buf]);
+        if (issuer) umma_commit_pair(&acc_full[buf]);
+        __syncwarp();
       }
-      umma_commit_pair(drain_bar);
+      if (issuer) umma_commit_pair(drain_bar);
+      __syncwarp();
     }
     // Both CTAs: every UMMA (which writes both TMEMs) completes before TMEM
     // is released.

@@ -1,11 +1,17 @@
 """Small, self-contained MoE layer run for timing and for ncu captures.
 
     python -m dw_tpu_b200.profile_case [--experts E] [--tokens T] [--iters N]
+    python -m dw_tpu_b200.profile_case --groups uniform|multinomial ...
 
 Runs the config-1 layer shapes (H=4096, I=2048, top-8, sigmoid routing) with
 a configurable expert count, so an ncu capture of the FP4 GEMM can stay at a
 few hundred MB on the device, and prints per-kernel CUDA-event times and the
 algorithmic HBM bandwidth of each gmm launch.
+
+With --groups the two grouped matmuls run alone on tokens * topk rows spread
+over the experts either exactly evenly or as one seeded multinomial draw
+(what uniform routing gives), and the median of --iters launches is
+reported.
 """
 
 from __future__ import annotations
@@ -33,7 +39,11 @@ def main():
     p.add_argument("--layout", default="b200", choices=["b200", "e2m1", "cm"])
     p.add_argument("--variant", type=int, default=0,
                    help="dwm_gmm_fp4_variant kernel choice (0 = automatic)")
+    p.add_argument("--groups", choices=["uniform", "multinomial"], default=None,
+                   help="time gmm1/gmm2 alone on these group sizes")
     a = p.parse_args()
+    if a.groups:
+        return gemm_only(a)
     e, h, i, t, k = a.experts, a.hidden, a.inter, a.tokens, a.topk
     w = synthetic.moe_weights(e, h, i, seed=a.seed, device="cuda")
     if a.layout == "b200":
@@ -88,6 +98,50 @@ def main():
         "gmm2_TFLOPs": round(2 * rows * i * h / m2 / 1e9, 1),
         "tokens_per_s": round(t / step * 1e3, 1),
     }))
+
+
+def gemm_only(a):
+    import numpy as np
+    e, h, i = a.experts, a.hidden, a.inter
+    rows = a.tokens * a.topk
+    w = synthetic.moe_weights(e, h, i, seed=a.seed, device="cuda")
+    w = w.to_b200() if a.layout == "b200" else w.to_cm() if a.layout == "cm" else w
+    if a.groups == "uniform":
+        gs_np = np.full(e, rows // e, np.int32)
+        gs_np[: rows - int(gs_np.sum())] += 1
+    else:
+        gs_np = np.random.default_rng(a.seed).multinomial(rows, [1.0 / e] * e).astype(np.int32)
+    gs = torch.from_numpy(gs_np).cuda()
+    x = torch.randn((rows, h), generator=torch.Generator().manual_seed(a.seed)).to(torch.bfloat16).cuda()
+    h1 = torch.empty((rows, i), dtype=torch.bfloat16, device="cuda")
+    y = torch.empty((rows, h), dtype=torch.bfloat16, device="cuda")
+
+    def g1():
+        ops.gmm_fp4_out(x, w.w13, w.s13, gs, h1, act=L.ACT_SWIGLU, layout=w.layout,
+                        variant=a.variant)
+
+    def g2():
+        ops.gmm_fp4_out(h1, w.w2, w.s2, gs, y, layout=w.layout, variant=a.variant)
+
+    res = {"experts": e, "rows": rows, "groups": a.groups, "max_group": int(gs_np.max()),
+           "min_group": int(gs_np.min())}
+    for f, name, flops in ((g1, "gmm1", 2.0 * rows * h * 2 * i), (g2, "gmm2", 2.0 * rows * i * h)):
+        for _ in range(a.warmup):
+            f()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(a.iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            f()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = float(np.median(ts))
+        res[f"{name}_ms"] = round(ms, 4)
+        res[f"{name}_TFLOPs"] = round(flops / ms / 1e9, 1)
+    L.raise_on_device_error()
+    print(json.dumps(res))
 
 
 if __name__ == "__main__":
