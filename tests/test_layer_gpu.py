@@ -93,6 +93,48 @@ def test_layer_graph_capture_replays_bitwise(dw):
     assert torch.equal(res.view(torch.int16), out.view(torch.int16))
 
 
+def test_layer_prefill_pair_kernel(dw):
+    """A prefill-sized layer (512 tokens, top-8 over 16 experts: ~256 rows
+    per expert) takes the GEMM on CTA pairs automatically: its output has the
+    single-CTA kernel's bits, replays bitwise from a CUDA graph, and matches
+    the oracle layer."""
+    from dw_tpu_b200 import synthetic
+    t, e, h, i, k = 512, 16, 512, 256, 8
+    w = synthetic.moe_weights(e, h, i, seed=8, device="cuda")
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 13, "cuda", lo=118,
+                                               hi=121))
+    raw, w = w, w.to_b200()
+    x, router = synthetic.layer_inputs(t, h, e, seed=8)
+    xc = x.cuda()
+    lc = (x.float() @ router.float()).to(torch.bfloat16).cuda()
+    auto = dw.MoELayer(w, k, t)
+    single = dw.MoELayer(w, k, t, gemm_variant=1)
+    out = auto(xc, lc)
+    ref_bits = single(xc, lc)
+    torch.cuda.synchronize()
+    from dw_tpu_b200 import _lib
+    _lib.raise_on_device_error()
+    assert int(auto.group_sizes.float().mean().item()) >= 128
+    assert torch.equal(out.view(torch.int16), ref_bits.view(torch.int16))
+    res = torch.empty_like(out)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        auto(xc, lc, out=res)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        auto(xc, lc, out=res)
+    res.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(res.view(torch.int16), out.view(torch.int16))
+    ref = O.fused_moe(bf16_to_np(x), bf16_to_np(lc.cpu()), raw.w13.cpu().numpy(),
+                      raw.s13.cpu().numpy(), raw.w2.cpu().numpy(), raw.s2.cpu().numpy(), k)
+    assert rel_fro(bf16_to_np(out), ref) < 2 * gemm_rel_tol(h)
+
+
 @pytest.mark.parametrize("layout,f32_reduce,limit", [("e2m1", False, None), ("b200", True, None),
                                                       ("b200", False, 7.0)])
 def test_one_call_layer_matches_layer_object(dw, layout, f32_reduce, limit):
