@@ -115,7 +115,7 @@ def load():
             if not os.path.exists(LIB_PATH):
                 raise ImportError(
                     f"{LIB_PATH} not found: build it with "
-                    "`python -m dw_tpu_b200.build` (nvcc, sm_100a)")
+                    "`python __graft_entry__.py` (nvcc, sm_100a)")
             lib = _c.CDLL(LIB_PATH)
             for name, (args, res) in SIGNATURES.items():
                 fn = getattr(lib, name, None)

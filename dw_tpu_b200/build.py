@@ -1,4 +1,6 @@
-"""Build libdw_moe.so in-tree for sm_100a (``python -m dw_tpu_b200.build``)."""
+"""Build libdw_moe.so in-tree for sm_100a: ``python dw_tpu_b200/build.py``
+(or ``python __graft_entry__.py``). Run it as a script: importing the
+package loads the library, which a fresh checkout does not have yet."""
 
 from __future__ import annotations
 
