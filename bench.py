@@ -16,6 +16,9 @@ Printed (rank 0, one JSON line): value (device-timed, inputs resident), e2e
 roofline of the dominant kernel (dw_moe gmm_fp4, timed with CUDA events on its
 stream), the CPU baseline (the NumPy oracle on the host cores, bounded
 sample), clocks sampled during the timed region and the kernel launch count.
+At N=1 the line also carries ``prefill``: the two grouped matmuls alone at
+one cfg3 rank's shape (32 of the experts, 8192 rows, i.e. 256 rows per
+expert), against the tensor roofline.
 
 ``--impl reference`` times the reference semantics on the host instead (the
 reference's JAX/Pallas path cannot run here; its NumPy restatement in
@@ -54,6 +57,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-experts", type=int, default=6,
                    help="experts whose GEMMs the CPU baseline times (then scaled)")
+    p.add_argument("--no-prefill", action="store_true",
+                   help="skip the prefill-sized GEMM measurement (N=1 only)")
     return p.parse_args()
 
 
@@ -188,6 +193,60 @@ def measured_peaks():
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except OSError:
         return None
+
+
+def prefill_gemm(weights, dev, seed, iters=10):
+    """The grouped matmuls at one cfg3 rank's shape at n=8 (32 local experts,
+    T=1024 tokens x top-8 = 8192 rows, 256 per expert on average): gmm1 with
+    SwiGLU and gmm2 on the first 32 experts of the bench's weights, with
+    groups of exactly 256 rows and with one seeded multinomial draw (uniform
+    routing). Median of `iters` launches (CUDA events) after 3 warm-ups; the
+    weights (0.43 GB) exceed L2. TFLOP/s against the measured bf16 peak."""
+    import torch
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    e, rows = 32, 1024 * TOPK
+    w = dw.FP4MoEWeights(weights.w13[:e], weights.s13[:e], weights.w2[:e], weights.s2[:e],
+                         weights.layout)
+    x = torch.randn((rows, H), generator=torch.Generator().manual_seed(seed)).to(
+        torch.bfloat16).to(dev)
+    h1 = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((rows, H), dtype=torch.bfloat16, device=dev)
+    peaks = measured_peaks()
+    peak = peaks["bf16_tflops"] if peaks else 1590.0
+    out = {"workload": "cfg3 rank at n=8: 32 experts, 8192 rows, H=4096, I=2048",
+           "bound": "tensor", "peak": peak, "unit": "TFLOP/s",
+           "peak_source": "measured burst" if peaks else "fallback",
+           "kernel": "dw_moe gmm_fp4 (automatic choice: tcgen05 on CTA pairs)"}
+    for kind in ("uniform", "multinomial"):
+        if kind == "uniform":
+            gs_np = np.full(e, rows // e, np.int32)
+        else:
+            gs_np = np.random.default_rng(seed).multinomial(rows, [1.0 / e] * e).astype(np.int32)
+        gs = torch.from_numpy(gs_np).to(dev)
+        for name, fn, flops in (
+                ("gmm1", lambda: ops.gmm_fp4_out(x, w.w13, w.s13, gs, h1, act=L.ACT_SWIGLU,
+                                                 layout=w.layout), 2.0 * rows * H * 2 * I),
+                ("gmm2", lambda: ops.gmm_fp4_out(h1, w.w2, w.s2, gs, y, layout=w.layout),
+                 2.0 * rows * I * H)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            ts = []
+            for _ in range(iters):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                ts.append(e0.elapsed_time(e1))
+            tf = flops / statistics.median(ts) / 1e9
+            out[f"{kind}_{name}_tflops"] = round(tf, 1)
+            out[f"{kind}_{name}_frac"] = round(tf / peak, 4)
+    L.raise_on_device_error()
+    return out
 
 
 def run_ours(args, rank, world, local_rank):
@@ -368,6 +427,8 @@ def run_ours(args, rank, world, local_rank):
             "link_peak_GBps": 770.0,
         }
         ep_ctx.close()
+    if world == 1 and not args.no_prefill:
+        res["prefill"] = prefill_gemm(weights, dev, args.seed)
     return res
 
 
@@ -436,6 +497,8 @@ def main():
     }
     if "exchange" in res:
         line["exchange"] = res["exchange"]
+    if "prefill" in res:
+        line["prefill"] = res["prefill"]
     print(json.dumps(line), flush=True)
 
 
