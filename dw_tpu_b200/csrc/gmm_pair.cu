@@ -538,6 +538,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int b = dw;
     const int p = act ? 2 * (b & 3) + (b >> 2) : b;
     const int gid = lane >> 2, tig = lane & 3;
+    const DecodeRegs dregs = DecodeRegs::make();  // decode constants held in registers
     const int r0 = 16 * p + gid;  // A rows r0 and r0 + 8
     const int row_a_off = (r0 >> 3) * 1024 + (r0 & 7) * 128;
     const int row_b_off = ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
@@ -558,28 +559,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
         const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE;
         uint8_t* astage = smem + L::OFF_STAGE + st * STAGE;
-        uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
-        bool two = false;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          two |= col_mult<SD, DELTA>(sstage + (h * ROWS + 16 * b + gid) * es, m1[h][0], m2[h][0]);
-          two |= col_mult<SD, DELTA>(sstage + (h * ROWS + 16 * b + gid + 8) * es, m1[h][1],
-                                     m2[h][1]);
-        }
+        // The four lanes of a quad (same gid) need the same four scales: k32
+        // half h, column gid + 8c. Lane tig converts scale (h, c) = (tig >> 1,
+        // tig & 1) and the quad exchanges the multipliers.
+        uint32_t m1s, m2s;
+        const bool two = col_mult<SD, DELTA>(
+            sstage + ((tig >> 1) * ROWS + 16 * b + gid + 8 * (tig & 1)) * es, m1s, m2s);
         const bool two_any = __any_sync(0xffffffffu, two);
-        if (two_any && SD == DWM_U8) {
+        uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int c = 0; c < 2; ++c) m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
-        }
+          for (int c = 0; c < 2; ++c) {
+            const int src = (lane & ~3) + 2 * h + c;
+            if (two_any) {  // both multiplies: 2^(126 - delta), then the scale
+              m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
+              m2[h][c] = __shfl_sync(0xffffffffu, m2s, src);
+            } else {
+              m1[h][c] = __shfl_sync(0xffffffffu, m1s, src);
+              m2[h][c] = 0u;
+            }
+          }
         uint8_t* row_a = astage + row_a_off;
         uint8_t* row_b = astage + row_b_off;
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
           const uint32_t w = *reinterpret_cast<const uint32_t*>(cstage + kb * 128 + lane * 4);
           uint32_t tv[4];
-          tvals<true>(w, tv);
+          tvals_b200(w, dregs, tv);
           const int h = kb >> 1;
           uint32_t v0 = hmul2_bf16(tv[0], m1[h][0]);
           uint32_t v1 = hmul2_bf16(tv[1], m1[h][1]);
