@@ -778,6 +778,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       // eight gid rows land on eight different 16-byte chunks).
       const int sub = dw >> 2;
       const int gid = lane >> 2, tig = lane & 3;
+      const DecodeRegs dregs = DecodeRegs::make();  // decode constants held in registers
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         for (int kk = 0; kk < KT; ++kk, ++step) {
           if ((int)(step & 1) != grp) continue;
@@ -796,22 +797,27 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
 #pragma unroll
           for (int bi = 0; bi < 2; ++bi) {
             const int cbl = 2 * (dw & 3) + bi;  // column block inside the sub-tile
-            uint32_t m1[2][2], m2[2][2];         // [k32 half][column gid / gid+8]
-            bool two = false;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              two |= col_mult<SD, DELTA>(sstage + (h * BW + 16 * cbl + gid) * es, m1[h][0],
-                                         m2[h][0]);
-              two |= col_mult<SD, DELTA>(sstage + (h * BW + 16 * cbl + gid + 8) * es, m1[h][1],
-                                         m2[h][1]);
-            }
+            // The four lanes of a quad (same gid) need the same four scales:
+            // k32 half h, column gid + 8c. Lane tig converts scale (h, c) =
+            // (tig >> 1, tig & 1) and the quad exchanges the multipliers.
+            uint32_t m1s, m2s;
+            const bool two = col_mult<SD, DELTA>(
+                sstage + ((tig >> 1) * BW + 16 * cbl + gid + 8 * (tig & 1)) * es, m1s, m2s);
             const bool two_any = __any_sync(0xffffffffu, two);
-            if (two_any && SD == DWM_U8) {
+            uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int c = 0; c < 2; ++c) m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
-            }
+              for (int c = 0; c < 2; ++c) {
+                const int src = (lane & ~3) + 2 * h + c;
+                if (two_any) {  // both multiplies: 2^(126 - delta), then the scale
+                  m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
+                  m2[h][c] = __shfl_sync(0xffffffffu, m2s, src);
+                } else {
+                  m1[h][c] = __shfl_sync(0xffffffffu, m1s, src);
+                  m2[h][c] = 0u;
+                }
+              }
             const int r0 = 16 * cbl + gid;  // A rows r0 and r0 + 8
             uint8_t* row_a = asub + (r0 >> 3) * 1024 + (r0 & 7) * 128;
             uint8_t* row_b = asub + ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
@@ -820,7 +826,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
               const uint32_t w = *reinterpret_cast<const uint32_t*>(cstage + cbl * 512 +
                                                                     kb * 128 + lane * 4);
               uint32_t tv[4];
-              tvals<true>(w, tv);
+              tvals_b200(w, dregs, tv);
               const int h = kb >> 1;
               uint32_t v0 = hmul2_bf16(tv[0], m1[h][0]);
               uint32_t v1 = hmul2_bf16(tv[1], m1[h][1]);
