@@ -88,8 +88,9 @@ int dwm_device_status(void* stream, int* bits);
  *   codes   DWM_FP4_E2M1: uint8 [num_local_groups, k, n/2], two e2m1 nibbles
  *           per byte, element 2j in the low nibble; DWM_FP4_B200: the same
  *           values re-laid by dwm_fp4_to_b200 (faster decode); DWM_FP4_CM:
- *           re-laid by dwm_fp4_to_cm (decoded into TMEM, for prefill-sized
- *           groups); convert tokamax codes once with dwm_fp4_codes_convert
+ *           re-laid by dwm_fp4_to_cm (read by variant 6, which decodes into
+ *           TMEM; DWM_FP4_B200 is as fast or faster at every group size);
+ *           convert tokamax codes once with dwm_fp4_codes_convert
  *   scales  [num_local_groups, k/32, n] of scale_dtype: DWM_U8 (E8M0 codes,
  *           KE:37-40), DWM_BF16 or DWM_F32 (cast to bf16 before use)
  *   group_sizes int32 [num_groups] on the device
