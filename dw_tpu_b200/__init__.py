@@ -10,13 +10,14 @@ names:
 * ``e8m0_encode`` / ``e8m0_decode``
 * ``route_topk``, ``MoELayer`` / ``fused_moe_func``
 
-Importing the package loads the library and raises if it is missing: there
-is no CPU or library fallback.
+Importing the package checks that the library has been built and raises if
+it is missing; the library itself is mapped on the first op call. There is no
+CPU or library fallback.
 """
 
 from . import _lib
 
-_lib.load()
+_lib.require_built()
 
 from .e8m0_scale import e8m0_decode, e8m0_encode  # noqa: E402
 from .fused_moe import FP4MoEWeights, MoELayer, fused_moe_func  # noqa: E402

@@ -35,8 +35,7 @@ ACT_SWIGLU_CLAMP = 2
 FP4_E2M1 = 0
 FP4_TOKAMAX = 1
 FP4_B200 = 2
-FP4_CM = 3
-LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200, "cm": FP4_CM}
+LAYOUTS = {"e2m1": FP4_E2M1, "b200": FP4_B200}
 SCORE_SOFTMAX = 0
 SCORE_SIGMOID = 1
 SCORE_SQRTSOFTPLUS = 2
@@ -65,7 +64,6 @@ SIGNATURES = {
                     _I),
     "dwm_fp4_dequant": ([_P, _I, _P, _I, _I, _I, _I, _P, _P], _I),
     "dwm_fp4_to_b200": ([_P, _P, _I, _I, _I, _I, _P], _I),
-    "dwm_fp4_to_cm": ([_P, _P, _I, _I, _I, _I, _P], _I),
     "dwm_gmm_fp4_variant": ([_P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P,
                              _I, _P], _I),
     "dwm_fp4_codes_convert": ([_P, _P, _SZ, _I, _I, _P], _I),
@@ -94,6 +92,7 @@ SIGNATURES = {
     "dwm_ep_dispatch": ([_P, _P, _P, _I, _P, _I, _P], _I),
     "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
     "dwm_ep_combine_shared": ([_P, _P, _I, _P, _I, _P, _I, _F, _I, _P, _I, _I, _P], _I),
+    "dwm_ep_set_wait_limit": ([_P, _c.c_uint64], _I),
     "dwm_ep_destroy": ([_P], _I),
 }
 
@@ -105,17 +104,22 @@ class DeviceError(RuntimeError):
     """A kernel reported a device-side fault through the status word."""
 
 
+def require_built() -> None:
+    """Raise ImportError if libdw_moe.so has not been built (without mapping it)."""
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} not found: build it with `python __graft_entry__.py` (nvcc, sm_100a)")
+
+
 def load():
-    """Load libdw_moe.so once; raise ImportError if it is absent."""
+    """Map libdw_moe.so once (on the first op call); raise ImportError if it
+    is absent."""
     global _lib
     if _lib is not None:
         return _lib
     with _lock:
         if _lib is None:
-            if not os.path.exists(LIB_PATH):
-                raise ImportError(
-                    f"{LIB_PATH} not found: build it with "
-                    "`python __graft_entry__.py` (nvcc, sm_100a)")
+            require_built()
             lib = _c.CDLL(LIB_PATH)
             for name, (args, res) in SIGNATURES.items():
                 fn = getattr(lib, name, None)

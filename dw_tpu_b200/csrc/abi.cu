@@ -4,7 +4,10 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "common.cuh"
 
@@ -16,11 +19,13 @@ thread_local char g_last_error[512] = "";
 __device__ int g_status;
 
 constexpr int kMaxDevices = 64;
-int* g_status_addr[kMaxDevices] = {};
-int g_num_sms[kMaxDevices] = {};
+std::atomic<int*> g_status_addr[kMaxDevices] = {};
+std::atomic<int> g_num_sms[kMaxDevices] = {};
 std::mutex g_mu;
+std::set<std::tuple<int, const void*, int>> g_smem_set;  // (device, kernel, bytes) done
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
+std::atomic<PFN_cuCtxGetCurrent_v4000> g_ctx_current{nullptr};
 
 }  // namespace
 
@@ -43,44 +48,73 @@ int check_cuda(cudaError_t e, const char* what) {
 int* status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (g_status_addr[dev]) return g_status_addr[dev];
+  if (int* p = g_status_addr[dev].load(std::memory_order_acquire)) return p;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_status_addr[dev]) {
+  if (!g_status_addr[dev].load(std::memory_order_relaxed)) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
-    g_status_addr[dev] = static_cast<int*>(p);
+    g_status_addr[dev].store(static_cast<int*>(p), std::memory_order_release);
   }
-  return g_status_addr[dev];
+  return g_status_addr[dev].load(std::memory_order_relaxed);
 }
 
 int num_sms() {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < kMaxDevices && g_num_sms[dev]) return g_num_sms[dev];
+  if (dev >= 0 && dev < kMaxDevices) {
+    const int n = g_num_sms[dev].load(std::memory_order_relaxed);
+    if (n) return n;
+  }
   int n = 0;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   if (n <= 0) n = 148;
-  if (dev >= 0 && dev < kMaxDevices) g_num_sms[dev] = n;
+  if (dev >= 0 && dev < kMaxDevices) g_num_sms[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
+int set_smem_limit(const void* kernel, int bytes, const char* what) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  const auto key = std::make_tuple(dev, kernel, bytes);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_smem_set.count(key)) return DWM_OK;
+  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                  what);
+  if (!rc) g_smem_set.insert(key);
+  return rc;
+}
+
 namespace {
-int resolve_encode() {
-  if (!g_encode) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_encode) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q;
-      cudaError_t e =
-          cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
-        return set_error(DWM_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+// Resolves a driver entry point through the runtime (no -lcuda link), once.
+template <typename PFN>
+int resolve_driver_fn(std::atomic<PFN>& slot, const char* name) {
+  if (slot.load(std::memory_order_acquire)) return DWM_OK;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!slot.load(std::memory_order_relaxed)) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(DWM_ERR_UNSUPPORTED, "%s unavailable", name);
+    slot.store(reinterpret_cast<PFN>(fn), std::memory_order_release);
   }
   return DWM_OK;
 }
+
+int resolve_encode() { return resolve_driver_fn(g_encode, "cuTensorMapEncodeTiled"); }
 }  // namespace
+
+int current_context(void** ctx) {
+  *ctx = nullptr;
+  int rc = resolve_driver_fn(g_ctx_current, "cuCtxGetCurrent");
+  if (rc) return rc;
+  CUcontext c = nullptr;
+  if (g_ctx_current.load(std::memory_order_acquire)(&c) != CUDA_SUCCESS || !c)
+    return set_error(DWM_ERR_STATE, "no current CUDA context");
+  *ctx = c;
+  return DWM_OK;
+}
 
 int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                    const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
@@ -96,7 +130,7 @@ int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const 
     estr[i] = 1;
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
-  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), d, st, b, estr,
+  CUresult r = g_encode.load(std::memory_order_acquire)(map, dtype, rank, const_cast<void*>(base), d, st, b, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -114,7 +148,7 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = g_encode.load(std::memory_order_acquire)(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)

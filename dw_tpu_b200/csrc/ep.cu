@@ -38,8 +38,8 @@
 //   + sum of lower ranks' counts of its expert
 //   + its rank among the source's own pairs of that expert (stable).
 //
-// Waits are bounded (2 s, then DWM_DEV_TIMEOUT in the status word and the
-// kernel winds down). Every wait depends only on kernels of other ranks or of
+// Waits are bounded (2 s by default, dwm_ep_set_wait_limit; then
+// DWM_DEV_TIMEOUT in the status word and the kernel winds down). Every wait depends only on kernels of other ranks or of
 // earlier launches, never on a particular CTA of the same grid: the counts are
 // published by whichever CTA starts first, and only the last CTA to finish
 // waits for the arrivals. Counters are monotonic and tagged with a
@@ -86,6 +86,7 @@ struct Params {
   int64_t cap;
   int32_t* sent;  // [max_pairs]: owner << ROW_BITS | row of each own pair, -1 if dropped
   uint32_t* ctl;  // [CTL_WORDS]
+  uint64_t wait_ns;  // limit of every device-side wait (dwm_ep_set_wait_limit)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -119,27 +120,30 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
   return old;
 }
 
-// Bounded spin until *p >= target (32-bit epoch flag).
-__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t target, int* status) {
+// Bounded spin until *p >= target (32-bit epoch flag); gives up after `limit`
+// ns (DWM_DEV_TIMEOUT).
+__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t target, uint64_t limit,
+                                          int* status) {
   if (ld_acquire_sys(p) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     __nanosleep(32);
     if (ld_acquire_sys(p) >= target) return true;
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit) {
       report(status, DWM_DEV_TIMEOUT);
       return false;
     }
   }
 }
 
-__device__ __forceinline__ bool wait_count(const uint64_t* p, uint64_t target, int* status) {
+__device__ __forceinline__ bool wait_count(const uint64_t* p, uint64_t target, uint64_t limit,
+                                           int* status) {
   if (ld_acquire_sys64(p) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     __nanosleep(32);
     if (ld_acquire_sys64(p) >= target) return true;
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit) {
       report(status, DWM_DEV_TIMEOUT);
       return false;
     }
@@ -147,7 +151,8 @@ __device__ __forceinline__ bool wait_count(const uint64_t* p, uint64_t target, i
 }
 
 // Bounded spin until the tagged count word carries `epoch`; its count or -1.
-__device__ __forceinline__ int wait_tagged(const uint64_t* p, uint32_t epoch, int* status) {
+__device__ __forceinline__ int wait_tagged(const uint64_t* p, uint32_t epoch, uint64_t limit,
+                                          int* status) {
   uint64_t v = ld_relaxed_sys64(p);
   if ((uint32_t)(v >> 32) == epoch) return (int)(uint32_t)v;
   const uint64_t t0 = globaltimer_ns();
@@ -155,7 +160,7 @@ __device__ __forceinline__ int wait_tagged(const uint64_t* p, uint32_t epoch, in
     __nanosleep(32);
     v = ld_relaxed_sys64(p);
     if ((uint32_t)(v >> 32) == epoch) return (int)(uint32_t)v;
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit) {
       report(status, DWM_DEV_TIMEOUT);
       return -1;
     }
@@ -249,7 +254,7 @@ __global__ void __launch_bounds__(XFER_THREADS)
       for (int s = 0; s < P.world; ++s) {
         int v = tot[x];
         if (s != P.rank) {
-          v = wait_tagged(count_word(P, P.rank, s, x), epoch, status);
+          v = wait_tagged(count_word(P, P.rank, s, x), epoch, P.wait_ns, status);
           if (v < 0) {
             s_fail = 1;
             v = 0;
@@ -346,7 +351,7 @@ __global__ void __launch_bounds__(XFER_THREADS)
           red_release_sys_add(reinterpret_cast<uint64_t*>(P.peer[p] + P.L.arrive), 1);
       if (ph & DWM_EP_WAIT)
         wait_count(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.arrive),
-                   (uint64_t)epoch * P.world, status);
+                   (uint64_t)epoch * P.world, P.wait_ns, status);
     }
   }
 }
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
       if (k0 == 0) {  // the peers' outputs: wait once for their announcements
         if (tid < P.world && tid != P.rank &&
             !wait_flag(reinterpret_cast<const uint32_t*>(P.peer[P.rank] + P.L.ready) + tid,
-                       s_epoch, status))
+                       s_epoch, P.wait_ns, status))
           s_ok = 0;
         __syncthreads();
       }
@@ -466,6 +471,7 @@ struct dwm_ep {
   bool connected = false;
   bool dispatched = false;  // a COUNTS phase was issued (host-side state check only)
   int last_t = -1;          // tokens of the current dispatch
+  uint64_t wait_ns = kWaitLimitNs;  // device-side wait limit
 };
 
 namespace {
@@ -484,6 +490,7 @@ ep::Params make_params(const dwm_ep* c) {
   P.topk = c->topk;
   P.T = c->last_t < 0 ? 0 : c->last_t;
   P.cap = c->cap;
+  P.wait_ns = c->wait_ns;
   P.sent = c->scratch;
   P.ctl = reinterpret_cast<uint32_t*>(c->scratch + c->max_pairs);
   return P;
@@ -712,6 +719,14 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
                               int w_dtype, void* out, int out_dtype, int phases, void* stream) {
   return dwm_ep_combine_shared(c, y, y_dtype, topk_weights, w_dtype, nullptr, DWM_F32, 1.0f,
                                DWM_BF16, out, out_dtype, phases, stream);
+}
+
+extern "C" int dwm_ep_set_wait_limit(dwm_ep* c, uint64_t limit_ns) {
+  DWM_CHECK_ARG(c, "NULL ep context");
+  DWM_CHECK_ARG(limit_ns >= 1000 && limit_ns <= 60000000000ull,
+                "wait limit %llu ns out of [1 us, 60 s]", (unsigned long long)limit_ns);
+  c->wait_ns = limit_ns;
+  return DWM_OK;
 }
 
 extern "C" int dwm_ep_destroy(dwm_ep* c) {

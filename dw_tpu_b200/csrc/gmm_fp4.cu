@@ -46,26 +46,20 @@ namespace gmm {
 
 using namespace fp4;
 
-enum Variant { kMN = 0, kKS = 1, kTS = 2 };
+enum Variant { kMN = 0, kKS = 1 };
 
 constexpr int NSUB = 2;    // sub-tiles (accumulators) per tile
 constexpr int BW = 128;    // weight columns per sub-tile (UMMA M)
 constexpr int BK = 64;     // K per pipeline stage (128 bytes of bf16)
+constexpr int BT = 128;    // token rows per tile at most (the UMMA N)
 constexpr int NUM_THREADS = 768;
-// The TMEM-A variant (one accumulator buffer, so the epilogue is serialised
-// with the main loop) adds warps 24-27 as a second epilogue set: warp e and
-// e + 24 drain alternate 16-token chunks of TMEM lane quarter e.
-constexpr int EPI2_WARP0 = 24;
-template <int VAR>
-constexpr int num_threads() { return VAR == 2 ? 896 : NUM_THREADS; }
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
 constexpr int TOKEN_WARP = 6;
-constexpr int MMA_WARP2 = 7;  // the TMEM variant's second UMMA issuer (sub-tile 1)
 constexpr int DEC_WARP0 = 8;
 constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
 constexpr int MAX_GROUPS = 1024;
-constexpr int TMEM_COLS = 512;    // NBUF buffers x NSUB x BT f32 columns
+constexpr int TMEM_COLS = 512;    // two buffers x NSUB x BT f32 columns
 
 constexpr int A_SUB_BYTES = BW * BK * 2;     // 16 KiB bf16 sub-tile
 constexpr int A_STAGE = NSUB * A_SUB_BYTES;  // 32 KiB
@@ -103,8 +97,7 @@ constexpr int EPI_WARP_BYTES = EPI_ROWS * 32 * 4;
 // reaches shared memory from L2 only after the UMMAs of the stage it
 // replaces have completed, so its latency has to be covered by the stages
 // ahead of it: 4 stages of 128 rows (2 A stages, 8 code stages) measured
-// 599 TFLOP/s against 562 with 3 (3 A stages); 256-row tiles take 3 token
-// stages of 32 KiB at the cost of the code ring.
+// 599 TFLOP/s against 562 with 3 (3 A stages).
 #ifndef DWM_GMM_TS
 #define DWM_GMM_TS 4
 #endif
@@ -114,48 +107,25 @@ constexpr int EPI_WARP_BYTES = EPI_ROWS * 32 * 4;
 #ifndef DWM_GMM_CS
 #define DWM_GMM_CS 8
 #endif
-// The same for 256-row tiles.
-#ifndef DWM_GMM_TS256
-#define DWM_GMM_TS256 3
-#endif
-#ifndef DWM_GMM_AS256
-#define DWM_GMM_AS256 2
-#endif
-#ifndef DWM_GMM_CS256
-#define DWM_GMM_CS256 3
-#endif
-// BT = token rows per tile (the UMMA N): 128 (two TMEM accumulator buffers,
-// the epilogue overlaps the next tile) or 256 (one buffer; every weight
-// column is decoded once per 256 rows and each UMMA does twice the work).
-// kTS keeps the decoded A tiles in TMEM: columns [0, NSUB*BT) hold the one
-// accumulator buffer, then A stage as, sub-tile s at TS_A_COL0 + (as*NSUB +
-// s) * 32 (128 lanes x 64 k as bf16 pairs); no A tiles in shared memory,
-// whose room goes to the token ring.
-constexpr int TS_A_COL0 = NSUB * 128;
-constexpr int TS_AS = (TMEM_COLS - TS_A_COL0) / (NSUB * 32);  // 4
-#ifndef DWM_GMM_TS_TS
-#define DWM_GMM_TS_TS 3
-#endif
-template <int SD, int BT, int VAR = kKS>
+// Two TMEM accumulator buffers, so a tile's epilogue overlaps the next
+// tile's main loop.
+template <int SD>
 struct Smem {
-  static constexpr bool TMEM_A = VAR == kTS;
-  static constexpr int TS = TMEM_A ? DWM_GMM_TS_TS : BT == 128 ? DWM_GMM_TS : DWM_GMM_TS256;
-  static constexpr int AS = TMEM_A ? TS_AS : BT == 128 ? DWM_GMM_AS : DWM_GMM_AS256;
-  // A token stage: BT/16 boxes of 16 rows x 64 k (one k-step of a full
-  // tile), two k-steps with the decoded A in TMEM, where the single MMA thread
-  // is the bottleneck and a token stage's wait and commit cost it ~150 cycles.
-  static constexpr int T_STAGE = (TMEM_A ? 2 : 1) * BT * BK * 2;
+  static constexpr int TS = DWM_GMM_TS;
+  static constexpr int AS = DWM_GMM_AS;
+  // A token stage: BT/16 boxes of 16 rows x 64 k (one k-step of a full tile).
+  static constexpr int T_STAGE = BT * BK * 2;
   static constexpr int T_BOXES = T_STAGE / T_BOX_BYTES;
-  static constexpr int NBUF = TMEM_A ? 1 : TMEM_COLS / (NSUB * BT);
+  static constexpr int NBUF = TMEM_COLS / (NSUB * BT);
   // Code ring: 8 stages (6 with f32 scales, 7 with bf16 scales, to fit the
   // epilogue's staging tiles in shared memory).
-  static constexpr int CS_BASE = BT == 128 ? DWM_GMM_CS : DWM_GMM_CS256;
+  static constexpr int CS_BASE = DWM_GMM_CS;
   static constexpr int CS = ScaleTraits<SD>::bytes == 4   ? (CS_BASE * 3 + 3) / 4
                             : ScaleTraits<SD>::bytes == 2 ? CS_BASE - (CS_BASE > 4)
                                                           : CS_BASE;
   static constexpr int S_STAGE = NSUB * 2 * BW * ScaleTraits<SD>::bytes;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_T = OFF_A + (TMEM_A ? 0 : AS * A_STAGE);
+  static constexpr int OFF_T = OFF_A + AS * A_STAGE;
   static constexpr int OFF_C = OFF_T + TS * T_STAGE;
   static constexpr int OFF_S = OFF_C + CS * C_STAGE;
   static constexpr int OFF_BAR = OFF_S + CS * S_STAGE;
@@ -164,7 +134,7 @@ struct Smem {
   static constexpr int OFF_ROWS = OFF_MISC + 32;
   static constexpr int OFF_TILES = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int OFF_EPI = (OFF_TILES + (MAX_GROUPS + 1) * 4 + 15) & ~15;
-  static constexpr int EPI_WARPS = TMEM_A ? 8 : 4;
+  static constexpr int EPI_WARPS = 4;
   static constexpr int BYTES = OFF_EPI + EPI_WARPS * EPI_WARP_BYTES;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
@@ -195,7 +165,6 @@ struct Tile {
   int n_idx;  // column tile
 };
 
-template <int BT>
 __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
                                          const Args& a) {
   int lo = 0, hi = a.n_local;  // tile_prefix[lo] <= idx < tile_prefix[hi]
@@ -250,17 +219,12 @@ __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint6
   return *slot != 0;
 }
 
-template <int SD, int VAR, int BT>
-__global__ void __launch_bounds__(num_threads<VAR>(), 1)
+template <int SD, int VAR>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
-  using L = Smem<SD, BT, VAR>;
-  static_assert(VAR != kTS || BT == 128, "kTS runs 128-row tiles");
-  // The TMEM variant issues its UMMAs from two threads (warps 5 and 7), one
-  // per sub-tile, so that one thread's barrier waits and commits (~500
-  // cycles a stage) overlap the other's UMMAs; each commits its own.
-  constexpr int MMA_ISSUERS = VAR == kTS ? 2 : 1;
+  using L = Smem<SD>;
   constexpr int CS = L::CS;
   constexpr int TS = L::TS;
   constexpr int AS = L::AS;
@@ -296,17 +260,17 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
     }
     for (int i = 0; i < TS; ++i) {
       mbar_init(&tk_full[i], 1);
-      mbar_init(&tk_empty[i], MMA_ISSUERS);
+      mbar_init(&tk_empty[i], 1);
     }
     for (int i = 0; i < AS; ++i) {
       mbar_init(&a_full[i], NUM_DEC_WARPS);
-      mbar_init(&a_empty[i], MMA_ISSUERS);
+      mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], MMA_ISSUERS);
+      mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], L::EPI_WARPS);
     }
-    mbar_init(drain_bar, MMA_ISSUERS);
+    mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -387,13 +351,11 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
   const int total = tile_prefix[a.n_local];
   const int KT = a.k / BK;
 
-  if (warp < 4 || warp >= EPI2_WARP0) {
+  if (warp < 4) {
     // ---------------- epilogue ----------------
     const int es = a.out_f32 ? 4 : 2;
-    const int eq = warp & 3;                             // TMEM lane quarter
-    const int eset = warp >= EPI2_WARP0 ? 1 : 0;         // which epilogue set
-    const int nsets = L::EPI_WARPS / 4;
-    if (a.zero_init && eset == 0) {
+    const int eq = warp;  // TMEM lane quarter
+    if (a.zero_init) {
       // Rows outside the local groups: [0, lo) and [hi, m).
       const int lo = row_start[a.group_offset];
       const int hi = row_start[a.group_offset + a.n_local];
@@ -406,13 +368,12 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       for (int64_t i = (int64_t)hi * n16 + tid; i < (int64_t)a.m * n16; i += stride) o[i] = z;
     }
     const int mrow = eq * 32 + lane;  // TMEM lane = A row = weight column slot
-    const uint32_t epi_s =
-        smem_u32(smem + L::OFF_EPI + (eset * 4 + eq) * EPI_WARP_BYTES);
+    const uint32_t epi_s = smem_u32(smem + L::OFF_EPI + eq * EPI_WARP_BYTES);
     const int col = VAR == kMN ? (mrow & ~7) + perm8(mrow & 7) : mrow;
     constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
     int it = 0;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++it) {
-      const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
+      const Tile t = get_tile(idx, row_start, tile_prefix, a);
       const int buf = it % NBUF;
       const uint32_t ph = (it / NBUF) & 1;
       const bool got = mbar_wait<DWM_GMM_EPI_SLEEP>(&acc_full[buf], ph, abort_flag, a.status);
@@ -430,7 +391,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       const int lcol = col - eq * 32;  // this lane's column inside the warp's 32
       const int row_bytes = 32 * es;     // one staged row: 64 or 128 bytes
       const int vec_per_row = row_bytes / 16;
-      for (int c = eset; c < nchunks; c += nsets) {
+      for (int c = 0; c < nchunks; ++c) {
         uint32_t r0[16], r1[16];
         tmem_ld16(tbase + c * 16, r0);
         tmem_ld16(tbase + BT + c * 16, r1);
@@ -493,7 +454,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       const int half = a.n / 2;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
         int col[NSUB];
         if (a.act == DWM_ACT_NONE) {
           col[0] = t.n_idx * (NSUB * BW);
@@ -517,9 +478,6 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
             if constexpr (VAR == kMN)  // [g*k + kk, n/2 bytes]: 64 rows x 64 bytes
               tma_load_2d(cdst + s * C_SUB_BYTES, &tm_codes, &cs_full[cs], col[s] / 2,
                           t.g * a.k + kk * BK, pol_stream);
-            else if constexpr (VAR == kTS)  // [g*n + column, k/8 words]: 128 columns x 8 words
-              tma_load_2d(cdst + s * C_SUB_BYTES, &tm_codes, &cs_full[cs], kk * (BK / 8),
-                          t.g * a.n + col[s], pol_stream);
             else  // [g*n/16 + block, (k/16)*32 words]: 8 column blocks x 4 k-blocks
               tma_load_2d(cdst + s * C_SUB_BYTES, &tm_codes, &cs_full[cs], kk * 4 * 32,
                           t.g * (a.n / 16) + col[s] / 16, pol_stream);
@@ -543,7 +501,7 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       uint32_t ts_ph = 0, ts_armed = 0, ts_par = 0;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
         const int nb = (t.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
         int nbp;
         const int kspan = token_span(nb, nbp, L::T_BOXES);
@@ -567,17 +525,15 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
       for (int s = 0; s < TS; ++s)
         if (ts_armed & (1u << s)) mbar_wait(&tk_full[s], (ts_par >> s) & 1, nullptr, a.status);
     }
-  } else if (warp == MMA_WARP || (MMA_ISSUERS == 2 && warp == MMA_WARP2)) {
-    // ---------------- UMMA issuer(s) ----------------
-    const int s_lo = MMA_ISSUERS == 2 && warp == MMA_WARP2 ? 1 : 0;
-    const int s_hi = MMA_ISSUERS == 2 ? s_lo + 1 : NSUB;
+  } else if (warp == MMA_WARP) {
+    // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       int as = 0, ts = 0;
       uint32_t as_ph = 0, ts_ph = 0;
       int it = 0;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
-        const Tile t = get_tile<BT>(idx, row_start, tile_prefix, a);
+        const Tile t = get_tile(idx, row_start, tile_prefix, a);
         const int nmma = (t.rows + 15) & ~15;
         const int nb = nmma / T_BOX_ROWS;
         int nbp;
@@ -605,17 +561,12 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bdesc = smem_desc_sw128(t_base + j * 32, 16, 1024);
-            for (int s = s_lo; s < s_hi; ++s) {
-              if constexpr (VAR == kTS) {
-                const uint32_t a_tm = tmem + (uint32_t)(TS_A_COL0 + (as * NSUB + s) * 32 + j * 8);
-                umma_ts_bf16(d0 + s * BT, a_tm, bdesc, idesc, (kk | j) != 0);
-              } else {
-                const uint64_t adesc =
-                    VAR == kMN
-                        ? smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 2048, A_LBO_MN, A_SBO_MN)
-                        : smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 32, 16, 1024);
-                umma_bf16(d0 + s * BT, adesc, bdesc, idesc, (kk | j) != 0);
-              }
+            for (int s = 0; s < NSUB; ++s) {
+              const uint64_t adesc =
+                  VAR == kMN
+                      ? smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 2048, A_LBO_MN, A_SBO_MN)
+                      : smem_desc_sw128(a_base + s * A_SUB_BYTES + j * 32, 16, 1024);
+              umma_bf16(d0 + s * BT, adesc, bdesc, idesc, (kk | j) != 0);
             }
           }
           umma_commit(&a_empty[as]);
@@ -700,67 +651,6 @@ __global__ void __launch_bounds__(num_threads<VAR>(), 1)
             run(std::false_type{});
           }
           fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&cs_empty[cs]);
-            mbar_arrive(&a_full[as]);
-          }
-        }
-      }
-    } else if constexpr (VAR == kTS) {
-      // CM layout, decoded A in TMEM: the thread of lane `lane` in warp dw
-      // owns A row r = 32 (warp % 4) + lane of sub-tile dw / 4 (its TMEM lane
-      // quarter is warp % 4), i.e. one weight column. Per stage it reads the
-      // column's 8 code words (64 k, 32 bytes), decodes and scales them into
-      // 32 bf16 pairs, and writes them to the A slot with one tcgen05.st.
-      const int q = warp & 3;
-      const int sub = dw >> 2;
-      const int r = q * 32 + lane;
-      constexpr int es = ScaleTraits<SD>::bytes;
-      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        for (int kk = 0; kk < KT; ++kk, ++step) {
-          if ((int)(step & 1) != grp) continue;
-          const int cs = (int)(step % CS);
-          const uint32_t cs_ph = (step / CS) & 1;
-          const int as = (int)(step % AS);
-          const uint32_t as_ph = (step / AS) & 1;
-          if (!group_wait<DWM_GMM_DEC_SLEEP>(grp, dw, step, &cs_full[cs], cs_ph, &a_empty[as],
-                                             as_ph ^ 1, abort_flag, group_go, a.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();  // the slot's previous UMMAs are complete
-          const uint8_t* crow = smem + L::OFF_C + cs * C_STAGE + sub * C_SUB_BYTES + r * 32;
-          const uint4 c0 = *reinterpret_cast<const uint4*>(crow);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(crow + 16);
-          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE + sub * (L::S_STAGE / NSUB);
-          uint32_t m1[2], m2[2];
-          bool two = false;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) two |= col_mult<SD, DELTA>(sstage + (h * BW + r) * es, m1[h], m2[h]);
-          const bool two_any = __any_sync(0xffffffffu, two);
-          if (two_any && SD == DWM_U8) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) m1[h] = pow2_126_minus_delta_x2<DELTA>();
-          }
-          uint32_t v[32];
-#pragma unroll
-          for (int wi = 0; wi < 8; ++wi) {
-            uint32_t tv[4];
-            tvals<true>(words[wi], tv);
-            const int h = wi >> 2;  // k32 block of k 8wi..8wi+7
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              uint32_t x = hmul2_bf16(tv[p], m1[h]);
-              if (two_any) x = hmul2_bf16(x, m2[h]);
-              v[4 * wi + p] = x;  // TMEM column 4 wi + p: k pair (8 wi + 2p, +1)
-            }
-          }
-          tmem_st32(lane_base + (uint32_t)(TS_A_COL0 + (as * NSUB + sub) * 32), v);
-          tmem_st_wait();
-          tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(&cs_empty[cs]);
@@ -961,51 +851,6 @@ __global__ void fp4_to_b200_kernel(const uint8_t* __restrict__ raw, uint32_t* __
   }
 }
 
-// raw [g, k, n/2] -> CM words [g][n][k/8]: word w of column c holds the
-// nibbles of k = 8w..8w+7 in order, B200-swizzled (one decode gives the bf16
-// pairs (k 8w+2p, 8w+2p+1)).
-__global__ void fp4_to_cm_kernel(const uint8_t* __restrict__ raw, uint32_t* __restrict__ out,
-                                 int groups, int k, int n) {
-  const int kw = k / 8;
-  const int64_t total = (int64_t)groups * n * kw;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int w = (int)(i % kw);
-    const int64_t gc = i / kw;
-    const int c = (int)(gc % n);
-    const int64_t g = gc / n;
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint8_t b = raw[(g * k + 8 * w + j) * (int64_t)(n / 2) + c / 2];
-      word |= (uint32_t)((c & 1) ? (b >> 4) : (b & 0xF)) << (4 * j);
-    }
-    out[i] = b200_swizzle_word(word);
-  }
-}
-
-// CM words -> raw [g, k, n/2] bytes.
-__global__ void fp4_from_cm_kernel(const uint32_t* __restrict__ cm, uint8_t* __restrict__ raw,
-                                   int groups, int k, int n) {
-  const int64_t total = (int64_t)groups * k * (n / 2);
-  const int kw = k / 8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int cp = (int)(i % (n / 2));
-    const int64_t gk = i / (n / 2);
-    const int kk = (int)(gk % k);
-    const int64_t g = gk / k;
-    uint32_t byte = 0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = 2 * cp + h;
-      const uint32_t word = b200_unswizzle_word(cm[(g * n + c) * kw + kk / 8]);
-      byte |= ((word >> (4 * (kk & 7))) & 0xFu) << (4 * h);
-    }
-    raw[i] = (uint8_t)byte;
-  }
-}
-
 // B200 words -> raw [g, k, n/2] bytes (one raw byte = columns 2c, 2c+1).
 __global__ void fp4_from_b200_kernel(const uint32_t* __restrict__ b200, uint8_t* __restrict__ raw,
                                      int groups, int k, int n) {
@@ -1055,11 +900,11 @@ __global__ void fp4_codes_convert_kernel(const uint8_t* __restrict__ in, uint8_t
 // Host launch
 // ---------------------------------------------------------------------------
 
-template <int SD, int VAR, int BT>
+template <int SD, int VAR>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
-  using L = Smem<SD, BT, VAR>;
+  using L = Smem<SD>;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
                           (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
@@ -1068,10 +913,6 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   if (VAR == kMN)
     rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)n / 2,
                         (uint64_t)n_local * k, (uint64_t)n / 2, BW / 2, BK,
-                        CU_TENSOR_MAP_SWIZZLE_NONE);
-  else if (VAR == kTS)  // CM: rows = columns [n_local * n], each k/8 words; box 8 words x 128
-    rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes, (uint64_t)k / 8,
-                        (uint64_t)n_local * n, (uint64_t)k / 2, BK / 8, BW,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
   else  // rows = column blocks, each (k/16) blocks x 32 words
     rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, codes,
@@ -1083,16 +924,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
 
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmm_fp4_kernel<SD, VAR, BT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC),
-                    "gmm smem attribute");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  rc = set_smem_limit(reinterpret_cast<const void*>(gmm_fp4_kernel<SD, VAR>), L::ALLOC, "gmm smem attribute");
+  if (rc) return rc;
   Args a;
   a.group_sizes = group_sizes;
   a.num_groups = num_groups;
@@ -1109,8 +942,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.n_tiles = n / (NSUB * BW);
   a.status = status_ptr();
-  gmm_fp4_kernel<SD, VAR, BT><<<num_sms(), num_threads<VAR>(), L::ALLOC, stream>>>(tm_lhs, tm_codes,
-                                                                           tm_scales, a);
+  gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
+                                                                         tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmm_fp4 launch");
 }
 
@@ -1127,10 +960,9 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
                     int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k,
                     int n, int group_offset, int num_local_groups, int act, int out_dtype,
                     void* out) {
-  DWM_CHECK_ARG(codes_format == DWM_FP4_E2M1 || codes_format == DWM_FP4_B200 ||
-                    codes_format == DWM_FP4_CM,
-                "gmm_fp4 takes e2m1 nibbles (raw, B200 or CM layout); convert tokamax codes "
-                "once with dwm_fp4_codes_convert");
+  DWM_CHECK_ARG(codes_format == DWM_FP4_E2M1 || codes_format == DWM_FP4_B200,
+                "gmm_fp4 takes e2m1 nibbles (raw or B200 layout); convert tokamax codes once "
+                "with dwm_fp4_codes_convert");
   DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
                 "scale dtype must be u8 (e8m0), bf16 or f32");
   DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
@@ -1153,10 +985,9 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 }
 
 // variant: 0 = choose, 1 = tcgen05 (shared-memory decode) with 128-row
-// tiles, 5 = the same with 256-row tiles, 2 = mma.sync decode kernel (B200
-// layout only) with 8- or 16-row token tiles by the average rows per local
-// group, 3 / 4 = the same with 8 / 16-row tiles, 6 = weights decoded into
-// TMEM (CM layout), 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout). The
+// tiles, 2 = mma.sync decode kernel (B200 layout only) with 8- or 16-row
+// token tiles by the average rows per local group, 3 / 4 = the same with 8 /
+// 16-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout). The
 // automatic choice for the B200 layout: mma.sync when the local groups
 // average at most 16 rows, CTA pairs from 128 rows (prefill), else the
 // single-CTA tcgen05 kernel with 128-row tiles.
@@ -1175,7 +1006,6 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
   if (variant == 0)
     variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 7 : 1;
-  if (codes_format == DWM_FP4_CM) variant = 6;
   if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
@@ -1184,23 +1014,17 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
                            out, s);
-#define DWM_GMM_LAUNCH(SD, VAR, BT)                                                       \
-  return launch<SD, VAR, BT>(lhs, codes, scales, group_sizes, num_groups, m, k, n,      \
-                             group_offset, num_local_groups, act, act_limit, out_dtype,  \
-                             zero_init, out, s)
-#define DWM_GMM_BY_SCALE(VAR, BT)                                   \
-  do {                                                              \
-    if (scale_dtype == DWM_U8) DWM_GMM_LAUNCH(DWM_U8, VAR, BT);     \
-    if (scale_dtype == DWM_BF16) DWM_GMM_LAUNCH(DWM_BF16, VAR, BT); \
-    DWM_GMM_LAUNCH(DWM_F32, VAR, BT);                               \
+#define DWM_GMM_LAUNCH(SD, VAR)                                                        \
+  return launch<SD, VAR>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset, \
+                         num_local_groups, act, act_limit, out_dtype, zero_init, out, s)
+#define DWM_GMM_BY_SCALE(VAR)                                   \
+  do {                                                          \
+    if (scale_dtype == DWM_U8) DWM_GMM_LAUNCH(DWM_U8, VAR);     \
+    if (scale_dtype == DWM_BF16) DWM_GMM_LAUNCH(DWM_BF16, VAR); \
+    DWM_GMM_LAUNCH(DWM_F32, VAR);                               \
   } while (0)
-  if (codes_format == DWM_FP4_CM) DWM_GMM_BY_SCALE(kTS, 128);
-  if (codes_format == DWM_FP4_B200) {
-    if (variant == 5) DWM_GMM_BY_SCALE(kKS, 256);
-    DWM_GMM_BY_SCALE(kKS, 128);
-  }
-  if (variant == 5) DWM_GMM_BY_SCALE(kMN, 256);
-  DWM_GMM_BY_SCALE(kMN, 128);
+  if (codes_format == DWM_FP4_B200) DWM_GMM_BY_SCALE(kKS);
+  DWM_GMM_BY_SCALE(kMN);
 #undef DWM_GMM_BY_SCALE
 #undef DWM_GMM_LAUNCH
 }
@@ -1229,14 +1053,11 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 7,
-                "variant must be 0 (auto), 1 / 5 (tcgen05, 128 / 256-row tiles), 2-4 "
-                "(mma.sync decode kernel), 6 (tcgen05, weights decoded into TMEM) or 7 "
-                "(tcgen05 on CTA pairs)");
-  DWM_CHECK_ARG(variant == 0 || (variant == 6) == (codes_format == DWM_FP4_CM),
-                "variant 6 takes (only) the CM layout");
-  DWM_CHECK_ARG(variant == 0 || variant == 6 || codes_format == DWM_FP4_B200,
-                "variants 1-5 and 7 need the B200 layout");
+  DWM_CHECK_ARG(variant >= 0 && variant <= 7 && variant != 5 && variant != 6,
+                "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-4 (mma.sync decode "
+                "kernel) or 7 (tcgen05 on CTA pairs)");
+  DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
+                "variants 1-4 and 7 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;
@@ -1302,24 +1123,6 @@ extern "C" int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int
     gmm::fp4_from_b200_kernel<<<gmm::grid_for(words * 4, 256), 256, 0, s>>>(
         static_cast<const uint32_t*>(in), static_cast<uint8_t*>(out), groups, k, n);
   return check_cuda(cudaGetLastError(), "fp4_to_b200 launch");
-}
-
-extern "C" int dwm_fp4_to_cm(const void* in, void* out, int groups, int k, int n, int inverse,
-                             void* stream) {
-  DWM_CHECK_ARG(in && out && in != out, "NULL or aliased pointers");
-  DWM_CHECK_ARG(groups >= 0 && k > 0 && n > 0 && k % 8 == 0 && n % 2 == 0,
-                "bad shape groups=%d k=%d n=%d (k %% 8, n %% 2)", groups, k, n);
-  DWM_CHECK_ARG(gmm::aligned16(in) && gmm::aligned16(out), "pointers must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t words = (int64_t)groups * n * (k / 8);
-  if (words == 0) return DWM_OK;
-  if (!inverse)
-    gmm::fp4_to_cm_kernel<<<gmm::grid_for(words, 256), 256, 0, s>>>(
-        static_cast<const uint8_t*>(in), static_cast<uint32_t*>(out), groups, k, n);
-  else
-    gmm::fp4_from_cm_kernel<<<gmm::grid_for(words * 4, 256), 256, 0, s>>>(
-        static_cast<const uint32_t*>(in), static_cast<uint8_t*>(out), groups, k, n);
-  return check_cuda(cudaGetLastError(), "fp4_to_cm launch");
 }
 
 extern "C" int dwm_fp4_codes_convert(const void* in, void* out, size_t nbytes, int from_format,

@@ -40,6 +40,8 @@
 // commits arrive on the matching barrier of both CTAs. Every wait is bounded
 // (common.cuh). Numerics are those of gmm_fp4.cu (E0901:84-95).
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "fp4_decode.cuh"
 
@@ -627,13 +629,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // Largest number of 2-CTA clusters resident at once (one CTA per SM), per
-// device.
+// device (cached; safe to call from several host threads).
 template <int SD>
 int max_pairs(cudaLaunchConfig_t cfg) {
-  static int cached[64] = {};
+  static std::mutex mu;
+  static std::map<int, int> cached;  // device -> clusters
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cached.find(dev);
+    if (it != cached.end()) return it->second;
+  }
   int n = 0;
   cfg.gridDim = dim3(2 * (unsigned)std::max(1, num_sms() / 2));
   cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gmm_pair_kernel<SD>, &cfg);
@@ -641,7 +648,8 @@ int max_pairs(cudaLaunchConfig_t cfg) {
     (void)cudaGetLastError();
     n = std::max(1, num_sms() / 2);
   }
-  if (dev < 64) cached[dev] = n;
+  std::lock_guard<std::mutex> lk(mu);
+  cached[dev] = n;
   return n;
 }
 
@@ -682,16 +690,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmm_pair_kernel<SD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC),
-                    "gmm pair smem attribute");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  rc = set_smem_limit(reinterpret_cast<const void*>(gmm_pair_kernel<SD>), L::ALLOC, "gmm pair smem attribute");
+  if (rc) return rc;
   Args a;
   a.group_sizes = group_sizes;
   a.num_groups = num_groups;

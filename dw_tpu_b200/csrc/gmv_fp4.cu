@@ -16,12 +16,15 @@
 // registers). So everything else per word is kept off the ALU and small:
 //   * E8M0 scales (the common case) are applied to the f32 partial of each
 //     32-deep k block after the MMA: the decode yields value * 2^-126
-//     (fp4_decode.cuh), the tokens are pre-scaled by 2^64 (exact), and the
-//     partial is multiplied by 2^(c-65) (one mad builds the factor): the
+//     (fp4_decode.cuh), the tokens are pre-scaled by 2^80 (exact), and the
+//     partial is multiplied by 2^(c-81) (one mad builds the factor): the
 //     reference's bf16(value * scale) x bf16 token products (E0901:84-95),
-//     exactly, up to the f32 summation order. A stage holding code 0 (scale
-//     +0) or a code above 192 instead multiplies the decoded weights in two
-//     exact bf16 steps (one SWAR test per lane per stage decides). Built with
+//     exactly, up to the f32 summation order, while |value * token| >= 2^-80
+//     (a product value * token * 2^-46 stays a normal f32) and |token| < 2^48
+//     (the pre-scaled token stays a finite bf16). A stage holding code 0
+//     (scale +0) or a code above 208 instead forms bf16(value * scale) in two exact bf16
+//     steps and multiplies the unscaled tokens, the reference's arithmetic
+//     (one SWAR test per lane per stage decides). Built with
 //     DWM_GMV_POST=0 the fast path instead multiplies each decoded weight
 //     register by 2^(c-1-4) in bf16 (exact for codes 1..132; the epilogue
 //     removes the 2^-4), about 3% slower.
@@ -45,8 +48,12 @@ namespace gmv {
 using namespace fp4;
 
 constexpr int MAX_GROUPS = 1024;
-constexpr uint32_t kBf16x2_2p64 = 0x5F805F80u;   // bf16 2^64, both halves
-constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
+// Token pre-scale of the post-MMA path, 2^kTokExp: the raw decode is value *
+// 2^-126, so products land at value * token * 2^(kTokExp - 126).
+constexpr int kTokExp = 80;
+constexpr uint32_t kBf16x2_TokScale = (uint32_t)(127 + kTokExp) * 0x00800080u;  // 2^80, both halves
+constexpr uint32_t kBf16x2_Norm = (uint32_t)(127 + 126 - kTokExp) * 0x00800080u;  // 2^46
+constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                            // 2^126
 
 // Ring depth per warp (stages of 64 k) for 1 and 2 n8 token tiles.
 #ifndef DWM_GMV_STAGES1
@@ -64,7 +71,7 @@ constexpr uint32_t kBf16x2_2p62 = 0x5E805E80u;   // bf16 2^62
 #define DWM_GMV_WARPS1 16
 #endif
 // 1: feed the raw decode (value * 2^-126, a bf16 subnormal for 0.5) to the
-// MMA on the E8M0 path; 0: first normalise it by 2^62 (4 more multiplies per
+// MMA on the E8M0 path; 0: first normalise it by 2^46 (4 more multiplies per
 // word, exact either way).
 #ifndef DWM_GMV_RAW_TVALS
 #define DWM_GMV_RAW_TVALS 1
@@ -102,9 +109,9 @@ struct Cfg {
   static constexpr int S =
       KS == 128 ? DWM_GMV_STAGES1_K128 : (NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2);
   static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
-  // Largest E8M0 code of the post-MMA path: the k-block factor 2^(c-65)
-  // (raw decode) or 2^(c-127) (normalised) must be a finite f32.
-  static constexpr uint32_t POST_MAX = POST ? (RAW ? 192u : 254u) : 128u + kDelta;
+  // Largest E8M0 code of the post-MMA path: the k-block factor
+  // 2^(c-1-kTokExp) (raw decode) or 2^(c-127) (normalised) must be a finite f32.
+  static constexpr uint32_t POST_MAX = POST ? (RAW ? 128u + kTokExp : 254u) : 128u + kDelta;
   static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of KS + 8 k (KS used)
   // Scales of a stage: [KS32 k32 rows][2 tiles][32 columns], one TMA copy.
   static constexpr int SC_ROW = 64 * es;
@@ -304,10 +311,10 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
   const int NSTAGE = a.k / KSTAGE;
   const DecodeRegs dregs = DecodeRegs::make();
   // Register-held constants of the post-MMA path: the zero quad of the
-  // partials' first MMA and the tokens' 2^64 pre-scale.
+  // partials' first MMA and the tokens' 2^kTokExp pre-scale.
   const float zq[4] = {__uint_as_float(pin(0u)), __uint_as_float(pin(0u)),
                        __uint_as_float(pin(0u)), __uint_as_float(pin(0u))};
-  const uint32_t tok_2p64 = pin(kBf16x2_2p64);
+  const uint32_t tok_scale = pin(kBf16x2_TokScale);
   // 2^(c-1-delta) for E8M0 code c, both bf16 halves: c * 0x00800080 + bias.
   const uint32_t wm_bias = pin((126u - C::DELTA) * 0x00800080u);
   const int wstride = gridDim.x * C::WARPS;
@@ -388,10 +395,11 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
       const uint8_t* sc = sc_s + slot * C::SC;
       // PRE: multiply the decoded weights by their scale in bf16 (the
       // reference's rounding; bf16/f32 scales, or E8M0 codes outside the
-      // post-MMA range), else scale the f32 partial of each k32 block.
+      // post-MMA range) and the tokens as they are, else scale the f32
+      // partial of each k32 block.
       auto stage = [&](auto pre_tag) {
         constexpr bool PRE = decltype(pre_tag)::value;
-        constexpr uint32_t M1 = C::POST ? kBf16x2_2p62 : pow2_126_minus_delta_x2<C::DELTA>();
+        constexpr uint32_t M1 = C::POST ? kBf16x2_2p126 : pow2_126_minus_delta_x2<C::DELTA>();
 #pragma unroll
         for (int h = 0; h < C::KS32; ++h) {  // 32-deep k block inside the stage
           // Scales of the lane's columns: block i, column gid (+8 for hc =
@@ -419,8 +427,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
                     : "=r"(wm[i][hc])
                     : "r"(c), "r"(wm_bias));
               } else {
-                post[i][hc] = C::RAW ? __uint_as_float(c * 0x00800000u + (62u << 23))  // 2^(c-65)
-                                     : __uint_as_float(c << 23);                       // 2^(c-127)
+                post[i][hc] = C::RAW ? __uint_as_float(c * 0x00800000u +  // 2^(c-1-kTokExp)
+                                                       ((uint32_t)(126 - kTokExp) << 23))
+                                     : __uint_as_float(c << 23);  // 2^(c-127)
               }
             }
           float part[4][NT][4];
@@ -436,9 +445,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
               const uint8_t* row = tok + (nt * 8 + gid) * TOK_ROW + kk * 32 + 4 * tig;
               uint32_t b0 = *reinterpret_cast<const uint32_t*>(row);
               uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + 16);
-              if constexpr (C::POST) {
-                b0 = hmul2_bf16(b0, tok_2p64);
-                b1 = hmul2_bf16(b1, tok_2p64);
+              if constexpr (C::POST && !PRE) {
+                b0 = hmul2_bf16(b0, tok_scale);
+                b1 = hmul2_bf16(b1, tok_scale);
               }
               b[nt][0] = b0;
               b[nt][1] = b1;
@@ -466,7 +475,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
               } else {
                 if constexpr (!C::RAW) {
 #pragma unroll
-                  for (int j = 0; j < 4; ++j) af[j] = hmul2_bf16(af[j], kBf16x2_2p62);
+                  for (int j = 0; j < 4; ++j) af[j] = hmul2_bf16(af[j], kBf16x2_Norm);
                 }
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
@@ -499,10 +508,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
           const uint32_t v = *reinterpret_cast<const uint32_t*>(sc + (q * 32 + lane) * 4);
           const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
           uint32_t high_byte;
-          if constexpr (C::POST_MAX == 192u)  // a byte >= 193: bit 7 set and low 7 bits >= 65
-            high_byte = ((v & 0x7F7F7F7Fu) + 0x3F3F3F3Fu) & v & 0x80808080u;
-          else if constexpr (C::POST_MAX == 128u + kDelta)  // a byte >= 133: low 7 bits >= 5
-            high_byte = ((v & 0x7F7F7F7Fu) + (0x80808080u - (1u + kDelta) * 0x01010101u)) & v &
+          if constexpr (C::POST_MAX >= 128u && C::POST_MAX < 255u)
+            // a byte > POST_MAX: bit 7 set and low 7 bits + (255 - POST_MAX) >= 128
+            high_byte = ((v & 0x7F7F7F7Fu) + (255u - C::POST_MAX) * 0x01010101u) & v &
                         0x80808080u;
           else  // a byte == 255
             high_byte = (~v - 0x01010101u) & v & 0x80808080u;
@@ -615,16 +623,8 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(gmv_fp4_kernel<SD, NT, KS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::ALLOC),
-                    "gmv smem attribute");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  rc = set_smem_limit(reinterpret_cast<const void*>(gmv_fp4_kernel<SD, NT, KS>), C::ALLOC, "gmv smem attribute");
+  if (rc) return rc;
   gmv_fp4_kernel<SD, NT, KS><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(
       tm_lhs, tm_codes, tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmv_fp4 launch");

@@ -4,6 +4,7 @@
 // entry point the caller could make itself, so results are bit-identical to
 // that sequence; the call only saves the host round trips (one call instead of
 // six) and the intermediate bookkeeping.
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -103,23 +104,32 @@ namespace layer {
 
 __device__ __align__(256) uint8_t g_scratch[DWM_LAYER_SCRATCH_BYTES];
 
-// Address of g_scratch on the current device, resolved once per device (with
-// that device current) and cached.
+// Address of g_scratch in the current context, resolved once per context
+// (with its device current) and cached under the context handle, so that a
+// new primary context (after cudaDeviceReset) resolves it afresh.
 int scratch_address(void** out) {
   static std::mutex mu;
-  static void* addr[64] = {};
-  int dev = 0;
-  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  if (rc) return rc;
-  if (dev < 0 || dev >= 64) return set_error(DWM_ERR_UNSUPPORTED, "device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  static std::map<void*, void*> addr;  // CUDA context -> g_scratch's address in it
+  void* ctx = nullptr;
+  if (current_context(&ctx) != DWM_OK) {
+    // No context current yet: resolving the symbol makes the runtime create
+    // the device's primary context.
     void* p = nullptr;
-    rc = check_cuda(cudaGetSymbolAddress(&p, g_scratch), "cudaGetSymbolAddress(layer scratch)");
+    int rc = check_cuda(cudaGetSymbolAddress(&p, g_scratch), "cudaGetSymbolAddress(layer scratch)");
     if (rc) return rc;
-    addr[dev] = p;
+    rc = current_context(&ctx);
+    if (rc) return rc;
   }
-  *out = addr[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = addr.find(ctx);
+  if (it == addr.end()) {
+    void* p = nullptr;
+    const int rc =
+        check_cuda(cudaGetSymbolAddress(&p, g_scratch), "cudaGetSymbolAddress(layer scratch)");
+    if (rc) return rc;
+    it = addr.emplace(ctx, p).first;
+  }
+  *out = it->second;
   return DWM_OK;
 }
 

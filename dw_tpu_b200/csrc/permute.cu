@@ -112,17 +112,10 @@ extern "C" int dwm_permute(const int32_t* topk_ids, int t, int topk, int e, int3
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n = t * topk;
   const size_t smem = (size_t)(moe::SORT_WARPS * e + e) * sizeof(int);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    int rc = check_cuda(cudaFuncSetAttribute(perm::permute_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)((moe::SORT_WARPS * 1024 + 1024) * sizeof(int))),
-                        "permute smem attribute");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  int rc = set_smem_limit(reinterpret_cast<const void*>(perm::permute_kernel),
+                          (int)((moe::SORT_WARPS * 1024 + 1024) * sizeof(int)),
+                          "permute smem attribute");
+  if (rc) return rc;
   perm::permute_kernel<<<1, moe::SORT_THREADS, smem, s>>>(
       topk_ids, n, topk, e, topk_argsort, token_indices_sorted, revert, group_sizes,
       status_ptr());

@@ -13,8 +13,9 @@ k) output and forms the k-order combine (KC:14-21). One kernel each way. One
 process per GPU; peers' buffers are mapped with CUDA IPC, exchanged once over
 ``torch.distributed``.
 
-``all_gather_local`` / ``reduce_scatter_local`` below are the NCCL
-comparison path (the reference's collectives on ``torch.distributed``).
+``NcclExchange`` (NCCL ``all_to_all_single``) and ``all_gather_local`` /
+``reduce_scatter_local`` (the reference's collectives on
+``torch.distributed``) below are the NCCL comparison paths.
 """
 
 from __future__ import annotations
@@ -155,6 +156,13 @@ class EPContext:
             L.stream_ptr() if stream is None else stream), "dwm_ep_combine_shared")
         return out
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of every device-side wait of later launches (default 2 s). A
+        wait that runs out reports DWM_DEV_TIMEOUT (``_lib.DeviceError`` on the
+        next status check); every rank's context must then be re-created."""
+        L.check(L.lib().dwm_ep_set_wait_limit(self._ctx, int(seconds * 1e9)),
+                "dwm_ep_set_wait_limit")
+
     def close(self) -> None:
         if getattr(self, "_ctx", None) is not None and self._ctx.value:
             L.lib().dwm_ep_destroy(self._ctx)
@@ -219,6 +227,83 @@ def emulated_combine(ctxs: list[EPContext], ys, weights, outs=None):
 # NCCL comparison path: the reference's collectives
 # ---------------------------------------------------------------------------
 
+class NcclExchange:
+    """The NCCL comparison path of the EP exchange: ``all_to_all_single`` of
+    per-expert counts, then of the token rows themselves (sorted by expert on
+    the sender), a local reorder into the one-shot path's receive order
+    (expert-major, then source rank, source token, k slot), and on the way back
+    an ``all_to_all_single`` of the expert outputs followed by the same k-order
+    combine (KC:44-54). Receive buffers and outputs equal the one-shot
+    kernels' bit for bit; the price is NCCL's uneven splits, which need the
+    counts on the host (one device-to-host sync per dispatch)."""
+
+    def __init__(self, num_experts: int, hidden: int, topk: int, group=None):
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if num_experts % self.world:
+            raise ValueError("num_experts must divide by the world size")
+        self.num_experts, self.hidden, self.topk = int(num_experts), int(hidden), int(topk)
+        self.local_experts = self.num_experts // self.world
+
+    def dispatch(self, hidden: torch.Tensor, topk_ids: torch.Tensor):
+        """hidden [T, H], topk_ids int32 [T, topk] (every id in range) ->
+        (received rows [R, H] in receive order, group sizes int32 [E/world])."""
+        t, k, le, world = hidden.shape[0], self.topk, self.local_experts, self.world
+        if topk_ids.shape != (t, k) or hidden.shape[1] != self.hidden:
+            raise ValueError("expected hidden [T, H] and topk_ids [T, topk]")
+        dev = hidden.device
+        flat = topk_ids.reshape(-1).long()
+        order = torch.argsort(flat, stable=True)  # (expert, token, k) order = by owner rank
+        send = hidden.index_select(0, order // k)
+        exp_counts = torch.bincount(flat, minlength=self.num_experts).to(torch.int64)
+        recv_exp = torch.empty_like(exp_counts)
+        dist.all_to_all_single(recv_exp, exp_counts, group=self.group)
+        recv_exp = recv_exp.view(world, le)              # [source rank, local expert]
+        counts = torch.stack([exp_counts.view(world, le).sum(1), recv_exp.sum(1)]).cpu()
+        in_splits, out_splits = counts[0].tolist(), counts[1].tolist()
+        recv = torch.empty((sum(out_splits), self.hidden), dtype=hidden.dtype, device=dev)
+        dist.all_to_all_single(recv, send, out_splits, in_splits, group=self.group)
+        # Row (source s, local expert x, j-th of that block) goes to
+        # ebase[x] + (rows of x from sources before s) + j.
+        gs = recv_exp.sum(0)
+        ebase = torch.cumsum(gs, 0) - gs
+        before = torch.cumsum(recv_exp, 0) - recv_exp
+        blocks = recv_exp.reshape(-1)
+        block_start = torch.cumsum(blocks, 0) - blocks
+        n = int(sum(out_splits))
+        block_of_row = torch.repeat_interleave(torch.arange(world * le, device=dev), blocks,
+                                               output_size=n)
+        j = torch.arange(n, device=dev) - block_start[block_of_row]
+        x_of_row = block_of_row % le
+        dest = ebase[x_of_row] + before.reshape(-1)[block_of_row] + j
+        out = torch.empty_like(recv)
+        out.index_copy_(0, dest, recv)
+        self._state = (order, dest, in_splits, out_splits, t)
+        return out, gs.to(torch.int32)
+
+    def return_rows(self, y: torch.Tensor) -> torch.Tensor:
+        """Expert outputs y [R, H] in receive order -> each of this rank's
+        (token, k) pairs' output row, [T * topk, H] in (token, k) order."""
+        order, dest, in_splits, out_splits, t = self._state
+        back = torch.empty((t * self.topk, y.shape[1]), dtype=y.dtype, device=y.device)
+        dist.all_to_all_single(back, y.index_select(0, dest), in_splits, out_splits,
+                               group=self.group)
+        rows = torch.empty_like(back)
+        rows.index_copy_(0, order, back)
+        return rows
+
+    def combine(self, y: torch.Tensor, topk_weights: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """The k-order combine of this rank's tokens from the expert outputs y
+        [R, H] (receive order) and topk_weights [T, topk]."""
+        rows = self.return_rows(y)
+        t = topk_weights.shape[0]
+        if out is None:
+            out = torch.empty((t, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+        ident = torch.arange(t * self.topk, dtype=torch.int32, device=y.device)
+        return ops.combine_out(rows, ident, topk_weights.contiguous(), self.topk, out)
+
+
 def all_gather_local(x: torch.Tensor, group=None) -> torch.Tensor:
     """KO:152-164: rank-major concatenation of every rank's block (NCCL)."""
     world = dist.get_world_size(group)
@@ -253,7 +338,9 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
         return 3  # mma.sync kernel, 8-row token tiles
     if expected_rows <= 16:
         return 4  # mma.sync kernel, 16-row token tiles
-    return 1      # tcgen05 kernel
+    if expected_rows >= 128:
+        return 7  # tcgen05 on CTA pairs (prefill)
+    return 1      # tcgen05 kernel, one CTA
 
 
 class EPMoELayer:

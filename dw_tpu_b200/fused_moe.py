@@ -44,17 +44,6 @@ class FP4MoEWeights:
         return FP4MoEWeights(ops.fp4_to_b200_out(self.w13), self.s13,
                              ops.fp4_to_b200_out(self.w2), self.s2, "b200")
 
-    def to_cm(self) -> "FP4MoEWeights":
-        """Load-time re-layout of both projections into the column-major CM
-        layout that the tcgen05 kernel with the decoded weights in TMEM reads
-        (prefill-sized groups); from raw e2m1 weights."""
-        if self.layout == "cm":
-            return self
-        if self.layout != "e2m1":
-            raise ValueError("to_cm converts raw e2m1 weights")
-        return FP4MoEWeights(ops.fp4_to_cm_out(self.w13), self.s13,
-                             ops.fp4_to_cm_out(self.w2), self.s2, "cm")
-
     @classmethod
     def from_dense(cls, w13: torch.Tensor, w2: torch.Tensor) -> "FP4MoEWeights":
         """Weight preparation on the device: dense (or dequantised MXFP4)

@@ -40,14 +40,14 @@ def _scale_view(s: torch.Tensor):
 # ----------------------------------------------------------------------------
 
 def fp4_dims(codes: torch.Tensor, layout: str):
-    """(groups, k, n) of packed FP4 weights: "e2m1" [g, k, n/2]; "b200" and
-    "cm" [g, n, k/2]."""
+    """(groups, k, n) of packed FP4 weights: "e2m1" [g, k, n/2]; "b200"
+    [g, n, k/2]."""
     if codes.dim() != 3:
         raise ValueError("FP4 weights must be 3-D packed bytes")
     g, a, b = codes.shape
     if layout == "e2m1":
         return g, a, 2 * b
-    if layout in ("b200", "cm"):
+    if layout == "b200":
         return g, 2 * b, a
     raise ValueError(f"unknown FP4 layout {layout!r}")
 
@@ -57,10 +57,9 @@ def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
                 zero_init=False, layout="e2m1", variant=0, stream=None):
     """out <- grouped matmul of lhs with the FP4 weights (see dwm_gmm_fp4).
     ``layout`` is "e2m1" (raw [g, k, n/2]) or "b200" (``fp4_to_b200_out``);
-    ``variant`` 0 picks the kernel; 1 forces the tcgen05 kernel, 2-4 the
-    mma.sync decode kernel (auto / 8 / 16-row token tiles), 5 the tcgen05
-    kernel with 256-row tiles, 6 the TMEM-decode kernel ("cm" layout) and 7
-    the tcgen05 kernel on CTA pairs; 1-5 and 7 need the B200 layout."""
+    ``variant`` 0 picks the kernel; 1 forces the tcgen05 kernel on one CTA,
+    2-4 the mma.sync decode kernel (auto / 8 / 16-row token tiles) and 7 the
+    tcgen05 kernel on CTA pairs; 1-4 and 7 need the B200 layout."""
     L.require_cuda(lhs, codes, scales, group_sizes, out)
     if lhs.dtype != torch.bfloat16 or lhs.dim() != 2:
         raise ValueError("lhs must be a 2-D bf16 tensor")
@@ -123,28 +122,6 @@ def fp4_to_b200_out(src, inverse=False, stream=None):
     rc = L.lib().dwm_fp4_to_b200(src.data_ptr(), dst.data_ptr(), g, k, n, int(inverse),
                                  L.stream_ptr() if stream is None else stream)
     L.check(rc, "fp4_to_b200")
-    return dst
-
-
-def fp4_to_cm_out(src, inverse=False, stream=None):
-    """Raw e2m1 [g, k, n/2] -> the column-major CM layout (u32 words
-    [g][n][k/8], returned as bytes shaped [g, n, k/2]), or back with
-    ``inverse``; returns a new tensor."""
-    L.require_cuda(src)
-    src = _u8view(src).contiguous()
-    if src.dim() != 3:
-        raise ValueError("expected packed FP4 weights [g, k, n/2] (or [g, n, k/2])")
-    if inverse:
-        g, n, k2 = src.shape
-        k = 2 * k2
-        dst = torch.empty((g, k, n // 2), dtype=torch.uint8, device=src.device)
-    else:
-        g, k, n2 = src.shape
-        n = 2 * n2
-        dst = torch.empty((g, n, k // 2), dtype=torch.uint8, device=src.device)
-    rc = L.lib().dwm_fp4_to_cm(src.data_ptr(), dst.data_ptr(), g, k, n, int(inverse),
-                               L.stream_ptr() if stream is None else stream)
-    L.check(rc, "fp4_to_cm")
     return dst
 
 
@@ -325,6 +302,43 @@ def combine_shared_out(x, indices, topk_weights, topk, shared, out, *, routed_sc
     return out
 
 
+def _check_layer_args(hidden, logits, w13, s13, w2, s2, out, layout, scoring_fn):
+    """Shape, dtype and layout checks of the one-call layer (the C layer builds
+    its tensor maps and stores from these sizes alone): hidden bf16 [t, h],
+    logits [t, e], w13 / s13 [e, h, 2I] and w2 / s2 [e, I, h] in ``layout``,
+    out bf16 [t, h], all contiguous. Returns (t, h, e, I)."""
+    if hidden.dtype != torch.bfloat16 or hidden.dim() != 2 or not hidden.is_contiguous():
+        raise ValueError("hidden must be a contiguous bf16 [t, h] tensor")
+    t, h = hidden.shape
+    if logits.dim() != 2 or logits.shape[0] != t or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous [t, e] tensor")
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("logits must be bf16 or f32")
+    e = logits.shape[1]
+    if scoring_fn not in _SCORING:
+        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
+    if s2.dim() < 3 or s13.dim() < 3:
+        raise ValueError("scales must be [e, k/32, n] (or [e, k/32, 1, n])")
+    inter = s2.shape[1] * 32
+    sc13, sd13 = _scale_view(s13)
+    sc2, sd2 = _scale_view(s2)
+    if sd13 != sd2:
+        raise ValueError("s13 and s2 must have the same dtype")
+    for name, codes, sc, k, n in (("w13", w13, sc13, h, 2 * inter), ("w2", w2, sc2, inter, h)):
+        if fp4_dims(_u8view(codes), layout) != (e, k, n):
+            raise ValueError(f"{name} must hold [{e}, {k}, {n}] FP4 weights in the {layout!r} "
+                             f"layout, got {tuple(codes.shape)}")
+        if sc.numel() != e * (k // 32) * n or sc.shape[0] != e:
+            raise ValueError(f"{name} scales must be [{e}, {k // 32}, {n}]")
+        if not codes.is_contiguous() or not sc.is_contiguous():
+            raise ValueError(f"{name} and its scales must be contiguous")
+    if h % 256 or inter % 128:
+        raise ValueError(f"hidden={h} must be a multiple of 256 and intermediate={inter} of 128")
+    if out.shape != (t, h) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous bf16 [{t}, {h}] tensor")
+    return t, h, e, inter
+
+
 def moe_layer_workspace_bytes(num_tokens, hidden, inter, topk, num_experts, y_f32=False):
     return int(L.lib().dwm_moe_layer_workspace_bytes(int(num_tokens), int(hidden), int(inter),
                                                      int(topk), int(num_experts), int(y_f32)))
@@ -336,16 +350,10 @@ def moe_layer_fp4_out(hidden, logits, top_k, w13, s13, w2, s2, out, workspace, *
     """The whole single-device layer in one C call (dwm_moe_layer_fp4):
     route -> permute -> gather -> gmm1 (SwiGLU) -> gmm2 -> combine, with its
     intermediates in ``workspace`` (uint8, moe_layer_workspace_bytes)."""
+    t, h, e, inter = _check_layer_args(hidden, logits, w13, s13, w2, s2, out, layout, scoring_fn)
+    if workspace.dtype != torch.uint8 or workspace.dim() != 1:
+        raise ValueError("workspace must be a 1-D uint8 tensor")
     L.require_cuda(hidden, logits, w13, s13, w2, s2, out, workspace)
-    if hidden.dtype != torch.bfloat16 or hidden.dim() != 2 or not hidden.is_contiguous():
-        raise ValueError("hidden must be a contiguous bf16 [t, h] tensor")
-    t, h = hidden.shape
-    if logits.dim() != 2 or logits.shape[0] != t or not logits.is_contiguous():
-        raise ValueError("logits must be a contiguous [t, e] tensor")
-    e = logits.shape[1]
-    if scoring_fn not in _SCORING:
-        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
-    inter = s2.shape[1] * 32
     act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
     rc = L.lib().dwm_moe_layer_fp4(
         hidden.data_ptr(), logits.data_ptr(), L.dtype_code(logits.dtype), t, h, e, int(top_k),
@@ -365,20 +373,14 @@ def moe_layer_fp4_noalloc_out(hidden, logits, top_k, w13, s13, w2, s2, out, *, l
     the intermediates live in the library's fixed device scratch
     (DWM_LAYER_SCRATCH_BYTES per device); larger inputs raise ValueError.
     Overlapping calls on one device race on that scratch."""
+    t, h, e, inter = _check_layer_args(hidden, logits, w13, s13, w2, s2, out, layout, scoring_fn)
     L.require_cuda(hidden, logits, w13, s13, w2, s2, out)
-    if hidden.dtype != torch.bfloat16 or hidden.dim() != 2 or not hidden.is_contiguous():
-        raise ValueError("hidden must be a contiguous bf16 [t, h] tensor")
-    t, h = hidden.shape
-    if logits.dim() != 2 or logits.shape[0] != t or not logits.is_contiguous():
-        raise ValueError("logits must be a contiguous [t, e] tensor")
-    if scoring_fn not in _SCORING:
-        raise ValueError(f"unknown scoring_fn {scoring_fn!r}")
     act = L.ACT_SWIGLU if act_limit is None else L.ACT_SWIGLU_CLAMP
     rc = L.lib().dwm_moe_layer_fp4_noalloc(
-        hidden.data_ptr(), logits.data_ptr(), L.dtype_code(logits.dtype), t, h, logits.shape[1],
+        hidden.data_ptr(), logits.data_ptr(), L.dtype_code(logits.dtype), t, h, e,
         int(top_k), _SCORING[scoring_fn], int(bool(renormalize)), _u8view(w13).data_ptr(),
         s13.data_ptr(), _u8view(w2).data_ptr(), s2.data_ptr(), L.LAYOUTS[layout],
-        L.dtype_code(s13.dtype), s2.shape[1] * 32, act,
+        L.dtype_code(s13.dtype), inter, act,
         0.0 if act_limit is None else float(act_limit), int(bool(f32_reduce)), out.data_ptr(),
         L.stream_ptr() if stream is None else stream)
     L.check(rc, "moe_layer_fp4_noalloc")

@@ -59,12 +59,6 @@ extern "C" {
                              m16n8k16 MMA for W^T, its bits permuted for a
                              one-PRMT bf16 decode */
 
-#define DWM_FP4_CM 3      /* column-major load-time layout (dwm_fp4_to_cm): u32
-                             words [groups][n][k/8], word w of column c the
-                             nibbles of k = 8w..8w+7 in order, bits permuted
-                             as in DWM_FP4_B200; taken by the tcgen05 kernel
-                             that keeps the decoded weights in TMEM */
-
 #define DWM_SCORE_SOFTMAX 0
 #define DWM_SCORE_SIGMOID 1
 #define DWM_SCORE_SQRTSOFTPLUS 2
@@ -87,10 +81,8 @@ int dwm_device_status(void* stream, int* bits);
  *           [sum(group_sizes[:g]), +group_sizes[g]))
  *   codes   DWM_FP4_E2M1: uint8 [num_local_groups, k, n/2], two e2m1 nibbles
  *           per byte, element 2j in the low nibble; DWM_FP4_B200: the same
- *           values re-laid by dwm_fp4_to_b200 (faster decode); DWM_FP4_CM:
- *           re-laid by dwm_fp4_to_cm (read by variant 6, which decodes into
- *           TMEM; DWM_FP4_B200 is as fast or faster at every group size);
- *           convert tokamax codes once with dwm_fp4_codes_convert
+ *           values re-laid by dwm_fp4_to_b200 (faster decode); convert
+ *           tokamax codes once with dwm_fp4_codes_convert
  *   scales  [num_local_groups, k/32, n] of scale_dtype: DWM_U8 (E8M0 codes,
  *           KE:37-40), DWM_BF16 or DWM_F32 (cast to bf16 before use)
  *   group_sizes int32 [num_groups] on the device
@@ -106,22 +98,19 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
 
 /* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4),
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
- * automatic choice for groups averaging 17-127 rows), 5 = the same with
- * 256-row tiles (one TMEM accumulator buffer),
+ * automatic choice for groups averaging 17-127 rows),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8- or 16-row token tiles by the average rows per local group),
  * 3 / 4 = the same with 8 / 16-row token tiles (2-4: the automatic choice
- * for B200 codes whose groups average at most 16 rows), 6 = tcgen05 MMA with
- * the weights decoded straight into TMEM (the A-from-TMEM UMMA form; the
- * automatic choice for, and the only variant of, DWM_FP4_CM codes),
+ * for B200 codes whose groups average at most 16 rows),
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
  * double-buffered accumulators (the automatic choice for B200 codes whose
- * groups average 128 rows or more). 1-5 and 7 need DWM_FP4_B200 codes.
- * Every variant decodes the same bf16 weights and accumulates in f32;
- * results differ between variants only by f32 summation order (1, 5, 6 and
- * 7 give identical bits). Same reference interface as dwm_gmm_fp4
- * (TK:107-153). */
+ * groups average 128 rows or more). 1-4 and 7 need DWM_FP4_B200 codes;
+ * 5 and 6 are not assigned. Every variant decodes the same bf16 weights and
+ * accumulates in f32; results differ between variants only by f32 summation
+ * order (1 and 7 give identical bits). Same reference interface as
+ * dwm_gmm_fp4 (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
                         int scale_dtype, const int32_t* group_sizes, int num_groups, int m,
                         int k, int n, int group_offset, int num_local_groups, int act,
@@ -143,12 +132,6 @@ int dwm_fp4_dequant(const void* codes, int codes_format, const void* scales, int
  * fp4_weight_to_codes (B01:276-299, TK:17-30). k % 16 == 0, n % 16 == 0. */
 int dwm_fp4_to_b200(const void* in, void* out, int groups, int k, int n, int inverse,
                     void* stream);
-
-/* Load-time re-layout of packed e2m1 weights: raw [g, k, n/2] -> DWM_FP4_CM
- * [g, n, k/2] (inverse = 0) or back (inverse = 1); lossless, out of place.
- * k % 8 == 0, n % 2 == 0. */
-int dwm_fp4_to_cm(const void* in, void* out, int groups, int k, int n, int inverse,
-                  void* stream);
 
 /* On-device weight preparation: quantize_tensor(float4_e2m1fn, w, block 32,
  * power_of_two_scale) (B01:319-347) of w [groups, k, n] (bf16 or f32) over
@@ -293,7 +276,9 @@ int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits
  * with the same dtypes, one combine per dispatch; calls on one context are
  * stream-ordered and must not overlap. The exchange keeps its step counter
  * in device memory, so the calls can be captured in a CUDA graph and
- * replayed. Device-side waits give up after 2 s with DWM_DEV_TIMEOUT. */
+ * replayed. Device-side waits give up after 2 s (dwm_ep_set_wait_limit) with
+ * DWM_DEV_TIMEOUT; the reference's barrier waits without bound
+ * (KO:70-77). */
 #define DWM_EP_HANDLE_BYTES 64 /* size of one rank's IPC handle */
 #define DWM_EP_COUNTS 1        /* dispatch phases (DWM_EP_ALL = all three) */
 #define DWM_EP_ROWS 2
@@ -347,6 +332,13 @@ int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_wei
 int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                           int w_dtype, const void* shared, int shared_dtype, float routed_scale,
                           int mid_dtype, void* out, int out_dtype, int phases, void* stream);
+/* Limit of every device-side wait of this context's later launches (default
+ * 2 s; 1 us .. 60 s). A wait that runs out sets DWM_DEV_TIMEOUT, the kernel
+ * drops the step's rows and returns; the contexts of all ranks must then be
+ * destroyed and created again before the next exchange (their step counters
+ * no longer agree). No counterpart in the reference, whose one-shot barrier
+ * waits without bound (KO:70-77). */
+int dwm_ep_set_wait_limit(dwm_ep* ctx, uint64_t limit_ns);
 /* Synchronise the context's device, unmap peers and free the buffers. */
 int dwm_ep_destroy(dwm_ep* ctx);
 

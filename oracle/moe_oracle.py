@@ -41,7 +41,7 @@ __all__ = [
     "codes_to_e2m1", "decode_codes", "round_to_e2m1", "b200_swizzle",
     "b200_unswizzle", "to_b200_layout", "from_b200_layout", "e8m0_encode",
     "e8m0_decode", "scales_to_f32", "dequant_fp4_block", "dequant_fp4_f32",
-    "gmm_f32", "gmm_ref", "silu_and_mul", "combine_shared", "to_cm_layout", "from_cm_layout", "quantize_fp4_block32",
+    "gmm_f32", "gmm_ref", "silu_and_mul", "combine_shared", "quantize_fp4_block32",
     "dequantize_fp4_block32", "apply_scoring_fn", "route_topk",
     "sorted_token_indices", "permute", "dispatch_gather", "combine",
     "fused_moe", "ep_dispatch", "ep_combine_korder", "ep_combine_rankorder",
@@ -219,38 +219,6 @@ def from_b200_layout(b200: np.ndarray) -> np.ndarray:
         blocks[:, :, :, dk[:, j], dc[:, j]] = (words >> np.uint32(4 * j)) & np.uint32(0xF)
     nib = blocks.transpose(0, 2, 3, 1, 4).reshape(g, k, n)
     return pack_nibbles(nib)
-
-
-def to_cm_layout(packed: np.ndarray) -> np.ndarray:
-    """Raw e2m1 weights [g, k, n/2] -> the column-major (CM) layout, returned
-    as uint8 [g, n, k/2] (same byte count): u32 words [g][n][k/8], word w of
-    column c holding the nibbles of k = 8w .. 8w+7 in order (nibble j in bits
-    4j..4j+3), then ``b200_swizzle`` on every word, so one decode of a word
-    gives the bf16 pairs (k 8w+2p, 8w+2p+1), p = 0..3. Not part of the
-    reference: a lossless load-time re-layout."""
-    packed = np.asarray(packed, np.uint8)
-    g, k, n2 = packed.shape
-    n = 2 * n2
-    nib = unpack_nibbles(packed).astype(np.uint32)           # [g, k, n]
-    cols = nib.transpose(0, 2, 1).reshape(g, n, k // 8, 8)   # [g, n, k/8, 8]
-    words = np.zeros((g, n, k // 8), np.uint32)
-    for j in range(8):
-        words |= cols[..., j] << np.uint32(4 * j)
-    raw = np.ascontiguousarray(words).view(np.uint8).reshape(g, n, k // 2)
-    return b200_swizzle(raw)
-
-
-def from_cm_layout(cm: np.ndarray) -> np.ndarray:
-    """Inverse of ``to_cm_layout``."""
-    cm = np.asarray(cm, np.uint8)
-    g, n, k2 = cm.shape
-    k = 2 * k2
-    words = np.ascontiguousarray(b200_unswizzle(cm)).view(np.uint32).reshape(g, n, k // 8)
-    cols = np.zeros((g, n, k // 8, 8), np.uint8)
-    for j in range(8):
-        cols[..., j] = (words >> np.uint32(4 * j)) & np.uint32(0xF)
-    nib = cols.reshape(g, n, k).transpose(0, 2, 1)
-    return pack_nibbles(np.ascontiguousarray(nib))
 
 
 def b200_unswizzle(packed: np.ndarray) -> np.ndarray:

@@ -54,3 +54,78 @@ def assert_gemm_close(got, ref_bf16, ref_f32, k, rows=None):
     ulp = 2.0 ** (np.floor(np.log2(amax)) - 7) if amax > 0 else 0.0
     err = float(np.max(np.abs(got - ref_bf16)))
     assert err <= 2 * ulp + 1e-30, f"max-abs {err:.3e} > 2 ulp ({ulp:.3e}) of max {amax:.3e}"
+
+
+# ---------------------------------------------------------------------------
+# A plain-PyTorch fp32 reference of the MoE layer on the GPU (for full-size
+# checks the NumPy oracle is too slow for). It restates the reference
+# numerics: e2m1 value x E8M0 scale rounded to bf16 (E0901:84-95), f32
+# products and sums, bf16 gmm outputs, SwiGLU in f32, k-order f32 combine
+# (KC:44-54). ``torch_dequant`` is pinned against the oracle's dequant by the
+# tests that use it.
+# ---------------------------------------------------------------------------
+
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+               -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def torch_round_bf16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+def torch_dequant(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Raw packed e2m1 [k, n/2] (element 2j in the low nibble) and E8M0 codes
+    [k/32, n] -> f32 [k, n] holding bf16(value * 2^(c-127)) (code 0 -> +0)."""
+    lut = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=codes.device)
+    c = codes.to(torch.int64)
+    k, n2 = codes.shape
+    v = torch.stack([lut[c & 0xF], lut[c >> 4]], dim=-1).reshape(k, 2 * n2)
+    s = (scales.to(torch.int32) << 23).view(torch.float32)  # 2^(c-127); c = 0 -> +0
+    return torch_round_bf16(v * s.repeat_interleave(32, dim=0))
+
+
+def torch_layer_reference(x, ids, w16, w13, s13, w2, s2, act_limit=None):
+    """out[t] = bf16(sum_k f32(y[t, k]) * f32(w16[t, k])), y = bf16(gmm2(bf16(
+    swiglu(gmm1(x))))) per (token, expert) with raw e2m1 weights w13 [E, H, I]
+    / w2 [E, I, H/2] bytes and E8M0 scales, all in fp32 on x's device."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        t, h = x.shape
+        k = ids.shape[1]
+        inter = s2.shape[1] * 32
+        xf = x.float()
+        y = torch.zeros((t, k, h), dtype=torch.float32, device=x.device)
+        for ex in torch.unique(ids).tolist():
+            tok, slot = (ids == ex).nonzero(as_tuple=True)
+            a = xf[tok] @ torch_dequant(w13[ex], s13[ex])
+            g, u = a[:, :inter], a[:, inter:]
+            if act_limit is not None:
+                g = g.clamp(max=act_limit)
+                u = u.clamp(-act_limit, act_limit)
+            hdn = torch_round_bf16(g * torch.sigmoid(g) * u)
+            y[tok, slot] = torch_round_bf16(hdn @ torch_dequant(w2[ex], s2[ex]))
+        acc = torch.zeros((t, h), dtype=torch.float32, device=x.device)
+        wf = w16.float()
+        for kk in range(k):
+            acc = acc + y[:, kk] * wf[:, kk:kk + 1]
+        return acc.to(torch.bfloat16)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def assert_layer_close(got: torch.Tensor, ref: torch.Tensor, k: int, what=""):
+    """The layer tolerance (stated): relative Frobenius error at most
+    gemm_rel_tol(k) and max-abs error at most 2 bf16 ulps of max|ref|, where
+    the reference already rounds like the reference path, so only f32
+    summation order (and a bf16 rounding that it flips) differs."""
+    g = got.float().cpu().numpy()
+    r = ref.float().cpu().numpy()
+    assert np.all(np.isfinite(g)), f"{what}: non-finite output"
+    rf = rel_fro(g, r)
+    assert rf <= gemm_rel_tol(k), f"{what}: rel Frobenius {rf:.3e} > {gemm_rel_tol(k):.3e}"
+    amax = float(np.max(np.abs(r)))
+    ulp = 2.0 ** (np.floor(np.log2(amax)) - 7) if amax > 0 else 0.0
+    err = float(np.max(np.abs(g - r)))
+    assert err <= 2 * ulp + 1e-30, f"{what}: max-abs {err:.3e} > 2 ulp ({ulp:.3e})"
+    return rf, err / ulp if ulp else 0.0

@@ -126,3 +126,62 @@ def test_build_writes_library_in_tree():
     from dw_tpu_b200 import _lib
     assert os.path.dirname(_lib.LIB_PATH) == os.path.join(ROOT, "dw_tpu_b200")
     assert os.path.exists(_lib.LIB_PATH)
+
+
+def _layer_tensors(t=8, e=4, h=256, i=128, layout="e2m1"):
+    import torch
+    x = torch.zeros((t, h), dtype=torch.bfloat16)
+    lg = torch.zeros((t, e), dtype=torch.bfloat16)
+    if layout == "e2m1":
+        w13 = torch.zeros((e, h, i), dtype=torch.uint8)
+        w2 = torch.zeros((e, i, h // 2), dtype=torch.uint8)
+    else:
+        w13 = torch.zeros((e, 2 * i, h // 2), dtype=torch.uint8)
+        w2 = torch.zeros((e, h, i // 2), dtype=torch.uint8)
+    s13 = torch.zeros((e, h // 32, 2 * i), dtype=torch.uint8)
+    s2 = torch.zeros((e, i // 32, h), dtype=torch.uint8)
+    out = torch.zeros((t, h), dtype=torch.bfloat16)
+    return x, lg, w13, s13, w2, s2, out
+
+
+@pytest.mark.parametrize("layout", ["e2m1", "b200"])
+def test_layer_wrappers_check_shapes_before_any_launch(layout):
+    """The one-call layer wrappers reject a wrong-sized out or weight tensor
+    (the C layer sizes its tensor maps and stores from the shapes alone)."""
+    import torch
+    from dw_tpu_b200 import ops
+    x, lg, w13, s13, w2, s2, out = _layer_tensors(layout=layout)
+    ws = torch.zeros(1 << 16, dtype=torch.uint8)
+    bad = {
+        "out_rows": dict(out=out[:4]),
+        "out_dtype": dict(out=out.float()),
+        "w13": dict(w13=w13[:, :, : w13.shape[2] // 2]),
+        "w2": dict(w2=w2[:2]),
+        "s13": dict(s13=s13[:, :4]),
+        "s2_dtype": dict(s2=s2.float()),
+    }
+    for name, kw in bad.items():
+        args = dict(hidden=x, logits=lg, w13=w13, s13=s13, w2=w2, s2=s2, out=out)
+        args.update(kw)
+        with pytest.raises(ValueError):
+            ops.moe_layer_fp4_out(args["hidden"], args["logits"], 2, args["w13"], args["s13"],
+                                  args["w2"], args["s2"], args["out"], ws, layout=layout)
+        with pytest.raises(ValueError):
+            ops.moe_layer_fp4_noalloc_out(args["hidden"], args["logits"], 2, args["w13"],
+                                          args["s13"], args["w2"], args["s2"], args["out"],
+                                          layout=layout)
+    # well-formed host tensors get past the shape checks and stop at the CUDA check
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.moe_layer_fp4_out(x, lg, 2, w13, s13, w2, s2, out, ws, layout=layout)
+
+
+def test_package_import_does_not_map_the_library():
+    """Importing the package (e.g. for its input generators) maps no library;
+    the first op call does."""
+    import subprocess
+    import sys
+    code = ("import dw_tpu_b200, dw_tpu_b200.synthetic, sys\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "sys.exit(3 if 'libdw_moe.so' in maps else 0)\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]

@@ -39,15 +39,10 @@ def _bits(t):
     return t.cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("world,t,e,k,h,dist", [
-    (2, 16, 256, 8, 4096, "uniform"),
-    (4, 128, 256, 8, 512, "zipf"),
-    (8, 64, 256, 8, 256, "uniform"),
-    (8, [5, 0, 17, 64, 1, 33, 2, 9], 64, 6, 128, "zipf"),   # ragged, one empty rank
-    (1, 40, 16, 4, 64, "uniform"),                           # degenerate: no exchange
-])
-def test_ep_dispatch_combine_bit_exact(ep, world, t, e, k, h, dist):
-    hid, ids, w = _inputs(world, t, e, k, h, seed=world + e, dist=dist)
+def _exchange_bit_exact(ep, world, t, e, k, h, dist, seed):
+    """One dispatch + combine of `world` emulated ranks against the oracle:
+    receive rows, group sizes and combine output bit for bit."""
+    hid, ids, w = _inputs(world, t, e, k, h, seed=seed, dist=dist)
     tmax = max(x.shape[0] for x in hid) or 1
     ctxs = ep.create_local_contexts(world, max_tokens=tmax, hidden=h, topk=k, num_experts=e)
     try:
@@ -62,9 +57,9 @@ def test_ep_dispatch_combine_bit_exact(ep, world, t, e, k, h, dist):
             n = int(rgs.sum())
             assert np.array_equal(gs.cpu().numpy(), rgs), r
             assert np.array_equal(_bits(recv[:n]), O.f32_to_bf16_bits(rrows)), r
-            # expert outputs: any values, in receive order
+            # expert outputs: any values, in receive order (the received rows only)
             y = O.round_bf16(np.random.default_rng(r).standard_normal(
-                (ctxs[r].capacity, h)).astype(np.float32))
+                (max(n, 1), h)).astype(np.float32))
             ys.append(y)
         outs = ep.emulated_combine(ctxs, [np_to_bf16(y) for y in ys],
                                    [torch.from_numpy(x).cuda() for x in w])
@@ -77,6 +72,66 @@ def test_ep_dispatch_combine_bit_exact(ep, world, t, e, k, h, dist):
     finally:
         for c in ctxs:
             c.close()
+
+
+@pytest.mark.parametrize("world,t,e,k,h,dist", [
+    (2, 16, 256, 8, 4096, "uniform"),
+    (4, 128, 256, 8, 512, "zipf"),
+    (8, 64, 256, 8, 256, "uniform"),
+    (8, [5, 0, 17, 64, 1, 33, 2, 9], 64, 6, 128, "zipf"),   # ragged, one empty rank
+    (1, 40, 16, 4, 64, "uniform"),                           # degenerate: no exchange
+])
+def test_ep_dispatch_combine_bit_exact(ep, world, t, e, k, h, dist):
+    _exchange_bit_exact(ep, world, t, e, k, h, dist, seed=world + e)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("dist", ["uniform", "zipf"])
+def test_ep_cfg2_full_size_bit_exact(ep, world, dist):
+    """BASELINE config 2 at its largest size: 512 tokens per rank of H=4096,
+    top-8 over 256 experts, uniform or Zipf(1.2) routing, 4 and 8 ranks."""
+    _exchange_bit_exact(ep, world, 512, 256, 8, 4096, dist, seed=40 + world)
+
+
+@pytest.mark.parametrize("t", [2, 16, 64, 128, 256, 512])
+def test_ep_cfg4_token_counts_bit_exact(ep, t):
+    """BASELINE config 4's per-rank token counts ({1, 8, 32, 64, 128, 256}
+    doubled) on 8 ranks with Zipf(1.2) routing, which leaves some experts
+    empty and others hot."""
+    _exchange_bit_exact(ep, 8, t, 256, 8, 4096, "zipf", seed=60 + t)
+
+
+def test_ep_wait_runs_out_and_recovers(ep):
+    """A rank that never publishes its counts: the other rank's dispatch waits
+    on a count word that nothing writes, gives up after the shortened limit
+    (10 ms) with DWM_DEV_TIMEOUT and returns; after every rank's context is
+    created again, the next exchange is bit-exact."""
+    import time
+    from dw_tpu_b200 import _lib as L
+    world, t, e, k, h = 2, 16, 32, 4, 256
+    hid, ids, _ = _inputs(world, t, e, k, h, seed=91)
+    ctxs = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        for c in ctxs:
+            c.set_wait_limit(0.01)
+        assert L.device_status() == 0
+        x0, i0 = np_to_bf16(hid[0]), torch.from_numpy(ids[0]).cuda()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for phase in (L.EP_COUNTS, L.EP_ROWS, L.EP_WAIT):  # rank 1 never runs COUNTS
+            ctxs[0].dispatch(x0, i0, phases=phase)
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+        bits = L.device_status()
+        assert bits & L.DEV_TIMEOUT, bits
+        assert elapsed < 5.0, elapsed  # two bounded waits of 10 ms, not the 2 s default
+        with pytest.raises(ValueError):
+            ctxs[0].set_wait_limit(0.0)
+    finally:
+        for c in ctxs:
+            c.close()
+    _exchange_bit_exact(ep, world, t, e, k, h, "uniform", seed=92)
+    assert L.device_status() == 0
 
 
 def test_ep_repeated_steps_and_f32_outputs(ep):
@@ -285,6 +340,47 @@ def test_ep_layer_matches_single_device_layer(ep, layout, t):
             torch.cuda.synchronize()
             rf = rel_fro(bf16_to_np(outs[r]), bf16_to_np(ref))
             assert rf < gemm_rel_tol(i), (r, rf)
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_ep_layer_full_size_matches_single_device(ep):
+    """The cfg1 architecture (H=4096, I=2048, 256 FP4 experts, top-8 sigmoid)
+    as an EP layer of 8 emulated ranks with 32 tokens each: every rank's output
+    matches the single-device layer over all 256 experts on its tokens, and the
+    plain-PyTorch fp32 reference."""
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import _lib as L
+    from dw_tpu_b200 import synthetic
+    from tests.gpu_util import assert_layer_close, torch_layer_reference
+    world, t, e, h, i, k = 8, 32, 256, 4096, 2048, 8
+    raw = synthetic.moe_weights(e, h, i, seed=7, device="cuda")
+    w = raw.to_b200()
+    le = e // world
+    ctxs = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        layers = [ep.EPMoELayer(dw.FP4MoEWeights(w.w13[r * le:(r + 1) * le],
+                                                 w.s13[r * le:(r + 1) * le],
+                                                 w.w2[r * le:(r + 1) * le],
+                                                 w.s2[r * le:(r + 1) * le], w.layout),
+                                ctxs[r], k) for r in range(world)]
+        xs, lgs = [], []
+        for r in range(world):
+            x, router = synthetic.layer_inputs(t, h, e, seed=70 + r)
+            xs.append(x.cuda())
+            lgs.append((x.float() @ router.float()).to(torch.bfloat16).cuda())
+        outs = ep.EPMoELayer.forward_emulated(layers, xs, lgs)
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        single = dw.MoELayer(w, k, t)
+        for r in range(world):
+            ref = single(xs[r], lgs[r])
+            torch.cuda.synchronize()
+            assert_layer_close(outs[r], ref, i, f"rank {r} vs single device")
+            ref32 = torch_layer_reference(xs[r], single.ids[:t], single.w16[:t], raw.w13,
+                                          raw.s13, raw.w2, raw.s2)
+            assert_layer_close(outs[r], ref32, i, f"rank {r} vs fp32 reference")
     finally:
         for c in ctxs:
             c.close()

@@ -69,6 +69,7 @@ def test_gemm_variant_choice():
     assert gemm_variant("b200", 2) == 3
     assert gemm_variant("b200", 16) == 4
     assert gemm_variant("b200", 64) == 1
+    assert gemm_variant("b200", 256) == 7
 
 
 def _free_port():
@@ -126,3 +127,57 @@ def test_gloo_world2_exchange_and_comparison_collectives():
         assert p.exitcode == 0
     for rank, ok_h, bad, ok_ag, ok_rs in res:
         assert ok_h and bad and ok_ag and ok_rs, (rank, ok_h, bad, ok_ag, ok_rs)
+
+
+def _a2a_worker(rank, world, port, q, t_per_rank, e, k, h, dist_):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from dw_tpu_b200 import ep, synthetic
+        hid, ids, w = [], [], []
+        for r in range(world):
+            rng = np.random.default_rng(100 + r)
+            hid.append(O.round_bf16(rng.standard_normal((t_per_rank[r], h)).astype(np.float32)))
+            i, ww = synthetic.route_ids(t_per_rank[r], e, k, seed=200 + r, dist=dist_)
+            ids.append(i)
+            w.append(ww)
+        xch = ep.NcclExchange(e, h, k)
+        recv, gs = xch.dispatch(torch.from_numpy(hid[rank]), torch.from_numpy(ids[rank]))
+        ref = O.ep_dispatch(hid, ids, e)
+        ok_gs = np.array_equal(gs.numpy(), ref[rank][1])
+        ok_rows = np.array_equal(recv.numpy(), ref[rank][0])
+        # expert outputs: the received rows scaled by 1 + rank, returned to the owners
+        y = recv * (1.0 + rank)
+        rows = xch.return_rows(y).numpy()
+        want = np.zeros_like(rows)
+        for owner in range(world):
+            src = ref[owner][2]
+            mine = src[:, 0] == rank
+            want[src[mine, 1] * k + src[mine, 2]] = ref[owner][0][mine] * (1.0 + owner)
+        ok_back = np.array_equal(rows, want)
+        q.put((rank, ok_gs, ok_rows, ok_back))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,t,dist_", [(2, [16, 16], "uniform"), (4, [9, 0, 24, 5], "zipf")])
+def test_gloo_nccl_exchange_path_receive_order(world, t, dist_):
+    """The all_to_all_single comparison path (NcclExchange) delivers the
+    oracle's EP receive order and group sizes, and returns each pair's expert
+    output to its owner, on gloo process groups."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_a2a_worker, args=(r, world, port, q, t, 32, 4, 16, dist_))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok_gs, ok_rows, ok_back in res:
+        assert ok_gs and ok_rows and ok_back, (rank, ok_gs, ok_rows, ok_back)

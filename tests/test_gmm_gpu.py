@@ -195,7 +195,7 @@ def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
         r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
                          out_dtype="f32" if dt == torch.float32 else "bf16")
         r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in (0, 1, 2, 5):
+        for variant in (0, 1, 2):
             got = ops.gmm_fp4_out(x, b200, sc, g,
                                   torch.empty((400, n_out), dtype=dt, device="cuda"), act=act,
                                   zero_init=True, layout="b200", variant=variant)
@@ -210,49 +210,6 @@ def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
     r32, _ = O.gmm_f32(lhs, packed, scales, gs)
     out = dw.gmm_v2(x, b200, g, sc, rhs_layout="b200")
     assert_gemm_close(bf16_to_np(out), r, r32, 128, rows=v)
-
-
-@pytest.mark.parametrize("sd", ["u8", "bf16", "f32", "u8_wide"])
-def test_cm_layout_tmem_kernel_matches_e2m1(dw, sd):
-    """The column-major CM layout (weights decoded into TMEM by the tcgen05
-    kernel, variant 6): the re-layout matches the oracle and inverts, and the
-    GEMM gives the raw e2m1 path's bits (the same decoded bf16 weights and
-    UMMA order) for plain, SwiGLU and f32 outputs, with ragged groups (one
-    empty, one above 128 rows) and E8M0 codes 0 and > 132."""
-    from dw_tpu_b200 import ops
-    from dw_tpu_b200 import _lib as L
-    lo, hi = (0, 140) if sd == "u8_wide" else (120, 140)
-    lhs, packed, scales, gs = _case(11, 400, 128, 512, 4, gs=[3, 0, 70, 300], lo=lo, hi=hi)
-    if sd in ("u8", "u8_wide"):
-        sc = torch.from_numpy(scales)
-    elif sd == "bf16":
-        sc = torch.from_numpy(O.e8m0_decode(scales)).to(torch.bfloat16)
-    else:
-        sc = torch.from_numpy(O.e8m0_decode(scales))
-    sc = sc.cuda()
-    raw = torch.from_numpy(packed).cuda()
-    cm = ops.fp4_to_cm_out(raw)
-    assert np.array_equal(cm.cpu().numpy(), O.to_cm_layout(packed))
-    assert torch.equal(ops.fp4_to_cm_out(cm, inverse=True), raw)
-    x = np_to_bf16(lhs)
-    g = torch.from_numpy(gs).cuda()
-    for act, n_out, dt in ((L.ACT_NONE, 512, torch.bfloat16), (L.ACT_SWIGLU, 256, torch.bfloat16),
-                           (L.ACT_NONE, 512, torch.float32)):
-        ref = ops.gmm_fp4_out(x, raw, sc, g, torch.empty((400, n_out), dtype=dt, device="cuda"),
-                              act=act, zero_init=True)
-        kind = "swiglu" if act == L.ACT_SWIGLU else None
-        r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
-                         out_dtype="f32" if dt == torch.float32 else "bf16")
-        r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in (0, 6):
-            got = ops.gmm_fp4_out(x, cm, sc, g, torch.empty((400, n_out), dtype=dt, device="cuda"),
-                                  act=act, zero_init=True, layout="cm", variant=variant)
-            torch.cuda.synchronize()
-            L.raise_on_device_error()
-            assert_gemm_close(to_np(got), O.round_bf16(r) if dt == torch.bfloat16 else r, r32,
-                              128, rows=v)
-            assert np.all(to_np(got)[~v] == 0)
-            assert torch.equal(ref.view(torch.int16), got.view(torch.int16)), (act, variant)
 
 
 @pytest.mark.parametrize("sd", ["u8", "bf16", "f32", "u8_wide"])
@@ -380,8 +337,8 @@ def test_gmm_decode_regime_group_offset(dw):
 
 @pytest.mark.parametrize("layout", ["b200", "e2m1"])
 def test_gmm_prefill_tiles(dw, layout):
-    """Groups of 129-300 rows: 128- and 256-row tcgen05 tiles, partial tiles,
-    SwiGLU, against the oracle."""
+    """Groups of 129-300 rows: 128-row tcgen05 tiles on one CTA and on CTA
+    pairs, partial tiles, SwiGLU, against the oracle."""
     from dw_tpu_b200 import ops
     from dw_tpu_b200 import _lib as L
     gs = [300, 0, 200, 170, 129]
@@ -394,7 +351,7 @@ def test_gmm_prefill_tiles(dw, layout):
     for act, kind, n_out in ((L.ACT_NONE, None, 512), (L.ACT_SWIGLU, "swiglu", 256)):
         r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind)
         r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in ((0, 1, 5) if layout == "b200" else (0,)):
+        for variant in ((0, 1, 7) if layout == "b200" else (0,)):
             out = torch.full((m, n_out), 5.0, dtype=torch.bfloat16, device="cuda")
             ops.gmm_fp4_out(np_to_bf16(lhs), codes, sc, g, out, act=act, zero_init=True,
                             layout=layout, variant=variant)
@@ -422,3 +379,30 @@ def test_gmm_bad_group_sizes_reported(dw):
     bits = _lib.device_status()
     assert bits & _lib.DEV_BAD_INDEX
     assert out.shape == (32, 256)
+
+
+@pytest.mark.parametrize("scale_exp", [-70, 0, 40])
+@pytest.mark.parametrize("variant", [3, 4])
+def test_decode_kernel_token_magnitudes(dw, scale_exp, variant):
+    """The mma.sync decode kernel keeps the reference's products for tokens
+    far from 1: whole token rows of magnitude ~2^-70 (which a fixed 2^64
+    token pre-scale used to flush) and ~2^40, with E8M0 codes that take both
+    the post-MMA path and the exact path (code 0 and codes above its range)."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    wide_hi = 215 if scale_exp <= 0 else 160  # keep the reference's f32 sums finite
+    for lo, hi in ((118, 130), (0, wide_hi)):
+        lhs, packed, scales, gs = _case(21, 96, 256, 512, 8, lo=lo, hi=hi)
+        lhs = (lhs * np.float32(2.0) ** scale_exp).astype(np.float32)  # exact power-of-two scaling
+        b200 = dw.fp4_weight_to_codes(torch.from_numpy(packed).cuda())
+        out = torch.full((96, 512), 3.0, dtype=torch.bfloat16, device="cuda")
+        ops.gmm_fp4_out(np_to_bf16(lhs), b200, torch.from_numpy(scales).cuda(),
+                        torch.from_numpy(gs).cuda(), out, zero_init=True, layout="b200",
+                        variant=variant)
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        r, v = O.gmm_ref(lhs, packed, scales, gs)
+        r32, _ = O.gmm_f32(lhs, packed, scales, gs)
+        got = bf16_to_np(out)
+        assert np.all(np.isfinite(r32[v])), "the case must stay in range for the reference"
+        assert_gemm_close(got, r, r32, 256, rows=v)

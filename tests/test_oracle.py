@@ -76,19 +76,6 @@ def test_b200_swizzle_is_a_lossless_bit_permutation():
         assert got == nib[g, kk, c], (g, kk, c)
 
 
-def test_cm_layout_round_trip_and_element_order():
-    rng = np.random.default_rng(14)
-    raw = rng.integers(0, 256, (2, 64, 24), dtype=np.uint8)  # [g, k, n/2]
-    cm = O.to_cm_layout(raw)
-    assert cm.shape == (2, 48, 32)                              # [g, n, k/2]
-    assert np.array_equal(O.from_cm_layout(cm), raw)
-    nib = O.unpack_nibbles(raw)                                # [g, k, n]
-    words = O.b200_unswizzle(cm).view(np.uint32).reshape(2, 48, 8)
-    for (g, kk, c) in [(0, 0, 0), (1, 63, 47), (0, 9, 17), (1, 22, 5), (0, 40, 30)]:
-        got = (int(words[g, c, kk // 8]) >> (4 * (kk % 8))) & 0xF
-        assert got == nib[g, kk, c], (g, kk, c)
-
-
 def test_e8m0_roundtrip_and_lossless_flag():
     e = np.arange(-126, 128)
     s = np.ldexp(np.ones(e.shape, np.float32), e).astype(np.float32)
@@ -259,3 +246,30 @@ def test_golden_fixtures_reproduce(name, golden):
         a, b = np.asarray(fresh[key]), stored[key]
         assert a.dtype == b.dtype and a.shape == b.shape, key
         assert np.array_equal(a, b, equal_nan=True), key
+
+
+def test_cpu_baseline_layer_matches_the_oracle():
+    """oracle/layer_cpu.py (the timed CPU baseline) is the oracle's layer
+    arithmetic: its table dequant equals dequant_fp4_block bit for bit (also
+    for E8M0 codes that underflow or overflow bf16), and its layer output
+    equals fused_moe's up to f32-vs-f64 summation order."""
+    from oracle import layer_cpu as C
+    rng = np.random.default_rng(21)
+    packed = rng.integers(0, 256, (64, 48), dtype=np.uint8)
+    for lo, hi in ((123, 129), (0, 255)):
+        sc = rng.integers(lo, hi + 1, (2, 96), dtype=np.uint8)
+        got = C.dequant_fp4_lut(packed, sc).copy()
+        assert np.array_equal(got, O.dequant_fp4_block(packed, sc), equal_nan=True), (lo, hi)
+    t, e, h, i, k = 12, 8, 256, 128, 4
+    hid = O.round_bf16(rng.standard_normal((t, h)).astype(np.float32))
+    logits = O.round_bf16(rng.standard_normal((t, e)).astype(np.float32))
+    w13 = rng.integers(0, 256, (e, h, i), dtype=np.uint8)
+    s13 = rng.integers(118, 122, (e, h // 32, 2 * i), dtype=np.uint8)
+    w2 = rng.integers(0, 256, (e, i, h // 2), dtype=np.uint8)
+    s2 = rng.integers(118, 122, (e, i // 32, h), dtype=np.uint8)
+    pool, _ = C.make_pool(2)
+    with pool:
+        got = C.layer_forward(hid, logits, w13, s13, w2, s2, k, pool=pool)
+    ref = O.fused_moe(hid, logits, w13, s13, w2, s2, k)
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel < 1e-3, rel

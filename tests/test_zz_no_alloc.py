@@ -1,7 +1,8 @@
 """dwm_moe_layer_fp4_noalloc (the layer on the library's fixed device scratch)
 against dwm_moe_layer_fp4 (the same layer on a caller workspace): identical
-bits on two calls in a row. This file sorts last so that it also runs after
-every other GPU test in the same process."""
+bits on two calls in a row, and no device memory taken by a call. This file
+sorts last so that it also runs after every other GPU test in the same
+process."""
 
 import pytest
 import torch
@@ -52,3 +53,34 @@ def test_noalloc_layer_rejects_oversize_inputs():
     out = torch.empty((t, h), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError, match="scratch"):
         ops.moe_layer_fp4_noalloc_out(x, lg, k, w13, s13, w2, s2, out)
+
+
+def test_noalloc_layer_setup_call_and_no_device_allocation():
+    """A num_tokens = 0 call does only the per-device set-up; later calls take
+    no device memory: PyTorch's allocator and the device's free bytes are
+    unchanged across a call (the first real call may still load kernels)."""
+    from dw_tpu_b200 import _lib as L
+    from dw_tpu_b200 import ops, synthetic
+    t, e, h, i, k = 32, 16, 512, 256, 4
+    w = synthetic.moe_weights(e, h, i, seed=14, device="cuda").to_b200()
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 15, "cuda", lo=118,
+                                               hi=121))
+    x, router = synthetic.layer_inputs(t, h, e, seed=16)
+    x = x.cuda()
+    lg = (x.float() @ router.cuda().float()).to(torch.bfloat16)
+    out = torch.empty((t, h), dtype=torch.bfloat16, device="cuda")
+    ops.moe_layer_fp4_noalloc_out(x[:0], lg[:0], k, w.w13, w.s13, w.w2, w.s2, out[:0],
+                                  layout="b200")                     # set-up only
+    ops.moe_layer_fp4_noalloc_out(x, lg, k, w.w13, w.s13, w.w2, w.s2, out, layout="b200")
+    torch.cuda.synchronize()
+    L.raise_on_device_error()
+    first = out.clone()
+    alloc0 = torch.cuda.memory_allocated()
+    free0, _ = torch.cuda.mem_get_info()
+    ops.moe_layer_fp4_noalloc_out(x, lg, k, w.w13, w.s13, w.w2, w.s2, out, layout="b200")
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert free1 >= free0, (free0, free1)
+    assert torch.equal(out.view(torch.int16), first.view(torch.int16))
