@@ -334,10 +334,12 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
     average (the receive buffer's row count is a capacity, not a size)."""
     if layout != "b200":
         return 0
-    if expected_rows <= 8:
+    if expected_rows <= 5:
         return 3  # mma.sync kernel, 8-row token tiles
-    if expected_rows <= 16:
+    if expected_rows <= 12:
         return 4  # mma.sync kernel, 16-row token tiles
+    if expected_rows <= 40:
+        return 5  # mma.sync kernel, 32-row token tiles
     if expected_rows >= 128:
         return 7  # tcgen05 on CTA pairs (prefill)
     return 1      # tcgen05 kernel, one CTA
