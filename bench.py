@@ -803,12 +803,21 @@ def ep_extras(args, local, dev, world, rank, link_gbps):
         L.raise_on_device_error()
 
         # ---- cfg3: the prefill EP layer, T=1024 per rank ----
-        out["prefill_layer"] = ep_layer_case(ctx, local, dev, world, rank, 1024, "router",
-                                             args.seed, link_gbps)
+        serial, o_s = ep_layer_case(ctx, local, dev, world, rank, 1024, "router", args.seed,
+                                    link_gbps)
+        over, o_o = ep_layer_case(ctx, local, dev, world, rank, 1024, "router", args.seed,
+                                  link_gbps, compact=True, overlap=True)
+        differ = max_over_ranks([0.0 if torch.equal(o_s.view(torch.int16),
+                                                    o_o.view(torch.int16)) else 1.0],
+                                world, dev)[0]
+        out["prefill_layer"] = {
+            "workload": serial.pop("workload"), "serial": serial, "overlapped": over,
+            "overlap_speedup": round(serial["ms_per_step"] / over["ms_per_step"], 3),
+            "overlapped_bitwise_equal_serial": differ == 0.0}
         # ---- cfg4: the decode sweep on 8 GPUs, Zipf(1.2) ----
         if world == 8:
             cases = [ep_layer_case(ctx, local, dev, world, rank, t, "zipf", args.seed,
-                                   link_gbps, compact=True)
+                                   link_gbps, compact=True)[0]
                      for t in (2, 16, 64, 128, 256, 512)]
             out["decode_sweep"] = {"workload": "cfg4: T_rank in {1,8,32,64,128,256}x2, "
                                                "Zipf(1.2) routing, 8 GPUs", "cases": cases}
@@ -818,11 +827,14 @@ def ep_extras(args, local, dev, world, rank, link_gbps):
 
 
 def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, compact=False,
-                  iters=10):
+                  iters=10, overlap=False):
     """The EP layer on t tokens per rank: routing from a random router
-    ("router", near-uniform) or Zipf(1.2)-skewed ids; median step time, the
-    GEMM's share and rates, and the exchange times."""
+    ("router", near-uniform) or Zipf(1.2)-skewed ids; median step time (max
+    over ranks) and, for the serial layer, the GEMM's time and rate. With
+    `overlap` the exchange is folded into the CTA-pair GEMMs. Returns (the
+    record, this rank's output)."""
     import torch
+    import torch.distributed as dist
     from dw_tpu_b200 import _lib as L
     from dw_tpu_b200 import ep as ep_mod
     from dw_tpu_b200 import synthetic
@@ -834,12 +846,11 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
         ids_np, _ = synthetic.route_ids(t, E, TOPK, seed=2000 + 7 * t + rank, dist="zipf")
         logits = zipf_logits(ids_np, dev)
     expected = t * TOPK / E * world
-    layer = ep_mod.EPMoELayer(local, ctx, TOPK, expected_rows=expected)
+    layer = ep_mod.EPMoELayer(local, ctx, TOPK, expected_rows=expected, overlap=overlap)
     out = torch.empty((t, H), dtype=torch.bfloat16, device=dev)
     for _ in range(3):
         layer(x, logits, out=out)
     torch.cuda.synchronize(dev)
-    import torch.distributed as dist
     dist.barrier()
     ts = []
     with GmmTimer() as gt:
@@ -854,26 +865,28 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
     g1, g2 = gt.ms()
     gs = ctx.recv_group_sizes.cpu().numpy()
     b1, b2, active, rows = gemm_bytes(gs)
-    gmm_ms = statistics.median(g1) + statistics.median(g2)
+    gmm_ms = statistics.median(g1) + statistics.median(g2) if g1 and g2 else 0.0
     flops = 2.0 * rows * (H * 2 * I + I * H)
     m = max_over_ranks([statistics.median(ts), gmm_ms, float(gs.max()), -float(gs.min())],
                        world, dev)
     peaks = measured_peaks()
-    res = {"tokens_per_rank": t, "routing": routing, "variant": layer.variant,
+    res = {"tokens_per_rank": t, "routing": routing,
+           "variant": 7 if overlap else layer.variant, "overlap": overlap,
            "tokens_per_s": round(t * world / m[0] * 1e3, 1), "ms_per_step": round(m[0], 4),
-           "gmm_ms_rank0": round(gmm_ms, 4), "gmm_ms_max": round(m[1], 4),
            "rows_per_expert_max": int(m[2]), "rows_per_expert_min": int(-m[3])}
-    if flops / max(1, b1 + b2) > 300:  # tensor-bound (cfg3 at n >= 4)
-        peak = peaks["bf16_tflops"] if peaks else 1590.0
-        res["gmm_tflops_rank0"] = round(flops / gmm_ms / 1e9, 1)
-        res["gmm_frac_of_tensor_rank0"] = round(flops / gmm_ms / 1e9 / peak, 4)
-    else:
-        peak = peaks["hbm_gbs"] if peaks else 6650.0
-        res["gmm_GBps_rank0"] = round((b1 + b2) / (gmm_ms * 1e-3) / 1e9, 1)
-        res["gmm_frac_of_hbm_rank0"] = round((b1 + b2) / (gmm_ms * 1e-3) / 1e9 / peak, 4)
+    if gmm_ms > 0:
+        res.update({"gmm_ms_rank0": round(gmm_ms, 4), "gmm_ms_max": round(m[1], 4)})
+        if flops / max(1, b1 + b2) > 300:  # tensor-bound (cfg3 at n >= 4)
+            peak = peaks["bf16_tflops"] if peaks else 1590.0
+            res["gmm_tflops_rank0"] = round(flops / gmm_ms / 1e9, 1)
+            res["gmm_frac_of_tensor_rank0"] = round(flops / gmm_ms / 1e9 / peak, 4)
+        else:
+            peak = peaks["hbm_gbs"] if peaks else 6650.0
+            res["gmm_GBps_rank0"] = round((b1 + b2) / (gmm_ms * 1e-3) / 1e9, 1)
+            res["gmm_frac_of_hbm_rank0"] = round((b1 + b2) / (gmm_ms * 1e-3) / 1e9 / peak, 4)
     if not compact:
         res["workload"] = f"cfg3: T={t} tokens per rank, {world} ranks, router-drawn routing"
-    return res
+    return res, out
 
 
 # ----------------------------------------------------------------------------

@@ -47,6 +47,10 @@ EP_WAIT = 4
 EP_ALL = 7
 EP_PUSH = 1
 EP_REDUCE = 2
+EP_GATED = 8
+EP_PUSHED = 4
+EP_GEMM_GATED = 1
+EP_GEMM_PUSH = 2
 
 _c = ctypes
 _P = _c.c_void_p
@@ -93,6 +97,7 @@ SIGNATURES = {
     "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
     "dwm_ep_combine_shared": ([_P, _P, _I, _P, _I, _P, _I, _F, _I, _P, _I, _I, _P], _I),
     "dwm_ep_set_wait_limit": ([_P, _c.c_uint64], _I),
+    "dwm_ep_gmm_fp4": ([_P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _F, _I, _P, _I, _P], _I),
     "dwm_ep_destroy": ([_P], _I),
 }
 

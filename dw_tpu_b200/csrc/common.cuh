@@ -269,6 +269,84 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's earlier generic-proxy accesses (an acquire of data
+// that other GPUs stored) before its later async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// System-scope flags and counters (peers' memory over NVLink)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// Bounded spin until the 64-bit counter *p reaches `target` (acquire at
+// system scope); gives up after `limit` ns with DWM_DEV_TIMEOUT.
+__device__ __forceinline__ bool wait_counter_ge(const uint64_t* p, uint64_t target,
+                                                uint64_t limit, int* status) {
+  if (ld_acquire_sys64(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(64);
+    if (ld_acquire_sys64(p) >= target) return true;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit) {
+      report(status, DWM_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Expert-parallel hooks of a grouped matmul (filled by dwm_ep_gmm_fp4; all
+// null for a plain grouped matmul):
+//   gating  the token rows of local expert g are loaded only once
+//           gate_arrive[g] (rows of g stored here by every source rank so far,
+//           cumulative) reaches gate_target[g];
+//   push    output row r goes to rank (push_tags[r] >> 28)'s push_base at row
+//           (push_tags[r] & 0x0FFFFFFF) (that rank's own (token, k) pair),
+//           instead of `out`; once every CTA has stored its rows, the last one
+//           adds 1 to every rank's push_done counter (release, system scope).
+constexpr int kEpMaxWorld = 8;
+constexpr int kEpTagBits = 28;
+struct EpHooks {
+  const uint64_t* gate_arrive;
+  const uint64_t* gate_target;
+  const int32_t* push_tags;
+  uint8_t* push_base[kEpMaxWorld];
+  uint64_t* push_done[kEpMaxWorld];
+  uint32_t* ticket;  // zero between launches; the last CTA resets it
+  int world;
+  uint64_t wait_ns;
+};
+
 // ---------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores, accumulators in TMEM)
 // ---------------------------------------------------------------------------

@@ -68,16 +68,24 @@ constexpr int ROW_BITS = 28;    // sent-row code: owner << ROW_BITS | row
 constexpr int64_t MAX_CAP = 1LL << ROW_BITS;
 
 struct Layout {  // byte offsets inside every rank's symmetric buffer
-  size_t ready;   // uint32 [MAX_WORLD]: epoch whose outputs source s has made readable
-  size_t arrive;  // uint64: dispatch arrivals (one per rank and epoch, monotonic)
-  size_t counts;  // uint64 [MAX_WORLD][E]: (epoch << 32) | count of expert x from source s
-  size_t recv;    // bf16 [cap][H]: received rows, expert-major
-  size_t outb;    // [cap][H], 4-byte capacity: expert outputs of the received rows
+  size_t ready;      // uint32 [MAX_WORLD]: epoch whose outputs source s has made readable
+  size_t arrive;     // uint64: dispatch arrivals (one per rank and epoch, monotonic)
+  size_t delivered;  // uint64: ranks whose gmm2 pushed this rank's outputs (monotonic)
+  size_t counts;     // uint64 [MAX_WORLD][E]: (epoch << 32) | count of expert x from source s
+  size_t exp_arrive; // uint64 [E/world]: rows of each local expert received (monotonic)
+  size_t tags;       // int32 [cap]: source rank << ROW_BITS | source pair of each received row
+  size_t recv;       // bf16 [cap][H]: received rows, expert-major
+  size_t outb;       // [cap][H], 4-byte capacity: expert outputs of the received rows, or
+                     // (pushed mode) this rank's own pairs' outputs, row = pair
   size_t total;
 };
 
-// Per-rank control words (ordinary device memory, not shared with peers).
-enum Ctl { CTL_EPOCH = 0, CTL_FIRST = 1, CTL_DONE = 2, CTL_RECV_ROWS = 3, CTL_WORDS = 4 };
+// Per-rank control words (ordinary device memory, not shared with peers),
+// followed by the per-local-expert arrival targets (uint64 [E/world]).
+enum Ctl {
+  CTL_EPOCH = 0, CTL_FIRST = 1, CTL_DONE = 2, CTL_RECV_ROWS = 3, CTL_GEMM_TICKET = 4,
+  CTL_PUSH_STEPS = 5, CTL_WORDS = 6
+};
 
 struct Params {
   uint8_t* peer[MAX_WORLD];
@@ -86,39 +94,9 @@ struct Params {
   int64_t cap;
   int32_t* sent;  // [max_pairs]: owner << ROW_BITS | row of each own pair, -1 if dropped
   uint32_t* ctl;  // [CTL_WORDS]
+  uint64_t* target;  // [E/world]: rows each local expert must have received (monotonic)
   uint64_t wait_ns;  // limit of every device-side wait (dwm_ep_set_wait_limit)
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_relaxed_sys64(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
 
 // Bounded spin until *p >= target (32-bit epoch flag); gives up after `limit`
 // ns (DWM_DEV_TIMEOUT).
@@ -172,8 +150,8 @@ __device__ __forceinline__ uint64_t* count_word(const Params& P, int rank_mem, i
 }
 
 // Dynamic shared memory of the dispatch kernel (ints): tot, run, col, scan,
-// dest [E] each, then the chunk's experts and rows [XFER_THREADS] each.
-inline size_t dispatch_smem_bytes(int e) { return (size_t)(5 * e + 2 * XFER_THREADS) * 4; }
+// dest, run0 [E] each, then the chunk's experts and rows [XFER_THREADS] each.
+inline size_t dispatch_smem_bytes(int e) { return (size_t)(6 * e + 2 * XFER_THREADS) * 4; }
 
 // Exclusive scan of in[0, n) into out by warp 0 (chunked per lane).
 __device__ __forceinline__ void warp0_exclusive_scan(const int* in, int* out, int n) {
@@ -201,7 +179,10 @@ __device__ __forceinline__ void warp0_exclusive_scan(const int* in, int* out, in
   }
 }
 
-// The dispatch (phases: DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_WAIT).
+// The dispatch (phases: DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_WAIT; with
+// DWM_EP_GATED each row also carries its tag, and each CTA adds the rows it
+// stored for every expert to the owner's arrival counter of that expert, so
+// the owner's grouped matmul can start on an expert as soon as its rows are in).
 __global__ void __launch_bounds__(XFER_THREADS)
     ep_dispatch_kernel(const __grid_constant__ Params P, const uint4* __restrict__ hidden,
                        const int32_t* __restrict__ ids, int32_t* recv_group_sizes, int ph,
@@ -212,13 +193,15 @@ __global__ void __launch_bounds__(XFER_THREADS)
   int* col = sm + 2 * P.E;       // all ranks' count of each expert
   int* scan = sm + 3 * P.E;      // exclusive scan of col
   int* dest = sm + 4 * P.E;      // first receive row of this rank's pairs of each expert
-  int* cx = sm + 5 * P.E;        // chunk: expert of each pair (-1: dropped)
+  int* run0 = sm + 5 * P.E;      // run before this CTA's slice (gated arrivals)
+  int* cx = sm + 6 * P.E;        // chunk: expert of each pair (-1: dropped)
   int* crow = cx + XFER_THREADS; // chunk: receive row of each pair (-1: dropped)
   __shared__ uint32_t s_epoch;
   __shared__ int s_first, s_last, s_fail;
   const int tid = threadIdx.x;
   const int n = P.T * P.topk;
   const bool counts = ph & DWM_EP_COUNTS, rows = ph & DWM_EP_ROWS;
+  const bool gated = ph & DWM_EP_GATED;
   if (tid == 0) {
     s_epoch = P.ctl[CTL_EPOCH] + (counts ? 1u : 0u);
     s_first = counts ? atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u : 0;
@@ -272,7 +255,11 @@ __global__ void __launch_bounds__(XFER_THREADS)
     for (int x = tid; x < P.E; x += blockDim.x) {
       const int owner = x / P.LE;
       dest[x] += scan[x] - scan[owner * P.LE];
-      if (blockIdx.x == 0 && owner == P.rank) recv_group_sizes[x - owner * P.LE] = col[x];
+      run0[x] = run[x];
+      if (blockIdx.x == 0 && owner == P.rank) {
+        recv_group_sizes[x - owner * P.LE] = col[x];
+        if (gated) P.target[x - owner * P.LE] += (uint64_t)col[x];
+      }
     }
     if (blockIdx.x == 0 && tid == 0) {
       const int last = (P.rank + 1) * P.LE - 1;
@@ -301,6 +288,9 @@ __global__ void __launch_bounds__(XFER_THREADS)
         }
         crow[tid] = row;
         P.sent[c0 + tid] = row < 0 ? -1 : ((x / P.LE) << ROW_BITS) | row;
+        if (gated && row >= 0)  // the owner's gmm2 sends this row's output back to pair c0+tid
+          reinterpret_cast<int32_t*>(P.peer[x / P.LE] + P.L.tags)[row] =
+              (P.rank << ROW_BITS) | (c0 + tid);
       }
       __syncthreads();
       if (tid < cn && cx[tid] >= 0) atomicAdd(&run[cx[tid]], 1);
@@ -332,6 +322,20 @@ __global__ void __launch_bounds__(XFER_THREADS)
     }
     if (s_fail)  // counts never came: this slice's pairs are dropped
       for (int j = j0 + tid; j < j1; j += blockDim.x) P.sent[j] = -1;
+    if (gated && !s_fail) {
+      // Every thread's row and tag stores precede (bar.sync) each release:
+      // one system-scope add per (CTA, expert) publishes this CTA's rows.
+      __syncthreads();
+      for (int x = tid; x < P.E; x += blockDim.x) {
+        const int d = run[x] - run0[x];
+        if (d > 0) {
+          const int owner = x / P.LE;
+          red_release_sys_add(
+              reinterpret_cast<uint64_t*>(P.peer[owner] + P.L.exp_arrive) + (x - owner * P.LE),
+              (uint64_t)d);
+        }
+      }
+    }
   }
   __syncthreads();
   // The last CTA to finish: reset the tickets, advance the epoch, signal the
@@ -381,9 +385,16 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   const int tid = threadIdx.x;
+  const bool pushed = ph & DWM_EP_PUSHED;
   if (tid == 0) {
     s_epoch = P.ctl[CTL_EPOCH];
     s_ok = 1;
+    // Pushed mode: every rank's gmm2 has stored its outputs of this rank's
+    // pairs here once `delivered` has grown by world this step.
+    if (pushed && (ph & DWM_EP_REDUCE) &&
+        !wait_counter_ge(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.delivered),
+                         (uint64_t)(P.ctl[CTL_PUSH_STEPS] + 1) * P.world, P.wait_ns, status))
+      s_ok = 0;
     // The outputs were written by earlier kernels on this stream: a release
     // store at system scope publishes them.
     if ((ph & DWM_EP_PUSH) && atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u)
@@ -407,8 +418,11 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
       Row v[KB];
       int code[KB] = {};
       auto load = [&](int q) {
-        const uint8_t* base = P.peer[code[q] >> ROW_BITS] + P.L.outb;
-        const int64_t off = (int64_t)(code[q] & ROW_MASK) * P.H + (int64_t)c * 8;
+        // Pulled: the owner's output row; pushed: this rank's row of the pair.
+        const uint8_t* base = pushed ? P.peer[P.rank] + P.L.outb
+                                     : P.peer[code[q] >> ROW_BITS] + P.L.outb;
+        const int64_t row = pushed ? t * P.topk + k0 + q : (int64_t)(code[q] & ROW_MASK);
+        const int64_t off = row * P.H + (int64_t)c * 8;
         if constexpr (XD == DWM_BF16)
           v[q] = moe::load8_bf16_raw_cg(base, off);
         else
@@ -419,8 +433,8 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
         code[q] = mine && k0 + q < P.topk ? __ldg(P.sent + t * P.topk + k0 + q) : -1;
 #pragma unroll
       for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0 && (code[q] >> ROW_BITS) == P.rank) load(q);
-      if (k0 == 0) {  // the peers' outputs: wait once for their announcements
+        if (code[q] >= 0 && (pushed || (code[q] >> ROW_BITS) == P.rank)) load(q);
+      if (k0 == 0 && !pushed) {  // the peers' outputs: wait once for their announcements
         if (tid < P.world && tid != P.rank &&
             !wait_flag(reinterpret_cast<const uint32_t*>(P.peer[P.rank] + P.L.ready) + tid,
                        s_epoch, P.wait_ns, status))
@@ -430,7 +444,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
       if (!s_ok) break;
 #pragma unroll
       for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0 && (code[q] >> ROW_BITS) != P.rank) load(q);
+        if (code[q] >= 0 && !pushed && (code[q] >> ROW_BITS) != P.rank) load(q);
 #pragma unroll
       for (int q = 0; q < KB; ++q)
         if (code[q] >= 0) {
@@ -451,6 +465,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
     __threadfence();
     P.ctl[CTL_DONE] = 0;
     P.ctl[CTL_FIRST] = 0;
+    if (pushed && (ph & DWM_EP_REDUCE)) P.ctl[CTL_PUSH_STEPS] += 1;
   }
 }
 
@@ -465,7 +480,8 @@ struct dwm_ep {
   int64_t cap, max_pairs;
   ep::Layout L;
   uint8_t* base = nullptr;     // own symmetric buffer
-  int32_t* scratch = nullptr;  // sent [max_pairs], then the control words
+  int32_t* scratch = nullptr;  // sent [max_pairs], the control words, then targets [E/world]
+  size_t target_off = 0;       // byte offset of the targets inside scratch
   uint8_t* peer[MAX_WORLD] = {};
   bool peer_ipc[MAX_WORLD] = {};
   bool connected = false;
@@ -493,6 +509,7 @@ ep::Params make_params(const dwm_ep* c) {
   P.wait_ns = c->wait_ns;
   P.sent = c->scratch;
   P.ctl = reinterpret_cast<uint32_t*>(c->scratch + c->max_pairs);
+  P.target = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(c->scratch) + c->target_off);
   return P;
 }
 
@@ -540,17 +557,22 @@ extern "C" int dwm_ep_create(int rank, int world, int max_tokens, int hidden, in
   ep::Layout& L = c->L;
   L.ready = 0;
   L.arrive = 64;
+  L.delivered = 72;
   L.counts = 128;
-  L.recv = align_up(L.counts + (size_t)MAX_WORLD * num_experts * 8, 256);
+  L.exp_arrive = align_up(L.counts + (size_t)MAX_WORLD * num_experts * 8, 256);
+  L.tags = align_up(L.exp_arrive + (size_t)c->local_experts * 8, 256);
+  L.recv = align_up(L.tags + (size_t)cap * 4, 256);
   L.outb = align_up(L.recv + (size_t)cap * hidden * 2, 256);
   L.total = align_up(L.outb + (size_t)cap * hidden * 4, 256);
   int rc = check_cuda(cudaMalloc(&c->base, L.total), "ep symmetric buffer");
   if (!rc) rc = check_cuda(cudaMemset(c->base, 0, L.recv), "ep header clear");
+  c->target_off = align_up((size_t)(max_pairs + ep::CTL_WORDS) * 4, 8);
+  const size_t scratch_bytes = c->target_off + (size_t)c->local_experts * 8;
+  if (!rc) rc = check_cuda(cudaMalloc(&c->scratch, scratch_bytes), "ep scratch");
   if (!rc)
-    rc = check_cuda(cudaMalloc(&c->scratch, (size_t)(max_pairs + ep::CTL_WORDS) * 4),
-                    "ep scratch");
-  if (!rc)
-    rc = check_cuda(cudaMemset(c->scratch + max_pairs, 0, ep::CTL_WORDS * 4), "ep control clear");
+    rc = check_cuda(cudaMemset(reinterpret_cast<uint8_t*>(c->scratch) + (size_t)max_pairs * 4, 0,
+                               scratch_bytes - (size_t)max_pairs * 4),
+                    "ep control clear");
   if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "ep create");
   if (rc) {
     if (c->base) cudaFree(c->base);
@@ -634,7 +656,9 @@ extern "C" int dwm_ep_dispatch(dwm_ep* c, const void* hidden, const int32_t* top
                                void* stream) {
   int rc = check_ctx(c);
   if (rc) return rc;
-  DWM_CHECK_ARG(phases >= 1 && phases <= DWM_EP_ALL, "phases=%d", phases);
+  DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_ALL | DWM_EP_GATED) &&
+                    phases != DWM_EP_GATED,
+                "phases=%d", phases);
   DWM_CHECK_ARG(num_tokens >= 0 && num_tokens <= c->max_tokens,
                 "num_tokens=%d out of [0, max_tokens=%d]", num_tokens, c->max_tokens);
   DWM_CHECK_ARG(num_tokens == 0 || (hidden && topk_ids), "NULL input");
@@ -663,7 +687,11 @@ extern "C" int dwm_ep_combine_shared(dwm_ep* c, const void* y, int y_dtype,
                                      void* out, int out_dtype, int phases, void* stream) {
   int rc = check_ctx(c);
   if (rc) return rc;
-  DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_PUSH | DWM_EP_REDUCE), "phases=%d", phases);
+  DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_PUSH | DWM_EP_REDUCE | DWM_EP_PUSHED) &&
+                    phases != DWM_EP_PUSHED,
+                "phases=%d", phases);
+  DWM_CHECK_ARG(!(phases & DWM_EP_PUSHED) || !(phases & DWM_EP_PUSH),
+                "PUSH (announce) has no part in the pushed mode");
   DWM_CHECK_ARG(c->dispatched, "combine before any dispatch");
   DWM_CHECK_ARG(y_dtype == DWM_BF16 || y_dtype == DWM_F32, "y dtype must be bf16 or f32");
   DWM_CHECK_ARG(w_dtype == DWM_BF16 || w_dtype == DWM_F32, "weight dtype must be bf16 or f32");
@@ -671,7 +699,7 @@ extern "C" int dwm_ep_combine_shared(dwm_ep* c, const void* y, int y_dtype,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const ep::Params P = make_params(c);
   const bool reduce = phases & DWM_EP_REDUCE;
-  if (phases & DWM_EP_PUSH) {
+  if ((phases & DWM_EP_PUSH) && !(phases & DWM_EP_PUSHED)) {
     DWM_CHECK_ARG(y && moe::aligned16(y), "y must be a 16-byte aligned device pointer");
     if (y != c->base + c->L.outb) {
       const int row_bytes = c->hidden * (y_dtype == DWM_F32 ? 4 : 2);
@@ -719,6 +747,60 @@ extern "C" int dwm_ep_combine(dwm_ep* c, const void* y, int y_dtype, const void*
                               int w_dtype, void* out, int out_dtype, int phases, void* stream) {
   return dwm_ep_combine_shared(c, y, y_dtype, topk_weights, w_dtype, nullptr, DWM_F32, 1.0f,
                                DWM_BF16, out, out_dtype, phases, stream);
+}
+
+namespace dwm {
+int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+                    const int32_t* group_sizes, int num_groups, int m, int k, int n,
+                    int group_offset, int n_local, int act, float limit, int out_dtype,
+                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream);
+}
+
+extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int codes_format,
+                              const void* scales, int scale_dtype,
+                              const int32_t* recv_group_sizes, int k, int n, int act,
+                              float act_limit, int out_dtype, void* out, int mode,
+                              void* stream) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DWM_CHECK_ARG(mode == DWM_EP_GEMM_GATED || mode == DWM_EP_GEMM_PUSH, "mode=%d", mode);
+  DWM_CHECK_ARG(codes_format == DWM_FP4_B200, "the EP grouped matmul takes the B200 layout");
+  DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
+                "scale dtype must be u8 (e8m0), bf16 or f32");
+  DWM_CHECK_ARG(out_dtype == DWM_BF16 || out_dtype == DWM_F32, "out dtype must be bf16 or f32");
+  DWM_CHECK_ARG(act == DWM_ACT_NONE || act == DWM_ACT_SWIGLU || act == DWM_ACT_SWIGLU_CLAMP,
+                "unknown activation %d", act);
+  DWM_CHECK_ARG(k > 0 && n > 0 && k % 64 == 0 && n % 256 == 0,
+                "k=%d (multiple of 64) n=%d (multiple of 256)", k, n);
+  DWM_CHECK_ARG(lhs && codes && scales && recv_group_sizes, "NULL pointer");
+  DWM_CHECK_ARG(moe::aligned16(lhs) && moe::aligned16(codes) && moe::aligned16(scales),
+                "pointers must be 16-byte aligned");
+  EpHooks hk{};
+  hk.wait_ns = c->wait_ns;
+  hk.world = c->world;
+  const ep::Params P = make_params(c);
+  void* dst = out;
+  if (mode == DWM_EP_GEMM_GATED) {
+    DWM_CHECK_ARG(lhs == c->base + c->L.recv && k == c->hidden,
+                  "the gated grouped matmul reads the receive buffer (k = hidden)");
+    DWM_CHECK_ARG(out && moe::aligned16(out), "out must be a 16-byte aligned device pointer");
+    hk.gate_arrive = reinterpret_cast<const uint64_t*>(c->base + c->L.exp_arrive);
+    hk.gate_target = P.target;
+  } else {
+    DWM_CHECK_ARG(act == DWM_ACT_NONE && n == c->hidden,
+                  "the pushing grouped matmul is the down projection (no activation, n = "
+                  "hidden)");
+    hk.push_tags = reinterpret_cast<const int32_t*>(c->base + c->L.tags);
+    for (int p = 0; p < c->world; ++p) {
+      hk.push_base[p] = c->peer[p] + c->L.outb;
+      hk.push_done[p] = reinterpret_cast<uint64_t*>(c->peer[p] + c->L.delivered);
+    }
+    hk.ticket = P.ctl + ep::CTL_GEMM_TICKET;
+    dst = c->base + c->L.outb;  // not written: every row goes to its token's owner
+  }
+  return launch_gmm_pair(lhs, codes, scales, scale_dtype, recv_group_sizes, c->local_experts,
+                         (int)c->cap, k, n, 0, c->local_experts, act, act_limit, out_dtype, 0, dst,
+                         &hk, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dwm_ep_set_wait_limit(dwm_ep* c, uint64_t limit_ns) {

@@ -40,7 +40,7 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
-                    int zero_init, void* out, cudaStream_t stream);
+                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream);
 
 namespace gmm {
 
@@ -985,11 +985,11 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 }
 
 // variant: 0 = choose, 1 = tcgen05 (shared-memory decode) with 128-row
-// tiles, 2 = mma.sync decode kernel (B200 layout only) with 8-, 16- or 32-row
-// token tiles by the average rows per local group, 3 / 4 / 5 = the same with
-// 8 / 16 / 32-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout).
+// tiles, 2 = mma.sync decode kernel (B200 layout only; 8-row token tiles,
+// measured fastest at every decode group size), 3 / 4 / 5 = the same with 8 /
+// 16 / 32-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout).
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 40 rows, CTA pairs from 128 rows (prefill), else the
+// average at most 16 rows, CTA pairs from 128 rows (prefill), else the
 // single-CTA tcgen05 kernel with 128-row tiles.
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
@@ -1005,19 +1005,19 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   }
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
   if (variant == 0)
-    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 40 ? 2 : avg >= 128 ? 7 : 1;
+    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 7 : 1;
   if (variant >= 2 && variant <= 5)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
                       variant == 3   ? 1
                       : variant == 4 ? 2
                       : variant == 5 ? 4
-                                     : (avg <= 5 ? 1 : avg <= 12 ? 2 : 4),
+                                     : 1,
                       s);
   if (variant == 7)
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
-                           out, s);
+                           out, nullptr, s);
 #define DWM_GMM_LAUNCH(SD, VAR)                                                        \
   return launch<SD, VAR>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset, \
                          num_local_groups, act, act_limit, out_dtype, zero_init, out, s)

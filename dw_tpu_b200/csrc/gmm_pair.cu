@@ -115,6 +115,7 @@ struct Args {
   int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // pair column tiles per group (n / 256)
   int* status;
+  EpHooks hk;   // expert-parallel gating / push (all null for a plain GEMM)
 };
 
 struct Tile {
@@ -398,8 +399,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int rr = c * 16 + e;
             if (rr < t.rows) {
               const uint4 v = lds_u128(epi_s + (uint32_t)(e * row_bytes + j * 16));
-              const int64_t off = ((t.row0 + rr) * (int64_t)a.ldo + ccol) * es + j * 16;
-              *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+              if (a.hk.push_tags != nullptr) {
+                // Expert parallel: straight into the token owner's buffer, at
+                // the row of its (token, k) pair (over NVLink for a peer).
+                const int tag = a.hk.push_tags[t.row0 + rr];
+                if (tag >= 0) {
+                  const int64_t off =
+                      ((int64_t)(tag & ((1 << kEpTagBits) - 1)) * a.ldo + ccol) * es + j * 16;
+                  *reinterpret_cast<uint4*>(a.hk.push_base[tag >> kEpTagBits] + off) = v;
+                }
+              } else {
+                const int64_t off = ((t.row0 + rr) * (int64_t)a.ldo + ccol) * es + j * 16;
+                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+              }
             }
           }
           __syncwarp();
@@ -449,8 +461,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int st = 0;
       uint32_t ph = 0, armed = 0, par = 0;
       bool ok = true;
+      int gated = -1;  // last local expert whose rows were seen to have arrived
       for (int idx = cl; idx < total && ok; idx += ncl) {
         const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        if (a.hk.gate_arrive != nullptr && t.g != gated) {
+          // Expert-parallel gating: every source rank's rows of this expert
+          // have been stored here (and made visible) before TMA reads them.
+          if (!wait_counter_ge(a.hk.gate_arrive + t.g, a.hk.gate_target[t.g], a.hk.wait_ns,
+                               a.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          fence_proxy_async_all();
+          gated = t.g;
+        }
         const int half = tile_n(t.rows) / 2;
         const int nb = half / T_BOX_ROWS;
         const int rbase = t.row0 + (int)rank * half;
@@ -621,6 +645,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // Both CTAs are done with every barrier, shared tile and TMEM column.
   tc_fence_before();
   cluster_sync();
+  if (a.hk.push_tags != nullptr && threadIdx.x == 0) {
+    // Every row this CTA stored precedes (cluster barrier, then an acq_rel
+    // ticket at gpu scope) the last CTA's ticket, which precedes its
+    // system-scope release to every rank: one release covers all CTAs.
+    if (atom_add_acq_rel_gpu(a.hk.ticket, 1u) == gridDim.x - 1) {
+      *a.hk.ticket = 0;
+      for (int p = 0; p < a.hk.world; ++p) red_release_sys_add(a.hk.push_done[p], 1);
+    }
+  }
   if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, TMEM_COLS);
@@ -656,7 +689,8 @@ int max_pairs(cudaLaunchConfig_t cfg) {
 template <int SD>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
-           float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
+           float limit, int out_dtype, int zero_init, void* out, const EpHooks* hooks,
+           cudaStream_t stream) {
   using L = Layout<SD>;
   constexpr int es = ScaleTraits<SD>::bytes;
   const bool act_on = act != DWM_ACT_NONE;
@@ -708,6 +742,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act_on ? n / 2 : n;
   a.n_tiles = n / 256;
   a.status = status_ptr();
+  a.hk = hooks ? *hooks : EpHooks{};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -729,21 +764,22 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
 
 // Entry from the grouped-matmul dispatcher (gmm_fp4.cu): B200-layout weights,
 // n a multiple of 256, k of 64; the caller has validated the arguments.
+// hooks: expert-parallel gating / push (dwm_ep_gmm_fp4), or nullptr.
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
-                    int zero_init, void* out, cudaStream_t stream) {
+                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream) {
   if (scale_dtype == DWM_U8)
     return gmm_pair::launch<DWM_U8>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                     group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                    stream);
+                                    hooks, stream);
   if (scale_dtype == DWM_BF16)
     return gmm_pair::launch<DWM_BF16>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                       group_offset, n_local, act, limit, out_dtype, zero_init,
-                                      out, stream);
+                                      out, hooks, stream);
   return gmm_pair::launch<DWM_F32>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                    group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                   stream);
+                                   hooks, stream);
 }
 
 }  // namespace dwm

@@ -156,6 +156,30 @@ class EPContext:
             L.stream_ptr() if stream is None else stream), "dwm_ep_combine_shared")
         return out
 
+    def gmm(self, lhs: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+            out: torch.Tensor | None, *, mode: int, act: int = L.ACT_NONE,
+            act_limit: float = 0.0, out_dtype: torch.dtype = torch.bfloat16,
+            stream: int | None = None) -> None:
+        """The grouped matmul of the overlapped exchange (dwm_ep_gmm_fp4) on
+        the B200-layout weights of this rank's experts: ``mode`` EP_GEMM_GATED
+        reads the receive buffer (lhs = ``recv``) expert by expert as the rows
+        arrive and writes ``out``; EP_GEMM_PUSH stores every output row into
+        its token owner's buffer (``out`` unused)."""
+        L.require_cuda(lhs, codes, scales)
+        sc = scales.view(torch.uint8) if scales.element_size() == 1 else scales
+        g, n, k2 = codes.shape
+        if g != self.local_experts or lhs.shape[1] != 2 * k2:
+            raise ValueError("codes must be this rank's experts in the B200 layout "
+                             "[E/world, n, k/2] matching lhs")
+        if mode == L.EP_GEMM_GATED and (out is None or out.shape[0] != self.capacity):
+            raise ValueError("the gated matmul writes out [capacity, n or n/2]")
+        odt = out.dtype if out is not None else out_dtype
+        L.check(L.lib().dwm_ep_gmm_fp4(
+            self._ctx, lhs.data_ptr(), codes.view(torch.uint8).data_ptr(), L.FP4_B200,
+            sc.data_ptr(), L.dtype_code(sc.dtype), self.recv_group_sizes.data_ptr(), 2 * k2, n,
+            int(act), float(act_limit), L.dtype_code(odt), L.ptr(out), int(mode),
+            L.stream_ptr() if stream is None else stream), "dwm_ep_gmm_fp4")
+
     def set_wait_limit(self, seconds: float) -> None:
         """Limit of every device-side wait of later launches (default 2 s). A
         wait that runs out reports DWM_DEV_TIMEOUT (``_lib.DeviceError`` on the
@@ -334,12 +358,8 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
     average (the receive buffer's row count is a capacity, not a size)."""
     if layout != "b200":
         return 0
-    if expected_rows <= 5:
-        return 3  # mma.sync kernel, 8-row token tiles
-    if expected_rows <= 12:
-        return 4  # mma.sync kernel, 16-row token tiles
-    if expected_rows <= 40:
-        return 5  # mma.sync kernel, 32-row token tiles
+    if expected_rows <= 16:
+        return 3  # mma.sync kernel, 8-row token tiles (measured fastest up to 16 rows)
     if expected_rows >= 128:
         return 7  # tcgen05 on CTA pairs (prefill)
     return 1      # tcgen05 kernel, one CTA
@@ -356,7 +376,7 @@ class EPMoELayer:
     def __init__(self, weights: FP4MoEWeights, ctx: EPContext, top_k: int, *,
                  scoring_fn: str = "sigmoid", renormalize: bool = True,
                  act_limit: float | None = None, f32_reduce: bool = False,
-                 expected_rows: float | None = None):
+                 expected_rows: float | None = None, overlap: bool = False):
         if weights.num_experts != ctx.local_experts:
             raise ValueError(f"weights hold {weights.num_experts} experts, the context "
                              f"{ctx.local_experts} per rank")
@@ -377,6 +397,13 @@ class EPMoELayer:
         if expected_rows is None:  # uniform routing over all experts
             expected_rows = t * k / ctx.num_experts * ctx.world
         self.variant = gemm_variant(weights.layout, expected_rows)
+        # overlap: the exchange folded into the CTA-pair grouped matmuls
+        # (dwm_ep_gmm_fp4): gmm1 starts on each expert as its rows arrive,
+        # gmm2 stores its rows straight into the token owners' buffers.
+        self.overlap = bool(overlap)
+        if self.overlap and weights.layout != "b200":
+            raise ValueError("the overlapped exchange takes B200-layout weights")
+        self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
 
     kernels_per_forward = 5  # route, dispatch, 2 gmm, combine
 
@@ -394,9 +421,22 @@ class EPMoELayer:
         ops.gmm_fp4_out(self.h1, self.w.w2, self.w.s2, gs, self.y, layout=self.w.layout,
                         variant=self.variant)
 
+    def _experts_overlapped(self) -> None:
+        c = self.ctx
+        c.gmm(c.recv, self.w.w13, self.w.s13, self.h1, mode=L.EP_GEMM_GATED, act=self.act,
+              act_limit=self.act_limit)
+        c.gmm(self.h1, self.w.w2, self.w.s2, None, mode=L.EP_GEMM_PUSH, out_dtype=self.y_dtype)
+
+    _DISPATCH_OVERLAP = L.EP_COUNTS | L.EP_ROWS | L.EP_GATED
+    _COMBINE_OVERLAP = L.EP_REDUCE | L.EP_PUSHED
+
     def forward(self, hidden: torch.Tensor, logits: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         ids, w16 = self._route(logits)
+        if self.overlap:
+            self.ctx.dispatch(hidden, ids, phases=self._DISPATCH_OVERLAP)
+            self._experts_overlapped()
+            return self.ctx.combine(self.y, w16, out, phases=self._COMBINE_OVERLAP)
         self.ctx.dispatch(hidden, ids)
         self._experts()
         return self.ctx.combine(self.y, w16, out)
@@ -409,6 +449,22 @@ class EPMoELayer:
         ``create_local_contexts``): each exchange phase is issued for every
         rank before the next phase."""
         routed = [ly._route(lg) for ly, lg in zip(layers, logits)]
+        if layers[0].overlap:
+            outs = outs or [None] * len(layers)
+            for phase in (L.EP_COUNTS | L.EP_GATED, L.EP_ROWS | L.EP_GATED):
+                for ly, h, (ids, _) in zip(layers, hiddens, routed):
+                    ly.ctx.dispatch(h, ids, phases=phase)
+            for gated in (True, False):  # every rank's gmm1, then every rank's gmm2
+                for ly in layers:
+                    c = ly.ctx
+                    if gated:
+                        c.gmm(c.recv, ly.w.w13, ly.w.s13, ly.h1, mode=L.EP_GEMM_GATED,
+                              act=ly.act, act_limit=ly.act_limit)
+                    else:
+                        c.gmm(ly.h1, ly.w.w2, ly.w.s2, None, mode=L.EP_GEMM_PUSH,
+                              out_dtype=ly.y_dtype)
+            return [ly.ctx.combine(ly.y, r[1], o, phases=EPMoELayer._COMBINE_OVERLAP)
+                    for ly, r, o in zip(layers, routed, outs)]
         emulated_dispatch([ly.ctx for ly in layers], hiddens, [r[0] for r in routed])
         for ly in layers:
             ly._experts()

@@ -100,9 +100,9 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
  * automatic choice for groups averaging 17-127 rows),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
- * groups; 8-, 16- or 32-row token tiles by the average rows per local group),
- * 3 / 4 / 5 = the same with 8 / 16 / 32-row token tiles (2-5: the automatic
- * choice for B200 codes whose groups average at most 40 rows),
+ * groups; 8-row token tiles), 3 / 4 / 5 = the same with 8 / 16 / 32-row
+ * token tiles (2: the automatic choice for B200 codes whose groups average
+ * at most 16 rows),
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
  * double-buffered accumulators (the automatic choice for B200 codes whose
@@ -286,6 +286,10 @@ int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits
 #define DWM_EP_ALL 7
 #define DWM_EP_PUSH 1          /* combine phases: make this rank's outputs readable, */
 #define DWM_EP_REDUCE 2        /* then reduce every own token */
+#define DWM_EP_GATED 8         /* dispatch flag: per-expert arrivals for dwm_ep_gmm_fp4 */
+#define DWM_EP_PUSHED 4        /* combine flag: outputs were pushed by dwm_ep_gmm_fp4 */
+#define DWM_EP_GEMM_GATED 1    /* dwm_ep_gmm_fp4 modes: the up projection, gated, */
+#define DWM_EP_GEMM_PUSH 2     /* the down projection, pushing its rows to the owners */
 
 typedef struct dwm_ep dwm_ep;
 
@@ -332,6 +336,34 @@ int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_wei
 int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                           int w_dtype, const void* shared, int shared_dtype, float routed_scale,
                           int mid_dtype, void* out, int out_dtype, int phases, void* stream);
+/* The overlapped form of the exchange (cfg3 prefill): the grouped matmuls run
+ * on the CTA-pair kernel (dwm_gmm_fp4_variant 7) with the exchange folded in,
+ * instead of the dispatch waiting for every row and the combine pulling every
+ * output after the GEMMs.
+ *   dwm_ep_dispatch(..., DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_GATED): stores
+ *       the rows with their (source rank, pair) tags; each CTA adds the rows it
+ *       stored for each expert to the owner's arrival counter of that expert;
+ *       no wait at the end.
+ *   dwm_ep_gmm_fp4(..., DWM_EP_GEMM_GATED): lhs = the receive buffer
+ *       (dwm_ep_recv_buffer), k = hidden; the tiles of a local expert load its
+ *       rows only once all of them have arrived, so the GEMM starts on the
+ *       experts that are complete while other rows are still in flight
+ *       (out: [capacity, n or n/2], e.g. the SwiGLU activations).
+ *   dwm_ep_gmm_fp4(..., DWM_EP_GEMM_PUSH): act = none, n = hidden; the
+ *       epilogue stores each output row straight into its token owner's
+ *       buffer (over NVLink), at the row of its (token, k) pair; the last CTA
+ *       tells every rank (out is not written).
+ *   dwm_ep_combine(..., DWM_EP_REDUCE | DWM_EP_PUSHED): waits until every
+ *       rank has pushed, then forms the k-order f32 sum from local memory
+ *       (y is not read; y_dtype = the down projection's out_dtype).
+ * Bits are those of the serial exchange with the same kernels. Counterpart
+ * of the reference's fused dispatch-GEMM-combine kernel
+ * (E0901:361-449,690-767) and next-expert prefetch (E0902:48-66). The
+ * recv_group_sizes are the dispatch's; codes in the B200 layout. */
+int dwm_ep_gmm_fp4(dwm_ep* ctx, const void* lhs, const void* codes, int codes_format,
+                   const void* scales, int scale_dtype, const int32_t* recv_group_sizes, int k,
+                   int n, int act, float act_limit, int out_dtype, void* out, int mode,
+                   void* stream);
 /* Limit of every device-side wait of this context's later launches (default
  * 2 s; 1 us .. 60 s). A wait that runs out sets DWM_DEV_TIMEOUT, the kernel
  * drops the step's rows and returns; the contexts of all ranks must then be

@@ -384,3 +384,47 @@ def test_ep_layer_full_size_matches_single_device(ep):
     finally:
         for c in ctxs:
             c.close()
+
+
+@pytest.mark.parametrize("f32_reduce", [False, True])
+def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce):
+    """The overlapped exchange (rows gated per expert into gmm1, gmm2 pushing
+    its rows to the token owners, local combine) gives the serial EP layer's
+    bits, three steps in a row, on 4 emulated ranks with prefill-sized groups
+    (~256 rows per expert: the CTA-pair kernel)."""
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import _lib as L
+    from dw_tpu_b200 import synthetic
+    world, t, e, h, i, k = 4, 128, 16, 512, 256, 8
+    w = synthetic.moe_weights(e, h, i, seed=17, device="cuda")
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 18, "cuda", lo=118,
+                                               hi=121))
+    w = w.to_b200()
+    le = e // world
+    ctx_s = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    ctx_o = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        def shard(r):
+            return dw.FP4MoEWeights(w.w13[r * le:(r + 1) * le], w.s13[r * le:(r + 1) * le],
+                                    w.w2[r * le:(r + 1) * le], w.s2[r * le:(r + 1) * le], "b200")
+        serial = [ep.EPMoELayer(shard(r), ctx_s[r], k, f32_reduce=f32_reduce)
+                  for r in range(world)]
+        over = [ep.EPMoELayer(shard(r), ctx_o[r], k, f32_reduce=f32_reduce, overlap=True)
+                for r in range(world)]
+        assert all(ly.variant == 7 for ly in serial + over)
+        for step in range(3):
+            xs, lgs = [], []
+            for r in range(world):
+                x, router = synthetic.layer_inputs(t, h, e, seed=200 + 10 * step + r)
+                xs.append(x.cuda())
+                lgs.append((x.float() @ router.float()).to(torch.bfloat16).cuda())
+            a = ep.EPMoELayer.forward_emulated(serial, xs, lgs)
+            b = ep.EPMoELayer.forward_emulated(over, xs, lgs)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            for r in range(world):
+                assert torch.equal(a[r].view(torch.int16), b[r].view(torch.int16)), (step, r)
+    finally:
+        for c in ctx_s + ctx_o:
+            c.close()

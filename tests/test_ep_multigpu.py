@@ -1,7 +1,9 @@
 """Expert-parallel exchange across real GPUs: one process per GPU over NCCL
 plumbing, peer buffers mapped with CUDA IPC, dispatch/combine bit-exact
-against the oracle and the EP layer against the single-device layer. Skipped
-with fewer than 2 GPUs."""
+against the oracle, the EP layer against the single-device layer, the
+one-shot exchange against the NCCL all_to_all_single path at cfg2's size,
+and the overlapped layer against the serial one. Skipped with fewer than 2
+GPUs."""
 
 import datetime
 import os
@@ -91,9 +93,56 @@ def _worker(rank, world, port, q):
         rf = rel_fro(bf16_to_np(out), bf16_to_np(ref))
         if not rf < gemm_rel_tol(ii) or L.device_status():
             msgs.append(f"layer rel_fro {rf:.3e}")
+        # cfg2 size (512 tokens per rank, H=4096, top-8 over 256 experts):
+        # the one-shot exchange and the NCCL all_to_all_single path give the
+        # same receive buffer and combine output, bit for bit.
+        ctx3 = ep.create_context(max_tokens=512, hidden=4096, topk=8, num_experts=256)
+        nccl = ep.NcclExchange(256, 4096, 8)
+        ids3, w3 = synthetic.route_ids(512, 256, 8, seed=70 + rank, dist="zipf")
+        ids3 = torch.from_numpy(ids3).cuda()
+        w3 = torch.from_numpy(w3).cuda()
+        x3 = torch.randn((512, 4096), generator=torch.Generator().manual_seed(rank)).to(
+            torch.bfloat16).cuda()
+        recv3, gs3 = ctx3.dispatch(x3, ids3)
+        n3 = int(gs3.sum())
+        y3 = ctx3.output(torch.bfloat16)
+        y3[:n3].copy_(recv3[:n3])
+        o1 = ctx3.combine(y3, w3)
+        r2, g2 = nccl.dispatch(x3, ids3)
+        o2 = nccl.combine(r2, w3)
+        torch.cuda.synchronize()
+        if not (torch.equal(gs3, g2) and torch.equal(recv3[:n3].view(torch.int16),
+                                                     r2.view(torch.int16))
+                and torch.equal(o1.view(torch.int16), o2.view(torch.int16))):
+            msgs.append("one-shot and NCCL all_to_all exchanges differ")
+        # The overlapped exchange (gated gmm1, gmm2 pushing to the owners)
+        # against the serial EP layer, prefill-sized groups, two steps.
+        e4, h4, i4, k4, t4 = 8 * world, 512, 256, 8, 128
+        w4 = synthetic.moe_weights(e4, h4, i4, seed=5, device="cuda")
+        for name in ("s13", "s2"):
+            setattr(w4, name, synthetic.random_e8m0(getattr(w4, name).shape, 6, "cuda",
+                                                    lo=118, hi=121))
+        w4 = w4.to_b200()
+        sl4 = slice(rank * 8, (rank + 1) * 8)
+        lw4 = dw.FP4MoEWeights(w4.w13[sl4], w4.s13[sl4], w4.w2[sl4], w4.s2[sl4], "b200")
+        ctx4 = ep.create_context(max_tokens=t4, hidden=h4, topk=k4, num_experts=e4)
+        ctx5 = ep.create_context(max_tokens=t4, hidden=h4, topk=k4, num_experts=e4)
+        ser = ep.EPMoELayer(lw4, ctx4, k4)
+        ovl = ep.EPMoELayer(lw4, ctx5, k4, overlap=True)
+        for step in range(2):
+            x4, r4 = synthetic.layer_inputs(t4, h4, e4, seed=90 + 10 * step + rank)
+            x4 = x4.cuda()
+            lg4 = (x4.float() @ r4.cuda().float()).to(torch.bfloat16)
+            a4 = ser(x4, lg4)
+            b4 = ovl(x4, lg4)
+            torch.cuda.synchronize()
+            if not torch.equal(a4.view(torch.int16), b4.view(torch.int16)):
+                msgs.append(f"overlapped layer differs from the serial one at step {step}")
+        if L.device_status():
+            msgs.append("device status set")
         dist.barrier()
-        ctx.close()
-        ctx2.close()
+        for c in (ctx, ctx2, ctx3, ctx4, ctx5):
+            c.close()
         q.put((rank, msgs))
     except Exception as ex:  # report, then leave the group
         q.put((rank, msgs + [f"{type(ex).__name__}: {ex}"]))
