@@ -552,8 +552,7 @@ def run_ours(args, rank, world, local_rank):
             res["prefill"] = prefill_gemm(local, dev, args.seed)
             res["prefill_layer"] = prefill_layer_single(local, dev, args.seed)
         else:
-            res["link"] = link_peak(dev, world, rank)
-            res.update(ep_extras(args, local, dev, world, rank, res["link"]["GBps"]))
+            res.update(ep_extras(args, local, dev, world, rank))
     if ctx is not None:
         ctx.close()
     return res
@@ -664,9 +663,11 @@ def prefill_layer_single(weights, dev, seed, iters=10):
 # decode sweep (cfg4)
 # ----------------------------------------------------------------------------
 
-def link_peak(dev, world, rank, mib=256, iters=5):
-    """Per-rank NVLink bandwidth measured here: NCCL send/recv of `mib` MiB to
-    the next rank while receiving as much from the previous one (a ring)."""
+def link_peak(dev, world, rank, ctx, mib=256, iters=5):
+    """Per-rank NVLink bandwidth measured here, each rank sending `mib` MiB to
+    the next rank while receiving as much from the previous one (a ring):
+    with NCCL send/recv, and with one copy-engine copy into the peer's mapped
+    receive buffer (dwm_ep_link_probe). The larger is the link peak."""
     import torch
     import torch.distributed as dist
     n = mib * 2**20
@@ -691,9 +692,26 @@ def link_peak(dev, world, rank, mib=256, iters=5):
         e1.record()
         torch.cuda.synchronize(dev)
         ts.append(e0.elapsed_time(e1))
-    ms = max_over_ranks([statistics.median(ts)], world, dev)[0]
-    return {"GBps": round(n / (ms * 1e-3) / 1e9, 1), "how": f"NCCL send/recv ring, {mib} MiB "
-            "per rank each way, median of 5, max over ranks"}
+    cts = []
+    for i in range(iters + 2):
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = events()
+        e0.record()
+        ctx.link_probe(nxt, n)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 2:
+            cts.append(e0.elapsed_time(e1))
+    dist.barrier()
+    ms, cms = max_over_ranks([statistics.median(ts), statistics.median(cts)], world, dev)
+    nccl_gbps = n / (ms * 1e-3) / 1e9
+    copy_gbps = n / (cms * 1e-3) / 1e9
+    return {"GBps": round(max(nccl_gbps, copy_gbps), 1), "nccl_sendrecv_GBps": round(nccl_gbps, 1),
+            "peer_copy_GBps": round(copy_gbps, 1),
+            "how": f"ring of {mib} MiB per rank each way: NCCL send/recv and a copy-engine copy "
+                   "into the peer's mapped buffer, median of 5, max over ranks; GBps = the "
+                   "larger"}
 
 
 def zipf_logits(ids, dev):
@@ -706,7 +724,7 @@ def zipf_logits(ids, dev):
     return lg.to(torch.bfloat16).to(dev)
 
 
-def ep_extras(args, local, dev, world, rank, link_gbps):
+def ep_extras(args, local, dev, world, rank):
     import torch
     import torch.distributed as dist
     from dw_tpu_b200 import _lib as L
@@ -717,6 +735,8 @@ def ep_extras(args, local, dev, world, rank, link_gbps):
     ctx = ep_mod.create_context(max_tokens=1024, hidden=H, topk=TOPK, num_experts=E)
     nccl = ep_mod.NcclExchange(E, H, TOPK)
     try:
+        out["link"] = link_peak(dev, world, rank, ctx)
+        link_gbps = out["link"]["GBps"]
         # ---- cfg2: the exchange alone, one-shot vs NCCL all_to_all_single ----
         sweep = []
         for t in (16, 128, 512):
@@ -871,7 +891,7 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
                        world, dev)
     peaks = measured_peaks()
     res = {"tokens_per_rank": t, "routing": routing,
-           "variant": 7 if overlap else layer.variant, "overlap": overlap,
+           "variant": layer.variant, "overlap": overlap,
            "tokens_per_s": round(t * world / m[0] * 1e3, 1), "ms_per_step": round(m[0], 4),
            "rows_per_expert_max": int(m[2]), "rows_per_expert_min": int(-m[3])}
     if gmm_ms > 0:

@@ -97,7 +97,8 @@ SIGNATURES = {
     "dwm_ep_combine": ([_P, _P, _I, _P, _I, _P, _I, _I, _P], _I),
     "dwm_ep_combine_shared": ([_P, _P, _I, _P, _I, _P, _I, _F, _I, _P, _I, _I, _P], _I),
     "dwm_ep_set_wait_limit": ([_P, _c.c_uint64], _I),
-    "dwm_ep_gmm_fp4": ([_P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _F, _I, _P, _I, _P], _I),
+    "dwm_ep_link_probe": ([_P, _I, _I64, _P], _I),
+    "dwm_ep_gmm_fp4": ([_P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _F, _I, _P, _I, _I, _P], _I),
     "dwm_ep_destroy": ([_P], _I),
 }
 

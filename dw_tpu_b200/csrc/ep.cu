@@ -754,16 +754,23 @@ int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int 
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream);
+int launch_gmm_single_ep(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+                         const int32_t* group_sizes, int num_groups, int m, int k, int n,
+                         int act, float limit, int out_dtype, void* out, const EpHooks* hooks,
+                         cudaStream_t stream);
 }
 
 extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int codes_format,
                               const void* scales, int scale_dtype,
                               const int32_t* recv_group_sizes, int k, int n, int act,
-                              float act_limit, int out_dtype, void* out, int mode,
+                              float act_limit, int out_dtype, void* out, int mode, int variant,
                               void* stream) {
   int rc = check_ctx(c);
   if (rc) return rc;
   DWM_CHECK_ARG(mode == DWM_EP_GEMM_GATED || mode == DWM_EP_GEMM_PUSH, "mode=%d", mode);
+  DWM_CHECK_ARG(variant == 1 || variant == 7,
+                "the EP grouped matmul runs on the tcgen05 kernels: variant 1 (one CTA) or 7 "
+                "(CTA pairs)");
   DWM_CHECK_ARG(codes_format == DWM_FP4_B200, "the EP grouped matmul takes the B200 layout");
   DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
                 "scale dtype must be u8 (e8m0), bf16 or f32");
@@ -798,9 +805,26 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
     hk.ticket = P.ctl + ep::CTL_GEMM_TICKET;
     dst = c->base + c->L.outb;  // not written: every row goes to its token's owner
   }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (variant == 1)
+    return launch_gmm_single_ep(lhs, codes, scales, scale_dtype, recv_group_sizes,
+                                c->local_experts, (int)c->cap, k, n, act, act_limit, out_dtype,
+                                dst, &hk, s);
   return launch_gmm_pair(lhs, codes, scales, scale_dtype, recv_group_sizes, c->local_experts,
                          (int)c->cap, k, n, 0, c->local_experts, act, act_limit, out_dtype, 0, dst,
-                         &hk, static_cast<cudaStream_t>(stream));
+                         &hk, s);
+}
+
+extern "C" int dwm_ep_link_probe(dwm_ep* c, int peer, int64_t bytes, void* stream) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DWM_CHECK_ARG(peer >= 0 && peer < c->world && peer != c->rank, "peer=%d", peer);
+  const int64_t cap = c->cap * c->hidden * 2;
+  DWM_CHECK_ARG(bytes > 0 && bytes <= cap, "bytes=%lld out of (0, %lld]", (long long)bytes,
+                (long long)cap);
+  return check_cuda(cudaMemcpyAsync(c->peer[peer] + c->L.recv, c->base + c->L.recv, (size_t)bytes,
+                                    cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)),
+                    "ep link probe copy");
 }
 
 extern "C" int dwm_ep_set_wait_limit(dwm_ep* c, uint64_t limit_ns) {

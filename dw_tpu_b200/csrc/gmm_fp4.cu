@@ -153,6 +153,7 @@ struct Args {
   int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // column tiles per group
   int* status;
+  EpHooks hk;   // expert-parallel gating / push (all null for a plain GEMM)
 };
 
 // SMEM slot p of an 8-column group holds column perm8(p) (kMN).
@@ -431,9 +432,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const int r = rb + e;
               if (r < t.rows) {
                 const uint4 v = lds_u128(epi_s + (uint32_t)(e * row_bytes + j * 16));
-                const int64_t off = ((t.row0 + r) * (int64_t)a.ldo + colw + part * BW) * es +
-                                    j * 16;
-                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+                if (a.hk.push_tags != nullptr) {
+                  // Expert parallel: straight into the token owner's buffer,
+                  // at the row of its (token, k) pair (NVLink for a peer).
+                  const int tag = a.hk.push_tags[t.row0 + r];
+                  if (tag >= 0) {
+                    const int64_t off = ((int64_t)(tag & ((1 << kEpTagBits) - 1)) * a.ldo +
+                                         colw + part * BW) * es + j * 16;
+                    *reinterpret_cast<uint4*>(a.hk.push_base[tag >> kEpTagBits] + off) = v;
+                  }
+                } else {
+                  const int64_t off =
+                      ((t.row0 + r) * (int64_t)a.ldo + colw + part * BW) * es + j * 16;
+                  *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + off) = v;
+                }
               }
             }
             __syncwarp();
@@ -500,8 +512,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int ts = 0;
       uint32_t ts_ph = 0, ts_armed = 0, ts_par = 0;
       bool ok = true;
+      int gated = -1;  // last local expert whose rows were seen to have arrived
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         const Tile t = get_tile(idx, row_start, tile_prefix, a);
+        if (a.hk.gate_arrive != nullptr && t.g != gated) {
+          // Expert-parallel gating: every source rank's rows of this expert
+          // have been stored here (and made visible) before TMA reads them.
+          if (!wait_counter_ge(a.hk.gate_arrive + t.g, a.hk.gate_target[t.g], a.hk.wait_ns,
+                               a.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          fence_proxy_async_all();
+          gated = t.g;
+        }
         const int nb = (t.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
         int nbp;
         const int kspan = token_span(nb, nbp, L::T_BOXES);
@@ -750,6 +774,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (a.hk.push_tags != nullptr && threadIdx.x == 0) {
+    // Every row this CTA stored precedes (bar.sync, then an acq_rel ticket
+    // at gpu scope) the last CTA's ticket, which precedes its system-scope
+    // release to every rank: one release covers all CTAs.
+    if (atom_add_acq_rel_gpu(a.hk.ticket, 1u) == gridDim.x - 1) {
+      *a.hk.ticket = 0;
+      for (int p = 0; p < a.hk.world; ++p) red_release_sys_add(a.hk.push_done[p], 1);
+    }
+  }
   if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -903,7 +936,8 @@ __global__ void fp4_codes_convert_kernel(const uint8_t* __restrict__ in, uint8_t
 template <int SD, int VAR>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
-           float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream) {
+           float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream,
+           const EpHooks* hooks = nullptr) {
   using L = Smem<SD>;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
@@ -942,6 +976,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.n_tiles = n / (NSUB * BW);
   a.status = status_ptr();
+  a.hk = hooks ? *hooks : EpHooks{};
   gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
                                                                          tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmm_fp4 launch");
@@ -1037,6 +1072,25 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
 }  // namespace dwm
 
 using namespace dwm;
+
+namespace dwm {
+// The single-CTA tcgen05 kernel on B200-layout codes with expert-parallel
+// hooks (dwm_ep_gmm_fp4); the caller has validated the arguments.
+int launch_gmm_single_ep(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+                         const int32_t* group_sizes, int num_groups, int m, int k, int n,
+                         int act, float limit, int out_dtype, void* out, const EpHooks* hooks,
+                         cudaStream_t stream) {
+  if (scale_dtype == DWM_U8)
+    return gmm::launch<DWM_U8, gmm::kKS>(lhs, codes, scales, group_sizes, num_groups, m, k, n, 0,
+                                         num_groups, act, limit, out_dtype, 0, out, stream, hooks);
+  if (scale_dtype == DWM_BF16)
+    return gmm::launch<DWM_BF16, gmm::kKS>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
+                                           0, num_groups, act, limit, out_dtype, 0, out, stream,
+                                           hooks);
+  return gmm::launch<DWM_F32, gmm::kKS>(lhs, codes, scales, group_sizes, num_groups, m, k, n, 0,
+                                        num_groups, act, limit, out_dtype, 0, out, stream, hooks);
+}
+}  // namespace dwm
 
 extern "C" int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format,
                            const void* scales, int scale_dtype, const int32_t* group_sizes,

@@ -63,6 +63,14 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #ifndef DWM_GMV_STAGES1_K128
 #define DWM_GMV_STAGES1_K128 2
 #endif
+// 1: two-tile (16-row) tasks on k % 128 == 0 also take stages of 128 k, with
+// DWM_GMV_WARPS2_K128 warps per CTA.
+#ifndef DWM_GMV_K128_NT2
+#define DWM_GMV_K128_NT2 0
+#endif
+#ifndef DWM_GMV_WARPS2_K128
+#define DWM_GMV_WARPS2_K128 12
+#endif
 #ifndef DWM_GMV_STAGES2
 #define DWM_GMV_STAGES2 3
 #endif
@@ -128,7 +136,9 @@ struct Cfg {
   static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
   static constexpr int WARPS =
-      NT == 4 ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 8) : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
+      NT == 4                ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 8)
+      : (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
+                               : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
@@ -679,6 +689,12 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
     if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 1);
     if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 1);
     DWM_GMV(DWM_F32, 1);
+  }
+  if (nt == 2 && DWM_GMV_K128_NT2 && k % 128 == 0) {
+    if (scale_dtype == DWM_U8) return gmv::launch_impl<DWM_U8, 2, 128>(lhs, codes, scales, a, stream);
+    if (scale_dtype == DWM_BF16)
+      return gmv::launch_impl<DWM_BF16, 2, 128>(lhs, codes, scales, a, stream);
+    return gmv::launch_impl<DWM_F32, 2, 128>(lhs, codes, scales, a, stream);
   }
   if (nt == 2) {
     if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 2);

@@ -159,12 +159,13 @@ class EPContext:
     def gmm(self, lhs: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
             out: torch.Tensor | None, *, mode: int, act: int = L.ACT_NONE,
             act_limit: float = 0.0, out_dtype: torch.dtype = torch.bfloat16,
-            stream: int | None = None) -> None:
+            variant: int = 7, stream: int | None = None) -> None:
         """The grouped matmul of the overlapped exchange (dwm_ep_gmm_fp4) on
         the B200-layout weights of this rank's experts: ``mode`` EP_GEMM_GATED
         reads the receive buffer (lhs = ``recv``) expert by expert as the rows
         arrive and writes ``out``; EP_GEMM_PUSH stores every output row into
-        its token owner's buffer (``out`` unused)."""
+        its token owner's buffer (``out`` unused). ``variant`` 1 runs the
+        one-CTA tcgen05 kernel, 7 the CTA-pair kernel."""
         L.require_cuda(lhs, codes, scales)
         sc = scales.view(torch.uint8) if scales.element_size() == 1 else scales
         g, n, k2 = codes.shape
@@ -177,8 +178,15 @@ class EPContext:
         L.check(L.lib().dwm_ep_gmm_fp4(
             self._ctx, lhs.data_ptr(), codes.view(torch.uint8).data_ptr(), L.FP4_B200,
             sc.data_ptr(), L.dtype_code(sc.dtype), self.recv_group_sizes.data_ptr(), 2 * k2, n,
-            int(act), float(act_limit), L.dtype_code(odt), L.ptr(out), int(mode),
+            int(act), float(act_limit), L.dtype_code(odt), L.ptr(out), int(mode), int(variant),
             L.stream_ptr() if stream is None else stream), "dwm_ep_gmm_fp4")
+
+    def link_probe(self, peer: int, nbytes: int, stream: int | None = None) -> None:
+        """Copy nbytes of this rank's receive buffer into ``peer``'s over
+        NVLink (dwm_ep_link_probe); only between steps, every rank idle."""
+        L.check(L.lib().dwm_ep_link_probe(self._ctx, int(peer), int(nbytes),
+                                          L.stream_ptr() if stream is None else stream),
+                "dwm_ep_link_probe")
 
     def set_wait_limit(self, seconds: float) -> None:
         """Limit of every device-side wait of later launches (default 2 s). A
@@ -403,6 +411,8 @@ class EPMoELayer:
         self.overlap = bool(overlap)
         if self.overlap and weights.layout != "b200":
             raise ValueError("the overlapped exchange takes B200-layout weights")
+        if self.overlap:  # the tcgen05 kernels carry the exchange hooks
+            self.variant = 7 if expected_rows >= 128 else 1
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
 
     kernels_per_forward = 5  # route, dispatch, 2 gmm, combine
@@ -424,8 +434,9 @@ class EPMoELayer:
     def _experts_overlapped(self) -> None:
         c = self.ctx
         c.gmm(c.recv, self.w.w13, self.w.s13, self.h1, mode=L.EP_GEMM_GATED, act=self.act,
-              act_limit=self.act_limit)
-        c.gmm(self.h1, self.w.w2, self.w.s2, None, mode=L.EP_GEMM_PUSH, out_dtype=self.y_dtype)
+              act_limit=self.act_limit, variant=self.variant)
+        c.gmm(self.h1, self.w.w2, self.w.s2, None, mode=L.EP_GEMM_PUSH, out_dtype=self.y_dtype,
+              variant=self.variant)
 
     _DISPATCH_OVERLAP = L.EP_COUNTS | L.EP_ROWS | L.EP_GATED
     _COMBINE_OVERLAP = L.EP_REDUCE | L.EP_PUSHED
@@ -459,10 +470,10 @@ class EPMoELayer:
                     c = ly.ctx
                     if gated:
                         c.gmm(c.recv, ly.w.w13, ly.w.s13, ly.h1, mode=L.EP_GEMM_GATED,
-                              act=ly.act, act_limit=ly.act_limit)
+                              act=ly.act, act_limit=ly.act_limit, variant=ly.variant)
                     else:
                         c.gmm(ly.h1, ly.w.w2, ly.w.s2, None, mode=L.EP_GEMM_PUSH,
-                              out_dtype=ly.y_dtype)
+                              out_dtype=ly.y_dtype, variant=ly.variant)
             return [ly.ctx.combine(ly.y, r[1], o, phases=EPMoELayer._COMBINE_OVERLAP)
                     for ly, r, o in zip(layers, routed, outs)]
         emulated_dispatch([ly.ctx for ly in layers], hiddens, [r[0] for r in routed])

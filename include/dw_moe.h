@@ -336,8 +336,9 @@ int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_wei
 int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                           int w_dtype, const void* shared, int shared_dtype, float routed_scale,
                           int mid_dtype, void* out, int out_dtype, int phases, void* stream);
-/* The overlapped form of the exchange (cfg3 prefill): the grouped matmuls run
- * on the CTA-pair kernel (dwm_gmm_fp4_variant 7) with the exchange folded in,
+/* The overlapped form of the exchange (prefill): the grouped matmuls run on a
+ * tcgen05 kernel (`variant` 1, one CTA, or 7, CTA pairs, as in
+ * dwm_gmm_fp4_variant) with the exchange folded in,
  * instead of the dispatch waiting for every row and the combine pulling every
  * output after the GEMMs.
  *   dwm_ep_dispatch(..., DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_GATED): stores
@@ -363,7 +364,12 @@ int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* t
 int dwm_ep_gmm_fp4(dwm_ep* ctx, const void* lhs, const void* codes, int codes_format,
                    const void* scales, int scale_dtype, const int32_t* recv_group_sizes, int k,
                    int n, int act, float act_limit, int out_dtype, void* out, int mode,
-                   void* stream);
+                   int variant, void* stream);
+/* Link measurement: copies `bytes` of this rank's receive buffer into rank
+ * `peer`'s receive buffer over NVLink (one copy-engine copy on `stream`).
+ * It overwrites the peer's receive rows: call it only between steps, with
+ * every rank idle. No counterpart in the reference. */
+int dwm_ep_link_probe(dwm_ep* ctx, int peer, int64_t bytes, void* stream);
 /* Limit of every device-side wait of this context's later launches (default
  * 2 s; 1 us .. 60 s). A wait that runs out sets DWM_DEV_TIMEOUT, the kernel
  * drops the step's rows and returns; the contexts of all ranks must then be

@@ -386,16 +386,17 @@ def test_ep_layer_full_size_matches_single_device(ep):
             c.close()
 
 
-@pytest.mark.parametrize("f32_reduce", [False, True])
-def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce):
+@pytest.mark.parametrize("f32_reduce,t,variant", [(False, 128, 7), (True, 128, 7),
+                                                  (False, 32, 1)])
+def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce, t, variant):
     """The overlapped exchange (rows gated per expert into gmm1, gmm2 pushing
     its rows to the token owners, local combine) gives the serial EP layer's
     bits, three steps in a row, on 4 emulated ranks with prefill-sized groups
-    (~256 rows per expert: the CTA-pair kernel)."""
+    (~256 rows per expert: the CTA-pair kernel; ~64: the one-CTA kernel)."""
     import dw_tpu_b200 as dw
     from dw_tpu_b200 import _lib as L
     from dw_tpu_b200 import synthetic
-    world, t, e, h, i, k = 4, 128, 16, 512, 256, 8
+    world, e, h, i, k = 4, 16, 512, 256, 8
     w = synthetic.moe_weights(e, h, i, seed=17, device="cuda")
     for name in ("s13", "s2"):
         setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 18, "cuda", lo=118,
@@ -412,7 +413,7 @@ def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce):
                   for r in range(world)]
         over = [ep.EPMoELayer(shard(r), ctx_o[r], k, f32_reduce=f32_reduce, overlap=True)
                 for r in range(world)]
-        assert all(ly.variant == 7 for ly in serial + over)
+        assert all(ly.variant == variant for ly in serial + over)
         for step in range(3):
             xs, lgs = [], []
             for r in range(world):
