@@ -1020,9 +1020,10 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 }
 
 // variant: 0 = choose, 1 = tcgen05 (shared-memory decode) with 128-row
-// tiles, 2 = mma.sync decode kernel (B200 layout only; 8-row token tiles,
-// measured fastest at every decode group size), 3 / 4 / 5 = the same with 8 /
-// 16 / 32-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200 layout).
+// tiles, 2 = mma.sync decode kernel (B200 layout only) with 8-row token tiles
+// up to 6 rows per local group on average and 16-row tiles above, 3 / 4 = the
+// same with 8 / 16-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200
+// layout).
 // The automatic choice for the B200 layout: mma.sync when the local groups
 // average at most 16 rows, CTA pairs from 128 rows (prefill), else the
 // single-CTA tcgen05 kernel with 128-row tiles.
@@ -1041,14 +1042,10 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
   if (variant == 0)
     variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 7 : 1;
-  if (variant >= 2 && variant <= 5)
+  if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
-                      variant == 3   ? 1
-                      : variant == 4 ? 2
-                      : variant == 5 ? 4
-                                     : 1,
-                      s);
+                      variant == 3 ? 1 : variant == 4 ? 2 : (avg <= 6 ? 1 : 2), s);
   if (variant == 7)
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
@@ -1111,11 +1108,11 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 7 && variant != 6,
-                "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-5 (mma.sync decode "
+  DWM_CHECK_ARG(variant >= 0 && variant <= 7 && variant != 5 && variant != 6,
+                "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-4 (mma.sync decode "
                 "kernel) or 7 (tcgen05 on CTA pairs)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
-                "variants 1-5 and 7 need the B200 layout");
+                "variants 1-4 and 7 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

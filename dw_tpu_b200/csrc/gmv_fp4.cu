@@ -64,24 +64,16 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #define DWM_GMV_STAGES1_K128 2
 #endif
 // 1: two-tile (16-row) tasks on k % 128 == 0 also take stages of 128 k, with
-// DWM_GMV_WARPS2_K128 warps per CTA.
+// DWM_GMV_WARPS2_K128 warps per CTA (measured 17% faster than 64-k stages at
+// 32 experts x 512 rows, the per-rank shape of 8 GPUs).
 #ifndef DWM_GMV_K128_NT2
-#define DWM_GMV_K128_NT2 0
+#define DWM_GMV_K128_NT2 1
 #endif
 #ifndef DWM_GMV_WARPS2_K128
 #define DWM_GMV_WARPS2_K128 12
 #endif
 #ifndef DWM_GMV_STAGES2
 #define DWM_GMV_STAGES2 3
-#endif
-// Ring depth and warps per CTA for four n8 token tiles (32-row tasks): the
-// accumulators of 32 rows need about 170 registers a thread, and a stage
-// holds 32 token rows, so fewer, wider warps.
-#ifndef DWM_GMV_STAGES4
-#define DWM_GMV_STAGES4 3
-#endif
-#ifndef DWM_GMV_WARPS4
-#define DWM_GMV_WARPS4 8
 #endif
 // Warps per CTA (E8M0 / bf16 scales; f32 scales take 12).
 #ifndef DWM_GMV_WARPS1
@@ -124,8 +116,7 @@ struct Cfg {
   static constexpr int DELTA = (SD == DWM_U8 && !POST) ? kDelta : 0;  // weight-side bias
   static constexpr int es = ScaleTraits<SD>::bytes;
   static constexpr int S =
-      KS == 128 ? DWM_GMV_STAGES1_K128
-                : (NT == 1 ? DWM_GMV_STAGES1 : NT == 2 ? DWM_GMV_STAGES2 : DWM_GMV_STAGES4);
+      KS == 128 ? DWM_GMV_STAGES1_K128 : (NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2);
   static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
   // Largest E8M0 code of the post-MMA path: the k-block factor
   // 2^(c-1-kTokExp) (raw decode) or 2^(c-127) (normalised) must be a finite f32.
@@ -135,10 +126,8 @@ struct Cfg {
   static constexpr int SC_ROW = 64 * es;
   static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
-  static constexpr int WARPS =
-      NT == 4                ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 8)
-      : (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
-                               : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
+  static constexpr int WARPS = (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
+                                                     : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
@@ -655,9 +644,8 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
 
 // Decode-regime grouped GEMM on the B200 layout (called by the dwm_gmm_fp4
 // dispatcher after argument validation: k % 64 == 0, n % 256 == 0, 16-byte
-// aligned pointers). nt: 1, 2 or 4 n8 token tiles per task (8, 16 or 32 token
-// rows: every weight is decoded once per task, so a group's rows should fit
-// as few tasks as possible).
+// aligned pointers). nt: 1 or 2 n8 token tiles per task (8 or 16 token rows;
+// every weight is decoded once per task).
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
@@ -696,14 +684,9 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
       return gmv::launch_impl<DWM_BF16, 2, 128>(lhs, codes, scales, a, stream);
     return gmv::launch_impl<DWM_F32, 2, 128>(lhs, codes, scales, a, stream);
   }
-  if (nt == 2) {
-    if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 2);
-    if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 2);
-    DWM_GMV(DWM_F32, 2);
-  }
-  if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 4);
-  if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 4);
-  DWM_GMV(DWM_F32, 4);
+  if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 2);
+  if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 2);
+  DWM_GMV(DWM_F32, 2);
 #undef DWM_GMV
 }
 

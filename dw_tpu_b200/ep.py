@@ -366,8 +366,10 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
     average (the receive buffer's row count is a capacity, not a size)."""
     if layout != "b200":
         return 0
+    if expected_rows <= 6:
+        return 3  # mma.sync kernel, 8-row token tiles
     if expected_rows <= 16:
-        return 3  # mma.sync kernel, 8-row token tiles (measured fastest up to 16 rows)
+        return 4  # mma.sync kernel, 16-row token tiles (one task per expert)
     if expected_rows >= 128:
         return 7  # tcgen05 on CTA pairs (prefill)
     return 1      # tcgen05 kernel, one CTA

@@ -100,14 +100,14 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
  * automatic choice for groups averaging 17-127 rows),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
- * groups; 8-row token tiles), 3 / 4 / 5 = the same with 8 / 16 / 32-row
- * token tiles (2: the automatic choice for B200 codes whose groups average
- * at most 16 rows),
+ * groups; 8-row token tiles up to 6 rows per group on average, 16-row tiles
+ * above), 3 / 4 = the same with 8 / 16-row token tiles (2: the automatic
+ * choice for B200 codes whose groups average at most 16 rows),
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
  * double-buffered accumulators (the automatic choice for B200 codes whose
- * groups average 128 rows or more). 1-5 and 7 need DWM_FP4_B200 codes;
- * 6 is not assigned. Every variant decodes the same bf16 weights and
+ * groups average 128 rows or more). 1-4 and 7 need DWM_FP4_B200 codes;
+ * 5 and 6 are not assigned. Every variant decodes the same bf16 weights and
  * accumulates in f32; results differ between variants only by f32 summation
  * order (1 and 7 give identical bits). Same reference interface as
  * dwm_gmm_fp4 (TK:107-153). */

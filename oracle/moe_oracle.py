@@ -401,7 +401,11 @@ def dequantize_fp4_block32(nib: np.ndarray, scale: np.ndarray) -> np.ndarray:
 
 def apply_scoring_fn(scoring_fn: str, logits: np.ndarray) -> np.ndarray:
     """Scores in f32 from f32-widened logits: softmax / sigmoid /
-    sqrtsoftplus (upstream apply_scoring_fn, used at E0901:668)."""
+    sqrtsoftplus (upstream apply_scoring_fn, used at E0901:668).
+
+    Assumption: upstream apply_scoring_fn lives in the tpu-inference
+    submodule, which the reference does not vendor, so its compute dtype is
+    not visible. This restatement (and the CUDA routing) scores in f32."""
     x = np.asarray(logits, dtype=np.float32)
     if scoring_fn == "softmax":
         m = x.max(axis=-1, keepdims=True)

@@ -67,8 +67,8 @@ def test_gemm_variant_choice():
     from dw_tpu_b200.ep import gemm_variant
     assert gemm_variant("e2m1", 4) == 0
     assert gemm_variant("b200", 2) == 3
-    assert gemm_variant("b200", 8) == 3
-    assert gemm_variant("b200", 16) == 3
+    assert gemm_variant("b200", 8) == 4
+    assert gemm_variant("b200", 16) == 4
     assert gemm_variant("b200", 64) == 1
     assert gemm_variant("b200", 256) == 7
 
