@@ -49,6 +49,7 @@ EP_PUSH = 1
 EP_REDUCE = 2
 EP_GATED = 8
 EP_PUSHED = 4
+EP_RANK_ORDER = 16
 EP_GEMM_GATED = 1
 EP_GEMM_PUSH = 2
 

@@ -376,7 +376,7 @@ __global__ void ep_stage_kernel(const __grid_constant__ Params P, const uint4* _
 // 8 consecutive elements of one token and keeps up to KB of its rows' loads in
 // flight: the rows on this rank are loaded before the wait for the peers'
 // announcements, the peers' rows after it.
-template <int XD, int WD, int OD>
+template <int XD, int WD, int OD, bool RANK_ORDER>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     ep_combine_kernel(const __grid_constant__ Params P, const void* __restrict__ w,
                       void* __restrict__ out, const moe::SharedAdd sa, int ph, int* status) {
@@ -445,15 +445,55 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
 #pragma unroll
       for (int q = 0; q < KB; ++q)
         if (code[q] >= 0 && !pushed && (code[q] >> ROW_BITS) != P.rank) load(q);
+      if constexpr (RANK_ORDER) {
+        // The reference's GMM_EP numerics (X0107:15-29 then KO:181-184):
+        // rank r's masked f32 partial over the k slots of its experts, in k
+        // order from +0.0 (a masked slot adds +0.0), then the partials summed
+        // in rank order 0..world-1. All k rows are in v (top_k <= KB).
+        float prod[KB][8];
 #pragma unroll
-      for (int q = 0; q < KB; ++q)
-        if (code[q] >= 0) {
-          const float wk = moe::load_weight<WD>(w, t * P.topk + k0 + q);
-          if constexpr (XD == DWM_BF16)
-            moe::mul_add8_bf16raw(acc, v[q], wk);
-          else
-            moe::mul_add8(acc, v[q], wk);
+        for (int q = 0; q < KB; ++q) {
+          const float wk = code[q] >= 0 ? moe::load_weight<WD>(w, t * P.topk + q) : 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float y;
+            if constexpr (XD == DWM_BF16) {
+              const uint32_t u = (e >> 1) == 0   ? v[q].x
+                                 : (e >> 1) == 1 ? v[q].y
+                                 : (e >> 1) == 2 ? v[q].z
+                                                 : v[q].w;
+              y = __uint_as_float((e & 1) ? (u & 0xFFFF0000u) : (u << 16));
+            } else {
+              y = v[q][e];
+            }
+            prod[q][e] = code[q] >= 0 ? __fmul_rn(y, wk) : 0.0f;
+          }
         }
+        for (int r = 0; r < P.world; ++r) {
+          float part[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) part[e] = 0.0f;
+#pragma unroll
+          for (int q = 0; q < KB; ++q) {
+            if (q >= P.topk) break;  // the reference's partial runs over the k slots only
+            const bool own = code[q] >= 0 && (code[q] >> ROW_BITS) == r;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part[e] = __fadd_rn(part[e], own ? prod[q][e] : 0.0f);
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = r == 0 ? part[e] : __fadd_rn(acc[e], part[e]);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < KB; ++q)
+          if (code[q] >= 0) {
+            const float wk = moe::load_weight<WD>(w, t * P.topk + k0 + q);
+            if constexpr (XD == DWM_BF16)
+              moe::mul_add8_bf16raw(acc, v[q], wk);
+            else
+              moe::mul_add8(acc, v[q], wk);
+          }
+      }
     }
     if (mine && s_ok) {
       moe::shared_add8(acc, sa, t * P.H + (int64_t)c * 8);
@@ -687,9 +727,14 @@ extern "C" int dwm_ep_combine_shared(dwm_ep* c, const void* y, int y_dtype,
                                      void* out, int out_dtype, int phases, void* stream) {
   int rc = check_ctx(c);
   if (rc) return rc;
-  DWM_CHECK_ARG(phases >= 1 && phases <= (DWM_EP_PUSH | DWM_EP_REDUCE | DWM_EP_PUSHED) &&
-                    phases != DWM_EP_PUSHED,
+  DWM_CHECK_ARG(phases >= 1 &&
+                    phases <= (DWM_EP_PUSH | DWM_EP_REDUCE | DWM_EP_PUSHED | DWM_EP_RANK_ORDER) &&
+                    (phases & (DWM_EP_PUSH | DWM_EP_REDUCE)) != 0,
                 "phases=%d", phases);
+  DWM_CHECK_ARG(!(phases & DWM_EP_RANK_ORDER) || (c->topk <= 8 && !(phases & DWM_EP_PUSHED) &&
+                                                  shared == nullptr),
+                "the rank-order combine takes top_k <= 8, the pulled exchange and no shared "
+                "expert");
   DWM_CHECK_ARG(!(phases & DWM_EP_PUSHED) || !(phases & DWM_EP_PUSH),
                 "PUSH (announce) has no part in the pushed mode");
   DWM_CHECK_ARG(c->dispatched, "combine before any dispatch");
@@ -725,10 +770,15 @@ extern "C" int dwm_ep_combine_shared(dwm_ep* c, const void* y, int y_dtype,
       reduce && threads > 0 ? (unsigned)((threads + ep::COMBINE_THREADS - 1) / ep::COMBINE_THREADS)
                             : 1;
   int* st = status_ptr();
+  const bool ro = phases & DWM_EP_RANK_ORDER;
 #define DWM_EP_COMBINE_CASE(XD, WD, OD)                                                        \
   if (y_dtype == XD && w_dtype == WD && out_dtype == OD) {                                     \
-    ep::ep_combine_kernel<XD, WD, OD><<<grid, ep::COMBINE_THREADS, 0, s>>>(P, topk_weights,    \
-                                                                           out, sa, phases, st); \
+    if (ro)                                                                                    \
+      ep::ep_combine_kernel<XD, WD, OD, true>                                                  \
+          <<<grid, ep::COMBINE_THREADS, 0, s>>>(P, topk_weights, out, sa, phases, st);         \
+    else                                                                                       \
+      ep::ep_combine_kernel<XD, WD, OD, false>                                                 \
+          <<<grid, ep::COMBINE_THREADS, 0, s>>>(P, topk_weights, out, sa, phases, st);         \
     return check_cuda(cudaGetLastError(), "ep combine launch");                                \
   }
   DWM_EP_COMBINE_CASE(DWM_BF16, DWM_BF16, DWM_BF16)

@@ -127,12 +127,18 @@ class EPContext:
     def combine(self, y: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None, *, phases: int = L.EP_PUSH | L.EP_REDUCE,
                 stream: int | None = None, shared: torch.Tensor | None = None,
-                routed_scale: float = 1.0, f32_reduce: bool = False) -> torch.Tensor | None:
+                routed_scale: float = 1.0, f32_reduce: bool = False,
+                rank_order: bool = False) -> torch.Tensor | None:
         """y [rows, H] expert outputs in receive order (bf16 or f32; best the
         ``output()`` view, else they are copied there first), topk_weights
         [T, topk] of this rank's dispatched tokens -> out [T, H] (bf16 unless
         ``out`` says otherwise). ``shared`` [T, H] (bf16/f32): the shared
-        expert summed in as ``combine_shared`` does (X0104:80-87)."""
+        expert summed in as ``combine_shared`` does (X0104:80-87).
+        ``rank_order``: the reference GMM_EP sum order (per-rank masked f32
+        partials, summed over ranks in rank order; X0107:15-29, KO:181-184)
+        instead of the k order."""
+        if rank_order:
+            phases |= L.EP_RANK_ORDER
         L.require_cuda(y, topk_weights)
         if y.dim() != 2 or y.shape[1] != self.hidden or not y.is_contiguous():
             raise ValueError(f"y must be a contiguous [rows, {self.hidden}] tensor")

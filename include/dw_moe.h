@@ -288,6 +288,7 @@ int dwm_moe_layer_fp4_noalloc(const void* hidden, const void* logits, int logits
 #define DWM_EP_REDUCE 2        /* then reduce every own token */
 #define DWM_EP_GATED 8         /* dispatch flag: per-expert arrivals for dwm_ep_gmm_fp4 */
 #define DWM_EP_PUSHED 4        /* combine flag: outputs were pushed by dwm_ep_gmm_fp4 */
+#define DWM_EP_RANK_ORDER 16   /* combine flag: the reference GMM_EP sum order (below) */
 #define DWM_EP_GEMM_GATED 1    /* dwm_ep_gmm_fp4 modes: the up projection, gated, */
 #define DWM_EP_GEMM_PUSH 2     /* the down projection, pushing its rows to the owners */
 
@@ -327,7 +328,11 @@ int dwm_ep_dispatch(dwm_ep* ctx, const void* hidden, const int32_t* topk_ids, in
  * buffer) -> out [num_tokens, hidden] of out_dtype, with topk_weights
  * [num_tokens, topk] (bf16 or f32) of the dispatch's tokens. Counterpart of
  * the masked combine + reduce_scatter_local (X0107:15-29, KO:167-185) with
- * the k-order contract of fast_combine (KC:14-21). */
+ * the k-order contract of fast_combine (KC:14-21). With DWM_EP_RANK_ORDER
+ * (top_k <= 8) the sum instead follows the reference's GMM_EP order: for each
+ * rank r, an f32 partial over the k slots whose expert rank r owns (k order,
+ * from +0.0, a slot of another rank adding +0.0), and the partials summed in
+ * f32 in rank order 0..world-1 (X0107:15-29, KO:181-184), rounded once. */
 int dwm_ep_combine(dwm_ep* ctx, const void* y, int y_dtype, const void* topk_weights,
                    int w_dtype, void* out, int out_dtype, int phases, void* stream);
 /* dwm_ep_combine with the shared expert summed into each own token's sum

@@ -266,6 +266,41 @@ def test_ep_combine_with_shared_expert(ep):
             c.close()
 
 
+@pytest.mark.parametrize("world,t,k,ydt", [(4, [24, 3, 17, 0], 8, "bf16"),
+                                           (8, [9, 16, 1, 30, 5, 12, 0, 7], 6, "f32")])
+def test_ep_rank_order_combine_bit_exact(ep, world, t, k, ydt):
+    """The reference GMM_EP numerics as a combine mode: each rank's masked f32
+    partial over the k slots of its experts, summed over ranks in rank order
+    (X0107:15-29, KO:181-184), bit-exact against oracle.ep_combine_rankorder."""
+    from dw_tpu_b200 import _lib as L
+    e, h = 32, 256
+    hid, ids, w = _inputs(world, t, e, k, h, seed=81 + world, dist="zipf")
+    ctxs = ep.create_local_contexts(world, max_tokens=max(t), hidden=h, topk=k, num_experts=e)
+    try:
+        ep.emulated_dispatch(ctxs, [np_to_bf16(x) for x in hid],
+                             [torch.from_numpy(i).cuda() for i in ids])
+        ref = O.ep_dispatch(hid, ids, e)
+        ys = []
+        for r in range(world):
+            n = int(ref[r][1].sum())
+            y = np.random.default_rng(90 + r).standard_normal((max(n, 1), h)).astype(np.float32)
+            ys.append(O.round_bf16(y) if ydt == "bf16" else y)
+        yt = [np_to_bf16(y) if ydt == "bf16" else torch.from_numpy(y).cuda() for y in ys]
+        for c, y in zip(ctxs, yt):
+            c.combine(y, torch.zeros((c.num_tokens, k), device="cuda"), phases=L.EP_PUSH)
+        outs = [c.combine(y, torch.from_numpy(ww).cuda(), phases=L.EP_REDUCE, rank_order=True)
+                for c, y, ww in zip(ctxs, yt, w)]
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        want = O.ep_combine_rankorder([y[:int(g[1].sum())] for y, g in zip(ys, ref)],
+                                      [g[2] for g in ref], w, e, ids)
+        for r in range(world):
+            assert np.array_equal(bf16_to_np(outs[r]), want[r]), r
+    finally:
+        for c in ctxs:
+            c.close()
+
+
 def test_ep_invalid_ids_reported_and_dropped(ep):
     world, e, k, h = 2, 16, 2, 64
     ctxs = ep.create_local_contexts(world, max_tokens=8, hidden=h, topk=k, num_experts=e)
