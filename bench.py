@@ -585,7 +585,8 @@ def prefill_gemm(weights, dev, seed, iters=10):
     out = {"workload": "cfg3 rank at n=8: 32 experts, 8192 rows, H=4096, I=2048",
            "bound": "tensor", "peak": peak, "unit": "TFLOP/s",
            "peak_source": "measured burst" if peaks else "fallback",
-           "kernel": "dw_moe gmm_fp4 (automatic choice: tcgen05 on CTA pairs)"}
+           "kernel": "dw_moe gmm_fp4 (automatic choice, variant 8: tcgen05 on CTA pairs, "
+                     "short group remainders on the mma.sync kernel)"}
     for kind in ("uniform", "multinomial"):
         if kind == "uniform":
             gs_np = np.full(e, rows // e, np.int32)
@@ -611,6 +612,25 @@ def prefill_gemm(weights, dev, seed, iters=10):
             tf = flops / statistics.median(ts) / 1e9
             out[f"{kind}_{name}_tflops"] = round(tf, 1)
             out[f"{kind}_{name}_frac"] = round(tf / peak, 4)
+        if kind == "multinomial":  # the pair kernel alone (variant 7), equal-size tiles
+            for name, fn, flops in (
+                    ("gmm1", lambda: ops.gmm_fp4_out(x, w.w13, w.s13, gs, h1, act=L.ACT_SWIGLU,
+                                                     layout=w.layout, variant=7),
+                     2.0 * rows * H * 2 * I),
+                    ("gmm2", lambda: ops.gmm_fp4_out(h1, w.w2, w.s2, gs, y, layout=w.layout,
+                                                     variant=7), 2.0 * rows * I * H)):
+                fn()
+                torch.cuda.synchronize(dev)
+                ts = []
+                for _ in range(iters):
+                    e0, e1 = events()
+                    e0.record()
+                    fn()
+                    e1.record()
+                    torch.cuda.synchronize(dev)
+                    ts.append(e0.elapsed_time(e1))
+                out[f"multinomial_pair_only_{name}_tflops"] = round(
+                    flops / statistics.median(ts) / 1e9, 1)
     L.raise_on_device_error()
     return out
 
@@ -827,13 +847,17 @@ def ep_extras(args, local, dev, world, rank):
                                     link_gbps)
         over, o_o = ep_layer_case(ctx, local, dev, world, rank, 1024, "router", args.seed,
                                   link_gbps, compact=True, overlap=True)
+        if over["variant"] != serial["variant"]:  # the bits check on the same GEMM kernel
+            _, o_s = ep_layer_case(ctx, local, dev, world, rank, 1024, "router", args.seed,
+                                   link_gbps, compact=True, iters=1,
+                                   gemm_variant=over["variant"])
         differ = max_over_ranks([0.0 if torch.equal(o_s.view(torch.int16),
                                                     o_o.view(torch.int16)) else 1.0],
                                 world, dev)[0]
         out["prefill_layer"] = {
             "workload": serial.pop("workload"), "serial": serial, "overlapped": over,
             "overlap_speedup": round(serial["ms_per_step"] / over["ms_per_step"], 3),
-            "overlapped_bitwise_equal_serial": differ == 0.0}
+            "overlapped_bitwise_equal_serial_same_kernel": differ == 0.0}
         # ---- cfg4: the decode sweep on 8 GPUs, Zipf(1.2) ----
         if world == 8:
             cases = [ep_layer_case(ctx, local, dev, world, rank, t, "zipf", args.seed,
@@ -847,7 +871,7 @@ def ep_extras(args, local, dev, world, rank):
 
 
 def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, compact=False,
-                  iters=10, overlap=False):
+                  iters=10, overlap=False, gemm_variant=None):
     """The EP layer on t tokens per rank: routing from a random router
     ("router", near-uniform) or Zipf(1.2)-skewed ids; median step time (max
     over ranks) and, for the serial layer, the GEMM's time and rate. With
@@ -866,7 +890,8 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
         ids_np, _ = synthetic.route_ids(t, E, TOPK, seed=2000 + 7 * t + rank, dist="zipf")
         logits = zipf_logits(ids_np, dev)
     expected = t * TOPK / E * world
-    layer = ep_mod.EPMoELayer(local, ctx, TOPK, expected_rows=expected, overlap=overlap)
+    layer = ep_mod.EPMoELayer(local, ctx, TOPK, expected_rows=expected, overlap=overlap,
+                              gemm_variant=gemm_variant)
     out = torch.empty((t, H), dtype=torch.bfloat16, device=dev)
     for _ in range(3):
         layer(x, logits, out=out)

@@ -36,15 +36,21 @@ namespace dwm {
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream);
+               cudaStream_t stream, int tail_min = 0);
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
-                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream);
+                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
+                    int tail_min);
 
 namespace gmm {
 
 using namespace fp4;
+
+// Variant 8: a group's last tile goes to the CTA-pair kernel only with at
+// least this many rows (a whole tile's decode costs about as much as the
+// decode kernel's six 16-row weight streams).
+constexpr int kPairTailMin = 96;
 
 enum Variant { kMN = 0, kKS = 1 };
 
@@ -1023,9 +1029,10 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // tiles, 2 = mma.sync decode kernel (B200 layout only) with 8-row token tiles
 // up to 6 rows per local group on average and 16-row tiles above, 3 / 4 = the
 // same with 8 / 16-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200
-// layout).
+// layout), 8 = 7 for each group's 256-row tiles and a remainder of at least
+// kPairTailMin rows, the decode kernel for shorter remainders.
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 16 rows, CTA pairs from 128 rows (prefill), else the
+// average at most 16 rows, variant 8 from 128 rows (prefill), else the
 // single-CTA tcgen05 kernel with 128-row tiles.
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
@@ -1041,7 +1048,7 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   }
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
   if (variant == 0)
-    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 7 : 1;
+    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 8 : 1;
   if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
@@ -1049,7 +1056,20 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   if (variant == 7)
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
-                           out, nullptr, s);
+                           out, nullptr, s, 0);
+  if (variant == 8) {
+    // Full 256-row tiles (and remainders of kPairTailMin rows or more) on CTA
+    // pairs, shorter remainders on the decode kernel: a remainder of r rows
+    // costs the pair kernel a whole tile's decode, the decode kernel one
+    // weight stream per 16 rows.
+    int rc = launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                             group_offset, num_local_groups, act, act_limit, out_dtype,
+                             zero_init, out, nullptr, s, kPairTailMin);
+    if (rc) return rc;
+    return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                      group_offset, num_local_groups, act, act_limit, out_dtype, 0, out, 2, s,
+                      kPairTailMin);
+  }
 #define DWM_GMM_LAUNCH(SD, VAR)                                                        \
   return launch<SD, VAR>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset, \
                          num_local_groups, act, act_limit, out_dtype, zero_init, out, s)
@@ -1108,11 +1128,11 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 7 && variant != 5 && variant != 6,
+  DWM_CHECK_ARG(variant >= 0 && variant <= 8 && variant != 5 && variant != 6,
                 "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-4 (mma.sync decode "
-                "kernel) or 7 (tcgen05 on CTA pairs)");
+                "kernel), 7 (tcgen05 on CTA pairs) or 8 (CTA pairs + decode-kernel tails)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
-                "variants 1-4 and 7 need the B200 layout");
+                "variants 1-4, 7 and 8 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

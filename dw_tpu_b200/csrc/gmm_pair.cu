@@ -114,6 +114,9 @@ struct Args {
   void* out;
   int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // pair column tiles per group (n / 256)
+  int tail_min; // 0: a group's rows in tiles of equal size; > 0: tiles of 256 rows and
+                // a last tile only if at least tail_min rows remain (fewer are left to
+                // the decode kernel, which streams the weights once per 16 rows)
   int* status;
   EpHooks hk;   // expert-parallel gating / push (all null for a plain GEMM)
 };
@@ -124,6 +127,12 @@ struct Tile {
   int rows;   // valid rows (1..BT)
   int n_idx;  // column tile
 };
+
+// Row tiles of a group of `rows` rows (see Args::tail_min).
+__device__ __forceinline__ int group_tiles(int rows, int tail_min) {
+  if (tail_min <= 0) return (rows + BT - 1) / BT;
+  return rows / BT + (rows % BT >= tail_min ? 1 : 0);
+}
 
 __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
                                          const Args& a) {
@@ -139,6 +148,11 @@ __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const in
   t.n_idx = local - t_idx * a.n_tiles;
   const int gs_start = row_start[a.group_offset + lo];
   const int gs_rows = row_start[a.group_offset + lo + 1] - gs_start;
+  if (a.tail_min > 0) {
+    t.row0 = gs_start + t_idx * BT;
+    t.rows = min(BT, gs_rows - t_idx * BT);
+    return t;
+  }
   const int nt = (gs_rows + BT - 1) / BT;
   const int r_lo = (int)(((int64_t)t_idx * gs_rows) / nt);
   const int r_hi = (int)(((int64_t)(t_idx + 1) * gs_rows) / nt);
@@ -269,7 +283,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int g = lane * per2 + i;
       if (g < NL) {
         const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        tsum += ((rows + BT - 1) / BT) * a.n_tiles;
+        tsum += group_tiles(rows, a.tail_min) * a.n_tiles;
       }
     }
     int tincl = tsum;
@@ -284,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (g < NL) {
         tile_prefix[g] = trun;
         const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        trun += ((rows + BT - 1) / BT) * a.n_tiles;
+        trun += group_tiles(rows, a.tail_min) * a.n_tiles;
       }
     }
     if (lane == 31) tile_prefix[NL] = trun;
@@ -690,7 +704,7 @@ template <int SD>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, const EpHooks* hooks,
-           cudaStream_t stream) {
+           int tail_min, cudaStream_t stream) {
   using L = Layout<SD>;
   constexpr int es = ScaleTraits<SD>::bytes;
   const bool act_on = act != DWM_ACT_NONE;
@@ -741,6 +755,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.out = out;
   a.ldo = act_on ? n / 2 : n;
   a.n_tiles = n / 256;
+  a.tail_min = tail_min;
   a.status = status_ptr();
   a.hk = hooks ? *hooks : EpHooks{};
   cudaLaunchAttribute attr[1];
@@ -764,22 +779,24 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
 
 // Entry from the grouped-matmul dispatcher (gmm_fp4.cu): B200-layout weights,
 // n a multiple of 256, k of 64; the caller has validated the arguments.
-// hooks: expert-parallel gating / push (dwm_ep_gmm_fp4), or nullptr.
+// hooks: expert-parallel gating / push (dwm_ep_gmm_fp4), or nullptr;
+// tail_min: Args::tail_min.
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
-                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream) {
+                    int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
+                    int tail_min) {
   if (scale_dtype == DWM_U8)
     return gmm_pair::launch<DWM_U8>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                     group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                    hooks, stream);
+                                    hooks, tail_min, stream);
   if (scale_dtype == DWM_BF16)
     return gmm_pair::launch<DWM_BF16>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                       group_offset, n_local, act, limit, out_dtype, zero_init,
-                                      out, hooks, stream);
+                                      out, hooks, tail_min, stream);
   return gmm_pair::launch<DWM_F32>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
                                    group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                   hooks, stream);
+                                   hooks, tail_min, stream);
 }
 
 }  // namespace dwm

@@ -150,8 +150,23 @@ struct Args {
   void* out;
   int ldo;
   int quads;  // tasks per row chunk: n / 64
+  int tail_min;  // 0: all rows; > 0: only the rows past a group's last full 256-row tile,
+                 // and only if fewer than tail_min (the CTA-pair kernel takes the rest)
   int* status;
 };
+
+// The rows [w0, w0 + wn) of a group starting at row gs0 with gsn rows that
+// this launch computes (see Args::tail_min).
+__device__ __forceinline__ void row_window(int gs0, int gsn, int tail_min, int& w0, int& wn) {
+  if (tail_min <= 0) {
+    w0 = gs0;
+    wn = gsn;
+    return;
+  }
+  const int rem = gsn % 256;
+  wn = (rem > 0 && rem < tail_min) ? rem : 0;
+  w0 = gs0 + gsn - wn;
+}
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
@@ -192,8 +207,10 @@ __device__ __forceinline__ Task get_task(int idx, const int* row_start, const in
   const int local = idx - task_prefix[lo];
   const int chunk = local / a.quads;
   t.quad = local - chunk * a.quads;
-  const int gs0 = row_start[a.group_offset + lo];
-  const int gsn = row_start[a.group_offset + lo + 1] - gs0;
+  int gs0, gsn;
+  row_window(row_start[a.group_offset + lo],
+             row_start[a.group_offset + lo + 1] - row_start[a.group_offset + lo], a.tail_min,
+             gs0, gsn);
   t.row0 = gs0 + chunk * 8 * NT;
   t.rows = min(8 * NT, gsn - chunk * 8 * NT);
   return t;
@@ -280,7 +297,10 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     for (int i = 0; i < per2; ++i) {
       const int g = lane * per2 + i;
       if (g < NL) {
-        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        int w0, rows;
+        row_window(row_start[a.group_offset + g],
+                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a.tail_min,
+                   w0, rows);
         tsum += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
       }
     }
@@ -295,7 +315,10 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
       const int g = lane * per2 + i;
       if (g < NL) {
         task_prefix[g] = trun;
-        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+        int w0, rows;
+        row_window(row_start[a.group_offset + g],
+                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a.tail_min,
+                   w0, rows);
         trun += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
       }
     }
@@ -649,7 +672,7 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream) {
+               cudaStream_t stream, int tail_min) {
   gmv::Args a;
   a.group_sizes = group_sizes;
   a.num_groups = num_groups;
@@ -665,6 +688,7 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.out = out;
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.quads = n / 64;
+  a.tail_min = tail_min;
   a.status = status_ptr();
 #define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
   if (nt <= 1 && k % 128 == 0 && DWM_GMV_K128) {

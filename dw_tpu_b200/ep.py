@@ -377,7 +377,7 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
     if expected_rows <= 16:
         return 4  # mma.sync kernel, 16-row token tiles (one task per expert)
     if expected_rows >= 128:
-        return 7  # tcgen05 on CTA pairs (prefill)
+        return 8  # tcgen05 on CTA pairs, short group remainders on the mma.sync kernel
     return 1      # tcgen05 kernel, one CTA
 
 
@@ -392,7 +392,8 @@ class EPMoELayer:
     def __init__(self, weights: FP4MoEWeights, ctx: EPContext, top_k: int, *,
                  scoring_fn: str = "sigmoid", renormalize: bool = True,
                  act_limit: float | None = None, f32_reduce: bool = False,
-                 expected_rows: float | None = None, overlap: bool = False):
+                 expected_rows: float | None = None, overlap: bool = False,
+                 gemm_variant: int | None = None):
         if weights.num_experts != ctx.local_experts:
             raise ValueError(f"weights hold {weights.num_experts} experts, the context "
                              f"{ctx.local_experts} per rank")
@@ -412,7 +413,8 @@ class EPMoELayer:
         self.y = ctx.output(torch.float32 if f32_reduce else torch.bfloat16)
         if expected_rows is None:  # uniform routing over all experts
             expected_rows = t * k / ctx.num_experts * ctx.world
-        self.variant = gemm_variant(weights.layout, expected_rows)
+        self.variant = (globals()["gemm_variant"](weights.layout, expected_rows)
+                        if gemm_variant is None else int(gemm_variant))
         # overlap: the exchange folded into the CTA-pair grouped matmuls
         # (dwm_ep_gmm_fp4): gmm1 starts on each expert as its rows arrive,
         # gmm2 stores its rows straight into the token owners' buffers.
@@ -421,6 +423,8 @@ class EPMoELayer:
             raise ValueError("the overlapped exchange takes B200-layout weights")
         if self.overlap:  # the tcgen05 kernels carry the exchange hooks
             self.variant = 7 if expected_rows >= 128 else 1
+            if gemm_variant is not None and int(gemm_variant) not in (1, 7):
+                raise ValueError("the overlapped exchange runs on variant 1 or 7")
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
 
     kernels_per_forward = 5  # route, dispatch, 2 gmm, combine

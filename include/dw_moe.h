@@ -105,11 +105,16 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * choice for B200 codes whose groups average at most 16 rows),
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
- * double-buffered accumulators (the automatic choice for B200 codes whose
- * groups average 128 rows or more). 1-4 and 7 need DWM_FP4_B200 codes;
- * 5 and 6 are not assigned. Every variant decodes the same bf16 weights and
+ * double-buffered accumulators, a group above 256 rows in tiles of equal
+ * size; 8 = the same kernel for each group's full 256-row tiles (and a last
+ * tile of 96 rows or more), the mma.sync kernel for a shorter remainder,
+ * which then costs one weight stream per 16 rows instead of a whole tile's
+ * decode (the automatic choice for B200 codes whose groups average 128 rows
+ * or more). 1-4, 7 and 8 need DWM_FP4_B200 codes; 5 and 6 are not
+ * assigned. Every variant decodes the same bf16 weights and
  * accumulates in f32; results differ between variants only by f32 summation
- * order (1 and 7 give identical bits). Same reference interface as
+ * order (1 and 7 give identical bits; 8 gives them on every group's first
+ * 256 rows). Same reference interface as
  * dwm_gmm_fp4 (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
                         int scale_dtype, const int32_t* group_sizes, int num_groups, int m,

@@ -444,8 +444,8 @@ def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce, t, variant):
         def shard(r):
             return dw.FP4MoEWeights(w.w13[r * le:(r + 1) * le], w.s13[r * le:(r + 1) * le],
                                     w.w2[r * le:(r + 1) * le], w.s2[r * le:(r + 1) * le], "b200")
-        serial = [ep.EPMoELayer(shard(r), ctx_s[r], k, f32_reduce=f32_reduce)
-                  for r in range(world)]
+        serial = [ep.EPMoELayer(shard(r), ctx_s[r], k, f32_reduce=f32_reduce,
+                                gemm_variant=variant) for r in range(world)]
         over = [ep.EPMoELayer(shard(r), ctx_o[r], k, f32_reduce=f32_reduce, overlap=True)
                 for r in range(world)]
         assert all(ly.variant == variant for ly in serial + over)

@@ -127,7 +127,7 @@ def _worker(rank, world, port, q):
         lw4 = dw.FP4MoEWeights(w4.w13[sl4], w4.s13[sl4], w4.w2[sl4], w4.s2[sl4], "b200")
         ctx4 = ep.create_context(max_tokens=t4, hidden=h4, topk=k4, num_experts=e4)
         ctx5 = ep.create_context(max_tokens=t4, hidden=h4, topk=k4, num_experts=e4)
-        ser = ep.EPMoELayer(lw4, ctx4, k4)
+        ser = ep.EPMoELayer(lw4, ctx4, k4, gemm_variant=7)
         ovl = ep.EPMoELayer(lw4, ctx5, k4, overlap=True)
         for step in range(2):
             x4, r4 = synthetic.layer_inputs(t4, h4, e4, seed=90 + 10 * step + rank)

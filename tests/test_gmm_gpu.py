@@ -354,7 +354,7 @@ def test_gmm_prefill_tiles(dw, layout):
     for act, kind, n_out in ((L.ACT_NONE, None, 512), (L.ACT_SWIGLU, "swiglu", 256)):
         r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind)
         r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in ((0, 1, 7) if layout == "b200" else (0,)):
+        for variant in ((0, 1, 7, 8) if layout == "b200" else (0,)):
             out = torch.full((m, n_out), 5.0, dtype=torch.bfloat16, device="cuda")
             ops.gmm_fp4_out(np_to_bf16(lhs), codes, sc, g, out, act=act, zero_init=True,
                             layout=layout, variant=variant)

@@ -97,9 +97,10 @@ def test_layer_graph_capture_replays_bitwise(dw):
 
 def test_layer_prefill_pair_kernel(dw):
     """A prefill-sized layer (512 tokens, top-8 over 16 experts: ~256 rows
-    per expert) takes the GEMM on CTA pairs automatically: its output has the
-    single-CTA kernel's bits, replays bitwise from a CUDA graph, and matches
-    the oracle layer."""
+    per expert) takes the GEMM on CTA pairs automatically (variant 8, short
+    group remainders on the decode kernel): it replays bitwise from a CUDA
+    graph and matches the oracle layer; the pair kernel alone (variant 7) has
+    the single-CTA kernel's bits."""
     from dw_tpu_b200 import synthetic
     t, e, h, i, k = 512, 16, 512, 256, 8
     w = synthetic.moe_weights(e, h, i, seed=8, device="cuda")
@@ -111,14 +112,17 @@ def test_layer_prefill_pair_kernel(dw):
     xc = x.cuda()
     lc = (x.float() @ router.float()).to(torch.bfloat16).cuda()
     auto = dw.MoELayer(w, k, t)
+    pair = dw.MoELayer(w, k, t, gemm_variant=7)
     single = dw.MoELayer(w, k, t, gemm_variant=1)
     out = auto(xc, lc)
+    out_pair = pair(xc, lc)
     ref_bits = single(xc, lc)
     torch.cuda.synchronize()
     from dw_tpu_b200 import _lib
     _lib.raise_on_device_error()
     assert int(auto.group_sizes.float().mean().item()) >= 128
-    assert torch.equal(out.view(torch.int16), ref_bits.view(torch.int16))
+    assert int(auto.group_sizes.max().item()) > 256  # a remainder for the decode kernel
+    assert torch.equal(out_pair.view(torch.int16), ref_bits.view(torch.int16))
     res = torch.empty_like(out)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
