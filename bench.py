@@ -63,6 +63,9 @@ GMM_TRAFFIC_PER_LAUNCH_N1 = 1504650000.0
 # fp32 restatement): the reference's GMM_EP error level, 4e-3 at K=4096,
 # scaled by sqrt(K/4096) with K = I for the last projection.
 PARITY_REL_TOL = 4e-3 * (I / 4096) ** 0.5
+# A device-side sleep (cycles, ~10 ms at 1.9 GHz) before a loop of short
+# launches, so that the launches queue up and CUDA events time the device.
+PREROLL_CYCLES = 20_000_000
 E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
                -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
 
@@ -422,6 +425,7 @@ def run_ours(args, rank, world, local_rank):
     with GmmTimer() as gt, ClockSampler(local_rank) as clk:
         barrier()
         torch.cuda.synchronize(dev)
+        torch.cuda._sleep(PREROLL_CYCLES)  # the steps queue up: the events time the device
         start.record(stream)
         for _ in range(args.steps):
             layer(x, logits, out=out)
@@ -799,7 +803,13 @@ def ep_extras(args, local, dev, world, rank):
                         c_fn()
                     torch.cuda.synchronize(dev)
                     dist.barrier()
-                    dts, cts = [], []
+                    evs = []
+                    # The one-shot kernels are shorter than the host's launch
+                    # path: queue all iterations behind a device-side sleep so
+                    # that the events time the device, not the host. (The NCCL
+                    # path syncs on the host every dispatch; it runs as is.)
+                    if name == "oneshot":
+                        torch.cuda._sleep(PREROLL_CYCLES)
                     for _ in range(20):
                         a0, a1 = events()
                         b0, b1 = events()
@@ -809,9 +819,10 @@ def ep_extras(args, local, dev, world, rank):
                         b0.record()
                         c_fn()
                         b1.record()
-                        torch.cuda.synchronize(dev)
-                        dts.append(a0.elapsed_time(a1))
-                        cts.append(b0.elapsed_time(b1))
+                        evs.append((a0, a1, b0, b1))
+                    torch.cuda.synchronize(dev)
+                    dts = [a0.elapsed_time(a1) for a0, a1, _, _ in evs]
+                    cts = [b0.elapsed_time(b1) for _, _, b0, b1 in evs]
                     times[name] = (statistics.median(dts), statistics.median(cts))
                 owners = ids_np // le
                 out_pairs = int((owners != rank).sum())
@@ -897,15 +908,17 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
         layer(x, logits, out=out)
     torch.cuda.synchronize(dev)
     dist.barrier()
-    ts = []
+    evs = []
     with GmmTimer() as gt:
+        torch.cuda._sleep(PREROLL_CYCLES)  # queue the steps: the events time the device
         for _ in range(iters):
             e0, e1 = events()
             e0.record()
             layer(x, logits, out=out)
             e1.record()
-            torch.cuda.synchronize(dev)
-            ts.append(e0.elapsed_time(e1))
+            evs.append((e0, e1))
+        torch.cuda.synchronize(dev)
+    ts = [a.elapsed_time(b) for a, b in evs]
     L.raise_on_device_error()
     g1, g2 = gt.ms()
     gs = ctx.recv_group_sizes.cpu().numpy()
