@@ -178,8 +178,23 @@ class EPContext:
         if g != self.local_experts or lhs.shape[1] != 2 * k2:
             raise ValueError("codes must be this rank's experts in the B200 layout "
                              "[E/world, n, k/2] matching lhs")
-        if mode == L.EP_GEMM_GATED and (out is None or out.shape[0] != self.capacity):
-            raise ValueError("the gated matmul writes out [capacity, n or n/2]")
+        k = 2 * k2
+        if sc.numel() != g * (k // 32) * n or not sc.is_contiguous() or not codes.is_contiguous():
+            raise ValueError(f"scales must be contiguous [{g}, {k // 32}, {n}] and codes "
+                             "contiguous")
+        if mode == L.EP_GEMM_GATED:
+            n_out = n if act == L.ACT_NONE else n // 2
+            if out is None or out.shape != (self.capacity, n_out) or not out.is_contiguous():
+                raise ValueError(f"the gated matmul writes a contiguous out "
+                                 f"[{self.capacity}, {n_out}]")
+            if lhs.data_ptr() != self.recv.data_ptr():
+                raise ValueError("the gated matmul reads the receive buffer (lhs = recv)")
+        elif mode == L.EP_GEMM_PUSH:
+            if act != L.ACT_NONE or n != self.hidden or lhs.shape[0] != self.capacity:
+                raise ValueError("the pushing matmul is the down projection: no activation, "
+                                 f"n = {self.hidden}, lhs [{self.capacity}, k]")
+        else:
+            raise ValueError(f"unknown mode {mode}")
         odt = out.dtype if out is not None else out_dtype
         L.check(L.lib().dwm_ep_gmm_fp4(
             self._ctx, lhs.data_ptr(), codes.view(torch.uint8).data_ptr(), L.FP4_B200,
