@@ -589,8 +589,8 @@ def prefill_gemm(weights, dev, seed, iters=10):
     out = {"workload": "cfg3 rank at n=8: 32 experts, 8192 rows, H=4096, I=2048",
            "bound": "tensor", "peak": peak, "unit": "TFLOP/s",
            "peak_source": "measured burst" if peaks else "fallback",
-           "kernel": "dw_moe gmm_fp4 (automatic choice, variant 8: tcgen05 on CTA pairs, "
-                     "short group remainders on the mma.sync kernel)"}
+           "kernel": "dw_moe gmm_fp4 (automatic choice, variant 9: tcgen05 on CTA pairs, "
+                     "tiles of up to 512 rows)"}
     for kind in ("uniform", "multinomial"):
         if kind == "uniform":
             gs_np = np.full(e, rows // e, np.int32)
@@ -616,7 +616,7 @@ def prefill_gemm(weights, dev, seed, iters=10):
             tf = flops / statistics.median(ts) / 1e9
             out[f"{kind}_{name}_tflops"] = round(tf, 1)
             out[f"{kind}_{name}_frac"] = round(tf / peak, 4)
-        if kind == "multinomial":  # the pair kernel alone (variant 7), equal-size tiles
+        if kind == "multinomial":  # the pair kernel with 256-row tiles (variant 7)
             for name, fn, flops in (
                     ("gmm1", lambda: ops.gmm_fp4_out(x, w.w13, w.s13, gs, h1, act=L.ACT_SWIGLU,
                                                      layout=w.layout, variant=7),

@@ -804,7 +804,7 @@ int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int 
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min);
+                    int tail_min, int wide);
 int launch_gmm_single_ep(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                          const int32_t* group_sizes, int num_groups, int m, int k, int n,
                          int act, float limit, int out_dtype, void* out, const EpHooks* hooks,
@@ -819,9 +819,9 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
   int rc = check_ctx(c);
   if (rc) return rc;
   DWM_CHECK_ARG(mode == DWM_EP_GEMM_GATED || mode == DWM_EP_GEMM_PUSH, "mode=%d", mode);
-  DWM_CHECK_ARG(variant == 1 || variant == 7,
-                "the EP grouped matmul runs on the tcgen05 kernels: variant 1 (one CTA) or 7 "
-                "(CTA pairs)");
+  DWM_CHECK_ARG(variant == 1 || variant == 7 || variant == 9,
+                "the EP grouped matmul runs on the tcgen05 kernels: variant 1 (one CTA), 7 "
+                "(CTA pairs) or 9 (CTA pairs, 512-row tiles)");
   DWM_CHECK_ARG(codes_format == DWM_FP4_B200, "the EP grouped matmul takes the B200 layout");
   DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
                 "scale dtype must be u8 (e8m0), bf16 or f32");
@@ -863,7 +863,7 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
                                 dst, &hk, s);
   return launch_gmm_pair(lhs, codes, scales, scale_dtype, recv_group_sizes, c->local_experts,
                          (int)c->cap, k, n, 0, c->local_experts, act, act_limit, out_dtype, 0, dst,
-                         &hk, s, 0);
+                         &hk, s, 0, variant == 9 ? 1 : 0);
 }
 
 extern "C" int dwm_ep_link_probe(dwm_ep* c, int peer, int64_t bytes, void* stream) {

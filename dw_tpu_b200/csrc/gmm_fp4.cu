@@ -41,7 +41,7 @@ int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int 
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min);
+                    int tail_min, int wide);
 
 namespace gmm {
 
@@ -1030,9 +1030,11 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // up to 6 rows per local group on average and 16-row tiles above, 3 / 4 = the
 // same with 8 / 16-row tiles, 7 = tcgen05 on CTA pairs (gmm_pair.cu, B200
 // layout), 8 = 7 for each group's 256-row tiles and a remainder of at least
-// kPairTailMin rows, the decode kernel for shorter remainders.
+// kPairTailMin rows, the decode kernel for shorter remainders, 9 = 7 with
+// tiles of up to 512 rows (two UMMAs per k-step over one decoded stage).
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 16 rows, variant 8 from 128 rows (prefill), else the
+// average at most 16 rows, variant 8 from 128 rows and variant 9 from 224
+// (prefill; most groups then exceed 256 rows or come close), else the
 // single-CTA tcgen05 kernel with 128-row tiles.
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
@@ -1048,7 +1050,11 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   }
   const int64_t avg = ((int64_t)m + num_local_groups - 1) / num_local_groups;
   if (variant == 0)
-    variant = codes_format != DWM_FP4_B200 ? 1 : avg <= 16 ? 2 : avg >= 128 ? 8 : 1;
+    variant = codes_format != DWM_FP4_B200 ? 1
+              : avg <= 16                  ? 2
+              : avg >= 224                 ? 9
+              : avg >= 128                 ? 8
+                                           : 1;
   if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
@@ -1056,7 +1062,11 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   if (variant == 7)
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
-                           out, nullptr, s, 0);
+                           out, nullptr, s, 0, 0);
+  if (variant == 9)
+    return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                           group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
+                           out, nullptr, s, 0, 1);
   if (variant == 8) {
     // Full 256-row tiles (and remainders of kPairTailMin rows or more) on CTA
     // pairs, shorter remainders on the decode kernel: a remainder of r rows
@@ -1064,7 +1074,7 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     // weight stream per 16 rows.
     int rc = launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                              group_offset, num_local_groups, act, act_limit, out_dtype,
-                             zero_init, out, nullptr, s, kPairTailMin);
+                             zero_init, out, nullptr, s, kPairTailMin, 0);
     if (rc) return rc;
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, 0, out, 2, s,
@@ -1128,11 +1138,12 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 8 && variant != 5 && variant != 6,
+  DWM_CHECK_ARG(variant >= 0 && variant <= 9 && variant != 5 && variant != 6,
                 "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-4 (mma.sync decode "
-                "kernel), 7 (tcgen05 on CTA pairs) or 8 (CTA pairs + decode-kernel tails)");
+                "kernel), 7 (tcgen05 on CTA pairs), 8 (CTA pairs + decode-kernel tails) or 9 "
+                "(CTA pairs, 512-row tiles)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
-                "variants 1-4, 7 and 8 need the B200 layout");
+                "variants 1-4 and 7-9 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

@@ -66,7 +66,6 @@ constexpr int TMEM_COLS = 512;    // two 256-column accumulator buffers
 constexpr int ACC_COLS = 256;
 constexpr int A_STAGE = ROWS * BK * 2;  // 16 KiB of bf16, 128-byte swizzled, K-major
 constexpr int T_STAGE = HALF * BK * 2;  // 16 KiB: this CTA's token rows of one k-step
-constexpr int STAGE = A_STAGE + T_STAGE;
 constexpr int C_STAGE = ROWS * BK / 2;  // 4 KiB of codes: 8 column blocks x 4 k-blocks x 32 words
 constexpr int T_BOX_ROWS = 16;
 constexpr int T_BOX_BYTES = T_BOX_ROWS * BK * 2;  // 2 KiB
@@ -82,13 +81,21 @@ constexpr int EPI_WARP_BYTES = 16 * 32 * 4;       // 16 token rows x 32 columns 
 #define DWM_PAIR_EPI_SLEEP 256
 #endif
 
-template <int SD>
+// WIDE: tiles of up to 512 token rows as two UMMAs per k16 step (N = 256 and
+// the rest) into both TMEM accumulator slots over one decoded A, so a group
+// of 257-512 rows costs one tile's decode instead of two; each CTA then
+// stages up to 256 token rows per k-step (a 32 KiB token stage), which leaves
+// room for 4 stages. Such a tile holds both slots, so its epilogue overlaps
+// only the next tile's wait for its first slot (AccRing).
+template <int SD, bool WIDE>
 struct Layout {
-  static constexpr int S = DWM_PAIR_STAGES;
-  static constexpr int CS = DWM_PAIR_CS;
+  static constexpr int S = WIDE ? 4 : DWM_PAIR_STAGES;
+  static constexpr int CS = WIDE ? (ScaleTraits<SD>::bytes == 1 ? 4 : 3) : DWM_PAIR_CS;
+  static constexpr int T_ST = (WIDE ? 2 : 1) * T_STAGE;  // this CTA's token rows of a k-step
+  static constexpr int STG = A_STAGE + T_ST;
   static constexpr int S_STAGE = 2 * ROWS * ScaleTraits<SD>::bytes;  // [k32 block][128 rows]
-  static constexpr int OFF_STAGE = 0;  // stage i: A at i * STAGE, tokens A_STAGE after it
-  static constexpr int OFF_C = OFF_STAGE + S * STAGE;
+  static constexpr int OFF_STAGE = 0;  // stage i: A at i * STG, tokens A_STAGE after it
+  static constexpr int OFF_C = OFF_STAGE + S * STG;
   static constexpr int OFF_S = OFF_C + CS * C_STAGE;
   static constexpr int OFF_BAR = OFF_S + CS * S_STAGE;
   static constexpr int NUM_BARS = 2 * CS + 2 * S + 4 + 1;
@@ -99,7 +106,7 @@ struct Layout {
   static constexpr int BYTES = OFF_EPI + EPI_WARPS * EPI_WARP_BYTES;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1 KiB alignment
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
-  static_assert(STAGE % 1024 == 0 && A_STAGE % 1024 == 0, "swizzled tiles need 1 KiB alignment");
+  static_assert(STG % 1024 == 0 && A_STAGE % 1024 == 0, "swizzled tiles need 1 KiB alignment");
   static_assert(CS <= 32 && S <= 32, "ring masks are 32-bit");
 };
 
@@ -114,6 +121,7 @@ struct Args {
   void* out;
   int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // pair column tiles per group (n / 256)
+  int max_rows; // token rows per tile at most: 256, or 512 for the WIDE kernel
   int tail_min; // 0: a group's rows in tiles of equal size; > 0: tiles of 256 rows and
                 // a last tile only if at least tail_min rows remain (fewer are left to
                 // the decode kernel, which streams the weights once per 16 rows)
@@ -128,10 +136,11 @@ struct Tile {
   int n_idx;  // column tile
 };
 
-// Row tiles of a group of `rows` rows (see Args::tail_min).
-__device__ __forceinline__ int group_tiles(int rows, int tail_min) {
-  if (tail_min <= 0) return (rows + BT - 1) / BT;
-  return rows / BT + (rows % BT >= tail_min ? 1 : 0);
+// Row tiles of a group of `rows` rows, tiles of at most bt rows (see
+// Args::tail_min).
+__device__ __forceinline__ int group_tiles(int rows, int bt, int tail_min) {
+  if (tail_min <= 0) return (rows + bt - 1) / bt;
+  return rows / bt + (rows % bt >= tail_min ? 1 : 0);
 }
 
 __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
@@ -148,18 +157,39 @@ __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const in
   t.n_idx = local - t_idx * a.n_tiles;
   const int gs_start = row_start[a.group_offset + lo];
   const int gs_rows = row_start[a.group_offset + lo + 1] - gs_start;
+  const int bt = a.max_rows;
   if (a.tail_min > 0) {
-    t.row0 = gs_start + t_idx * BT;
-    t.rows = min(BT, gs_rows - t_idx * BT);
+    t.row0 = gs_start + t_idx * bt;
+    t.rows = min(bt, gs_rows - t_idx * bt);
     return t;
   }
-  const int nt = (gs_rows + BT - 1) / BT;
+  const int nt = (gs_rows + bt - 1) / bt;
   const int r_lo = (int)(((int64_t)t_idx * gs_rows) / nt);
   const int r_hi = (int)(((int64_t)(t_idx + 1) * gs_rows) / nt);
   t.row0 = gs_start + r_lo;
   t.rows = r_hi - r_lo;
   return t;
 }
+
+// The two 256-column TMEM accumulator slots. A tile of up to 256 rows takes
+// the next slot and the one after alternates; a WIDE tile of more rows takes
+// both (rows 0-255 in the next slot, the rest in the other) and leaves the
+// pointer where it was, since the epilogue drains that slot first. The UMMA
+// issuer and the epilogue walk the same tile sequence with a ring each; par
+// bit s is the phase parity of slot s's next fill.
+struct AccRing {
+  int nxt = 0;
+  uint32_t par = 0;
+  __device__ __forceinline__ void take(bool both, int& sa, int& sb, uint32_t& pa,
+                                       uint32_t& pb) {
+    sa = nxt;
+    sb = nxt ^ 1;
+    pa = (par >> sa) & 1u;
+    pb = (par >> sb) & 1u;
+    par ^= 1u << sa;
+    if (both) par ^= 1u << sb; else nxt ^= 1;
+  }
+};
 
 // UMMA N of a tile: rows rounded up to 32 (each CTA's half a multiple of 16).
 __device__ __forceinline__ int tile_n(int rows) { return max(32, (rows + 31) & ~31); }
@@ -186,13 +216,13 @@ __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint6
   return *slot != 0;
 }
 
-template <int SD>
+template <int SD, bool WIDE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_pair_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                     const __grid_constant__ CUtensorMap tm_lhs_half,
                     const __grid_constant__ CUtensorMap tm_codes,
                     const __grid_constant__ CUtensorMap tm_scales, const Args a) {
-  using L = Layout<SD>;
+  using L = Layout<SD, WIDE>;
   constexpr int CS = L::CS;
   constexpr int S = L::S;
   extern __shared__ uint8_t smem_raw[];
@@ -283,7 +313,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int g = lane * per2 + i;
       if (g < NL) {
         const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        tsum += group_tiles(rows, a.tail_min) * a.n_tiles;
+        tsum += group_tiles(rows, a.max_rows, a.tail_min) * a.n_tiles;
       }
     }
     int tincl = tsum;
@@ -298,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (g < NL) {
         tile_prefix[g] = trun;
         const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        trun += group_tiles(rows, a.tail_min) * a.n_tiles;
+        trun += group_tiles(rows, a.max_rows, a.tail_min) * a.n_tiles;
       }
     }
     if (lane == 31) tile_prefix[NL] = trun;
@@ -339,15 +369,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t epi_s = smem_u32(smem + L::OFF_EPI + q * EPI_WARP_BYTES);
     constexpr float acc_scale = (float)(1 << decode_delta<SD>());  // undoes the decode bias
     const bool hi_lane = lane >= 16;
-    int it = 0;
-    for (int idx = cl; idx < total; idx += ncl, ++it) {
+    AccRing ring;
+    for (int idx = cl; idx < total; idx += ncl) {
       const Tile t = get_tile(idx, row_start, tile_prefix, a);
-      const int buf = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
-      const bool got = mbar_wait<DWM_PAIR_EPI_SLEEP>(&acc_full[buf], ph, abort_flag, a.status);
+      const bool both = WIDE && tile_n(t.rows) > BT;
+      int sa, sb;
+      uint32_t pa, pb;
+      ring.take(both, sa, sb, pa, pb);
+      bool got = mbar_wait<DWM_PAIR_EPI_SLEEP>(&acc_full[sa], pa, abort_flag, a.status);
+      if (both) got = got && mbar_wait<DWM_PAIR_EPI_SLEEP>(&acc_full[sb], pb, abort_flag, a.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * ACC_COLS);
+      const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t ta = tq + (uint32_t)(sa * ACC_COLS), tb = tq + (uint32_t)(sb * ACC_COLS);
+      // Chunk c of 16 token rows: rows 0-255 in slot sa, the rest in sb.
+      auto chunk_addr = [&](int c) { return (c < 16 ? ta : tb) + (uint32_t)((c & 15) * 16); };
+      // Slot sa of a two-slot tile is free once its 16 chunks are in registers.
+      auto release_first = [&](int c) {
+        if (both && c == 15) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(sa * 8));
+        }
+      };
       const int nchunks = (t.rows + 15) >> 4;
       if (act) {
         // Lanes 0-15 hold the gate, lanes 16-31 the up column of features
@@ -358,8 +402,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int vpr = row_bytes / 16;
         for (int c = 0; c < nchunks; ++c) {
           uint32_t r[16];
-          tmem_ld16(tbase + c * 16, r);
+          tmem_ld16(chunk_addr(c), r);
           tmem_ld_wait();
+          release_first(c);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float even = __uint_as_float(r[2 * e]) * acc_scale;
@@ -396,8 +441,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int vpr = row_bytes / 16;
         for (int c = 0; c < nchunks; ++c) {
           uint32_t r[16];
-          tmem_ld16(tbase + c * 16, r);
+          tmem_ld16(chunk_addr(c), r);
           tmem_ld_wait();
+          release_first(c);
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const float v = __uint_as_float(r[e]) * acc_scale;
@@ -433,7 +479,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(buf * 8));
+      if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)((both ? sb : sa) * 8));
     }
   } else if (warp == PRODUCER_WARP) {
     // ---------------- TMA producer: codes + scales (HBM stream) ----------------
@@ -469,7 +515,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == TOKEN_WARP) {
     // ---------------- TMA producer: this CTA's token rows ----------------
-    // A full half (128 rows) is one box; a partial one nb boxes of 16 rows.
+    // A tile's N rows are UMMA 1's first min(N, 256) and (WIDE) UMMA 2's rest;
+    // this CTA loads its half of each part, the second 16 KiB after the
+    // first. A full half (128 rows) is one box; a partial one nb boxes of 16
+    // rows.
     if (lane == 0) {
       const uint64_t pol_keep = policy_evict_last();
       int st = 0;
@@ -489,26 +538,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_all();
           gated = t.g;
         }
-        const int half = tile_n(t.rows) / 2;
-        const int nb = half / T_BOX_ROWS;
-        const int rbase = t.row0 + (int)rank * half;
+        const int n_all = tile_n(t.rows);
+        const int n1 = min(n_all, BT), n2 = n_all - n1;  // n2 > 0 only in WIDE tiles
+        const int nb1 = n1 / 2 / T_BOX_ROWS, nb2 = n2 / 2 / T_BOX_ROWS;
+        const int rbase1 = t.row0 + (int)rank * (n1 / 2);
+        const int rbase2 = t.row0 + n1 + (int)rank * (n2 / 2);
         for (int kk = 0; kk < KT; ++kk) {
           if (!mbar_wait(&empty[st], ph ^ 1, abort_flag, a.status)) {
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * nb * T_BOX_BYTES));
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * (nb1 + nb2) * T_BOX_BYTES));
           armed |= 1u << st;
           par = (par & ~(1u << st)) | (ph << st);
           const uint32_t bar0 = full_0 + (uint32_t)(st * 8);
-          uint8_t* tdst = smem + L::OFF_STAGE + st * STAGE + A_STAGE;
-          if (nb == HALF / T_BOX_ROWS) {
-            tma_load_2d_pair(tdst, &tm_lhs_half, bar0, kk * BK, rbase, pol_keep);
-          } else {
-            for (int bx = 0; bx < nb; ++bx)
-              tma_load_2d_pair(tdst + bx * T_BOX_BYTES, &tm_lhs, bar0, kk * BK,
-                               rbase + bx * T_BOX_ROWS, pol_keep);
-          }
+          uint8_t* tdst = smem + L::OFF_STAGE + st * L::STG + A_STAGE;
+          auto load_part = [&](uint8_t* dst, int nb, int rbase) {
+            if (nb == HALF / T_BOX_ROWS) {
+              tma_load_2d_pair(dst, &tm_lhs_half, bar0, kk * BK, rbase, pol_keep);
+            } else {
+              for (int bx = 0; bx < nb; ++bx)
+                tma_load_2d_pair(dst + bx * T_BOX_BYTES, &tm_lhs, bar0, kk * BK,
+                                 rbase + bx * T_BOX_ROWS, pol_keep);
+            }
+          };
+          load_part(tdst, nb1, rbase1);
+          if (WIDE && nb2 > 0) load_part(tdst + T_STAGE, nb2, rbase2);
           if (++st == S) { st = 0; ph ^= 1; }
         }
       }
@@ -525,37 +581,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool issuer = elect_one();
       int st = 0;
       uint32_t ph = 0;
-      int it = 0;
+      AccRing ring;
       bool ok = true;
-      for (int idx = cl; idx < total && ok; idx += ncl, ++it) {
+      for (int idx = cl; idx < total && ok; idx += ncl) {
         const Tile t = get_tile(idx, row_start, tile_prefix, a);
-        const uint32_t idesc = idesc_bf16(2 * ROWS, tile_n(t.rows), false, false);
-        const int buf = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag, a.status)))
-          break;
+        const int n_all = tile_n(t.rows);
+        const int n1 = min(n_all, BT), n2 = n_all - n1;  // n2 > 0 only in WIDE tiles
+        const bool both = WIDE && n2 > 0;
+        const uint32_t idesc = idesc_bf16(2 * ROWS, n1, false, false);
+        const uint32_t idesc2 = idesc_bf16(2 * ROWS, n2 > 0 ? n2 : 32, false, false);
+        int sa, sb;
+        uint32_t pa, pb;
+        ring.take(both, sa, sb, pa, pb);
+        bool free_ok = mbar_wait(&acc_empty[sa], pa ^ 1, abort_flag, a.status);
+        if (both) free_ok = free_ok && mbar_wait(&acc_empty[sb], pb ^ 1, abort_flag, a.status);
+        if (!__all_sync(0xffffffffu, free_ok)) break;
         tc_fence_after();
-        const uint32_t d0 = tmem + (uint32_t)(buf * ACC_COLS);
+        const uint32_t d0 = tmem + (uint32_t)(sa * ACC_COLS);
+        const uint32_t d1 = tmem + (uint32_t)(sb * ACC_COLS);
         for (int kk = 0; kk < KT; ++kk) {
           if (!__all_sync(0xffffffffu, mbar_wait(&full[st], ph, abort_flag, a.status))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + L::OFF_STAGE + st * STAGE);
+          const uint32_t a_base = smem_u32(smem + L::OFF_STAGE + st * L::STG);
           const uint32_t t_base = a_base + A_STAGE;
           if (issuer) {
 #pragma unroll
-            for (int j = 0; j < BK / 16; ++j)
-              umma_pair_bf16(d0, smem_desc_sw128(a_base + j * 32, 16, 1024),
-                             smem_desc_sw128(t_base + j * 32, 16, 1024), idesc, (kk | j) != 0);
+            for (int j = 0; j < BK / 16; ++j) {
+              const uint64_t adesc = smem_desc_sw128(a_base + j * 32, 16, 1024);
+              umma_pair_bf16(d0, adesc, smem_desc_sw128(t_base + j * 32, 16, 1024), idesc,
+                             (kk | j) != 0);
+              if (both)  // token rows 256.. into the other slot
+                umma_pair_bf16(d1, adesc,
+                               smem_desc_sw128(t_base + T_STAGE + j * 32, 16, 1024), idesc2,
+                               (kk | j) != 0);
+            }
             umma_commit_pair(&empty[st]);
           }
           __syncwarp();
           if (++st == S) { st = 0; ph ^= 1; }
         }
         if (!ok) break;
-        if (issuer) umma_commit_pair(&acc_full[buf]);
+        if (issuer) {
+          umma_commit_pair(&acc_full[sa]);
+          if (both) umma_commit_pair(&acc_full[sb]);
+        }
         __syncwarp();
       }
       if (issuer) umma_commit_pair(drain_bar);
@@ -598,7 +670,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
         const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE;
-        uint8_t* astage = smem + L::OFF_STAGE + st * STAGE;
+        uint8_t* astage = smem + L::OFF_STAGE + st * L::STG;
         // The four lanes of a quad (same gid) need the same four scales: k32
         // half h, column gid + 8c. Lane tig converts scale (h, c) = (tig >> 1,
         // tig & 1) and the quad exchanges the multipliers.
@@ -677,7 +749,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // Largest number of 2-CTA clusters resident at once (one CTA per SM), per
 // device (cached; safe to call from several host threads).
-template <int SD>
+template <int SD, bool WIDE>
 int max_pairs(cudaLaunchConfig_t cfg) {
   static std::mutex mu;
   static std::map<int, int> cached;  // device -> clusters
@@ -690,7 +762,7 @@ int max_pairs(cudaLaunchConfig_t cfg) {
   }
   int n = 0;
   cfg.gridDim = dim3(2 * (unsigned)std::max(1, num_sms() / 2));
-  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gmm_pair_kernel<SD>, &cfg);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gmm_pair_kernel<SD, WIDE>, &cfg);
   if (e != cudaSuccess || n < 1) {
     (void)cudaGetLastError();
     n = std::max(1, num_sms() / 2);
@@ -700,12 +772,12 @@ int max_pairs(cudaLaunchConfig_t cfg) {
   return n;
 }
 
-template <int SD>
+template <int SD, bool WIDE>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, const EpHooks* hooks,
            int tail_min, cudaStream_t stream) {
-  using L = Layout<SD>;
+  using L = Layout<SD, WIDE>;
   constexpr int es = ScaleTraits<SD>::bytes;
   const bool act_on = act != DWM_ACT_NONE;
   CUtensorMap tm_lhs, tm_lhs_half, tm_codes, tm_scales;
@@ -738,7 +810,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  rc = set_smem_limit(reinterpret_cast<const void*>(gmm_pair_kernel<SD>), L::ALLOC, "gmm pair smem attribute");
+  rc = set_smem_limit(reinterpret_cast<const void*>(gmm_pair_kernel<SD, WIDE>), L::ALLOC, "gmm pair smem attribute");
   if (rc) return rc;
   Args a;
   a.group_sizes = group_sizes;
@@ -756,6 +828,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act_on ? n / 2 : n;
   a.n_tiles = n / 256;
   a.tail_min = tail_min;
+  a.max_rows = WIDE ? 2 * BT : BT;
   a.status = status_ptr();
   a.hk = hooks ? *hooks : EpHooks{};
   cudaLaunchAttribute attr[1];
@@ -769,8 +842,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(2 * (unsigned)max_pairs<SD>(cfg));
-  return check_cuda(cudaLaunchKernelEx(&cfg, gmm_pair_kernel<SD>, tm_lhs, tm_lhs_half, tm_codes,
+  cfg.gridDim = dim3(2 * (unsigned)max_pairs<SD, WIDE>(cfg));
+  return check_cuda(cudaLaunchKernelEx(&cfg, gmm_pair_kernel<SD, WIDE>, tm_lhs, tm_lhs_half, tm_codes,
                                        tm_scales, a),
                     "gmm_pair launch");
 }
@@ -780,23 +853,21 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
 // Entry from the grouped-matmul dispatcher (gmm_fp4.cu): B200-layout weights,
 // n a multiple of 256, k of 64; the caller has validated the arguments.
 // hooks: expert-parallel gating / push (dwm_ep_gmm_fp4), or nullptr;
-// tail_min: Args::tail_min.
+// tail_min: Args::tail_min; wide: tiles of up to 512 token rows (Layout).
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min) {
-  if (scale_dtype == DWM_U8)
-    return gmm_pair::launch<DWM_U8>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                    group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                    hooks, tail_min, stream);
+                    int tail_min, int wide) {
+#define DWM_PAIR_LAUNCH(SD, W)                                                               \
+  gmm_pair::launch<SD, W>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset, \
+                          n_local, act, limit, out_dtype, zero_init, out, hooks, tail_min,   \
+                          stream)
+  if (scale_dtype == DWM_U8) return wide ? DWM_PAIR_LAUNCH(DWM_U8, true) : DWM_PAIR_LAUNCH(DWM_U8, false);
   if (scale_dtype == DWM_BF16)
-    return gmm_pair::launch<DWM_BF16>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                      group_offset, n_local, act, limit, out_dtype, zero_init,
-                                      out, hooks, tail_min, stream);
-  return gmm_pair::launch<DWM_F32>(lhs, codes, scales, group_sizes, num_groups, m, k, n,
-                                   group_offset, n_local, act, limit, out_dtype, zero_init, out,
-                                   hooks, tail_min, stream);
+    return wide ? DWM_PAIR_LAUNCH(DWM_BF16, true) : DWM_PAIR_LAUNCH(DWM_BF16, false);
+  return wide ? DWM_PAIR_LAUNCH(DWM_F32, true) : DWM_PAIR_LAUNCH(DWM_F32, false);
+#undef DWM_PAIR_LAUNCH
 }
 
 }  // namespace dwm

@@ -171,7 +171,8 @@ class EPContext:
         reads the receive buffer (lhs = ``recv``) expert by expert as the rows
         arrive and writes ``out``; EP_GEMM_PUSH stores every output row into
         its token owner's buffer (``out`` unused). ``variant`` 1 runs the
-        one-CTA tcgen05 kernel, 7 the CTA-pair kernel."""
+        one-CTA tcgen05 kernel, 7 the CTA-pair kernel, 9 the CTA-pair kernel
+        with tiles of up to 512 rows."""
         L.require_cuda(lhs, codes, scales)
         sc = scales.view(torch.uint8) if scales.element_size() == 1 else scales
         g, n, k2 = codes.shape
@@ -391,6 +392,8 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
         return 3  # mma.sync kernel, 8-row token tiles
     if expected_rows <= 16:
         return 4  # mma.sync kernel, 16-row token tiles (one task per expert)
+    if expected_rows >= 224:
+        return 9  # tcgen05 on CTA pairs, tiles of up to 512 rows
     if expected_rows >= 128:
         return 8  # tcgen05 on CTA pairs, short group remainders on the mma.sync kernel
     return 1      # tcgen05 kernel, one CTA
@@ -437,9 +440,10 @@ class EPMoELayer:
         if self.overlap and weights.layout != "b200":
             raise ValueError("the overlapped exchange takes B200-layout weights")
         if self.overlap:  # the tcgen05 kernels carry the exchange hooks
-            self.variant = 7 if expected_rows >= 128 else 1
-            if gemm_variant is not None and int(gemm_variant) not in (1, 7):
-                raise ValueError("the overlapped exchange runs on variant 1 or 7")
+            if gemm_variant is None:
+                self.variant = 9 if expected_rows >= 224 else 7 if expected_rows >= 128 else 1
+            elif int(gemm_variant) not in (1, 7, 9):
+                raise ValueError("the overlapped exchange runs on variant 1, 7 or 9")
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
 
     kernels_per_forward = 5  # route, dispatch, 2 gmm, combine

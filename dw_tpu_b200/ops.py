@@ -60,8 +60,9 @@ def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
     ``variant`` 0 picks the kernel; 1 forces the tcgen05 kernel on one CTA,
     2-4 the mma.sync decode kernel (auto / 8 / 16-row token tiles), 7 the
     tcgen05 kernel on CTA pairs and 8 the pair kernel for each group's full
-    256-row tiles with short remainders on the decode kernel; 1-4, 7 and 8
-    need the B200 layout."""
+    256-row tiles with short remainders on the decode kernel, 9 the pair
+    kernel with tiles of up to 512 rows; 1-4 and 7-9 need the B200
+    layout."""
     L.require_cuda(lhs, codes, scales, group_sizes, out)
     if lhs.dtype != torch.bfloat16 or lhs.dim() != 2:
         raise ValueError("lhs must be a 2-D bf16 tensor")

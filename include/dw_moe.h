@@ -109,12 +109,16 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * size; 8 = the same kernel for each group's full 256-row tiles (and a last
  * tile of 96 rows or more), the mma.sync kernel for a shorter remainder,
  * which then costs one weight stream per 16 rows instead of a whole tile's
- * decode (the automatic choice for B200 codes whose groups average 128 rows
- * or more). 1-4, 7 and 8 need DWM_FP4_B200 codes; 5 and 6 are not
- * assigned. Every variant decodes the same bf16 weights and
- * accumulates in f32; results differ between variants only by f32 summation
- * order (1 and 7 give identical bits; 8 gives them on every group's first
- * 256 rows). Same reference interface as
+ * decode (the automatic choice for B200 codes whose groups average 128-223
+ * rows); 9 = 7 with tiles of up to 512 token rows: two UMMAs per k-step
+ * (N = 256 and the rest) into both 256-column TMEM accumulator slots over
+ * one decoded stage, so a group of 257-512 rows costs one tile's decode;
+ * tiles of up to 256 rows keep the two slots double-buffered (the automatic
+ * choice for B200 codes whose groups average 224 rows or more). 1-4 and 7-9
+ * need DWM_FP4_B200 codes; 5 and 6 are not assigned. Every variant decodes
+ * the same bf16 weights and accumulates in f32; results differ between
+ * variants only by f32 summation order (1, 7 and 9 give identical bits; 8
+ * gives them on every group's first 256 rows). Same reference interface as
  * dwm_gmm_fp4 (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
                         int scale_dtype, const int32_t* group_sizes, int num_groups, int m,
@@ -347,8 +351,8 @@ int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* t
                           int w_dtype, const void* shared, int shared_dtype, float routed_scale,
                           int mid_dtype, void* out, int out_dtype, int phases, void* stream);
 /* The overlapped form of the exchange (prefill): the grouped matmuls run on a
- * tcgen05 kernel (`variant` 1, one CTA, or 7, CTA pairs, as in
- * dwm_gmm_fp4_variant) with the exchange folded in,
+ * tcgen05 kernel (`variant` 1, one CTA, 7, CTA pairs, or 9, CTA pairs with
+ * 512-row tiles, as in dwm_gmm_fp4_variant) with the exchange folded in,
  * instead of the dispatch waiting for every row and the combine pulling every
  * output after the GEMMs.
  *   dwm_ep_dispatch(..., DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_GATED): stores

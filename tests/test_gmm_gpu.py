@@ -216,11 +216,12 @@ def test_b200_layout_dequant_and_gmm_match_e2m1(dw, sd):
 def test_pair_kernel_matches_single_cta(dw, sd):
     """The CTA-pair tcgen05 kernel (variant 7: M = 256 UMMAs over two SMs,
     double-buffered accumulators, groups above 256 rows split into equal
-    tiles) gives the single-CTA kernel's bits (the same decoded bf16 weights
-    and UMMA k order) for plain, SwiGLU, clamped SwiGLU and f32 outputs, on
-    ragged groups: empty, 1 row, below and above 128, exactly 256, 257 and
-    600 rows (2 and 3 tiles); also on a window of local groups with
-    zero_init."""
+    tiles; variant 9: tiles of up to 512 rows as two UMMAs per k-step) gives
+    the single-CTA kernel's bits (the same decoded bf16 weights and UMMA k
+    order) for plain, SwiGLU, clamped SwiGLU and f32 outputs, on ragged
+    groups: empty, 1 row, below and above 128, exactly 256, 257 and 600 rows
+    (2 and 3 tiles; 1 and 2 wide tiles); also on a window of local groups
+    with zero_init."""
     from dw_tpu_b200 import ops
     from dw_tpu_b200 import _lib as L
     lo, hi = (0, 140) if sd == "u8_wide" else (120, 140)
@@ -246,7 +247,7 @@ def test_pair_kernel_matches_single_cta(dw, sd):
                                   (L.ACT_SWIGLU_CLAMP, 256, torch.float32, 0.5),
                                   (L.ACT_NONE, 512, torch.float32, 0.0)):
         outs = []
-        for variant in (1, 7):
+        for variant in (1, 7, 9):
             o = torch.full((m, n_out), float("nan"), dtype=dt, device="cuda")
             ops.gmm_fp4_out(x, b200, sc, g, o, act=act, act_limit=limit, layout="b200",
                             variant=variant)
@@ -254,6 +255,7 @@ def test_pair_kernel_matches_single_cta(dw, sd):
         torch.cuda.synchronize()
         L.raise_on_device_error()
         assert torch.equal(bits(outs[0]), bits(outs[1])), (act, dt)
+        assert torch.equal(bits(outs[0]), bits(outs[2])), (act, dt, "wide")
         if act != L.ACT_SWIGLU_CLAMP:
             kind = "swiglu" if act == L.ACT_SWIGLU else None
             r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind,
@@ -263,7 +265,7 @@ def test_pair_kernel_matches_single_cta(dw, sd):
                               r32, 256, rows=v)
     # Local groups 2..5 of 8 (rows 1..659), rows outside zeroed.
     wins = []
-    for variant in (1, 7):
+    for variant in (1, 7, 9):
         o = torch.full((m, 256), float("nan"), dtype=torch.bfloat16, device="cuda")
         ops.gmm_fp4_out(x, b200[2:6], sc[2:6], g, o, group_offset=2, num_local_groups=4,
                         act=L.ACT_SWIGLU, zero_init=True, layout="b200", variant=variant)
@@ -271,6 +273,7 @@ def test_pair_kernel_matches_single_cta(dw, sd):
     torch.cuda.synchronize()
     L.raise_on_device_error()
     assert torch.equal(bits(wins[0]), bits(wins[1]))
+    assert torch.equal(bits(wins[0]), bits(wins[2]))
     w = to_np(wins[1])
     assert np.all(w[:1] == 0) and np.all(w[660:] == 0)
 
@@ -354,7 +357,7 @@ def test_gmm_prefill_tiles(dw, layout):
     for act, kind, n_out in ((L.ACT_NONE, None, 512), (L.ACT_SWIGLU, "swiglu", 256)):
         r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind)
         r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
-        for variant in ((0, 1, 7, 8) if layout == "b200" else (0,)):
+        for variant in ((0, 1, 7, 8, 9) if layout == "b200" else (0,)):
             out = torch.full((m, n_out), 5.0, dtype=torch.bfloat16, device="cuda")
             ops.gmm_fp4_out(np_to_bf16(lhs), codes, sc, g, out, act=act, zero_init=True,
                             layout=layout, variant=variant)

@@ -97,10 +97,11 @@ def test_layer_graph_capture_replays_bitwise(dw):
 
 def test_layer_prefill_pair_kernel(dw):
     """A prefill-sized layer (512 tokens, top-8 over 16 experts: ~256 rows
-    per expert) takes the GEMM on CTA pairs automatically (variant 8, short
-    group remainders on the decode kernel): it replays bitwise from a CUDA
-    graph and matches the oracle layer; the pair kernel alone (variant 7) has
-    the single-CTA kernel's bits."""
+    per expert) takes the GEMM on CTA pairs with 512-row tiles automatically
+    (variant 9): it replays bitwise from a CUDA graph, matches the oracle
+    layer and has the single-CTA kernel's bits, as does the pair kernel with
+    256-row tiles (variant 7); variant 8 (256-row pair tiles, short group
+    remainders on the decode kernel) matches the oracle layer."""
     from dw_tpu_b200 import synthetic
     t, e, h, i, k = 512, 16, 512, 256, 8
     w = synthetic.moe_weights(e, h, i, seed=8, device="cuda")
@@ -113,16 +114,19 @@ def test_layer_prefill_pair_kernel(dw):
     lc = (x.float() @ router.float()).to(torch.bfloat16).cuda()
     auto = dw.MoELayer(w, k, t)
     pair = dw.MoELayer(w, k, t, gemm_variant=7)
+    tails = dw.MoELayer(w, k, t, gemm_variant=8)
     single = dw.MoELayer(w, k, t, gemm_variant=1)
     out = auto(xc, lc)
     out_pair = pair(xc, lc)
+    out_tails = tails(xc, lc)
     ref_bits = single(xc, lc)
     torch.cuda.synchronize()
     from dw_tpu_b200 import _lib
     _lib.raise_on_device_error()
     assert int(auto.group_sizes.float().mean().item()) >= 128
-    assert int(auto.group_sizes.max().item()) > 256  # a remainder for the decode kernel
+    assert int(auto.group_sizes.max().item()) > 256  # two UMMAs per k-step / a remainder
     assert torch.equal(out_pair.view(torch.int16), ref_bits.view(torch.int16))
+    assert torch.equal(out.view(torch.int16), ref_bits.view(torch.int16))
     res = torch.empty_like(out)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -139,6 +143,7 @@ def test_layer_prefill_pair_kernel(dw):
     ref = O.fused_moe(bf16_to_np(x), bf16_to_np(lc.cpu()), raw.w13.cpu().numpy(),
                       raw.s13.cpu().numpy(), raw.w2.cpu().numpy(), raw.s2.cpu().numpy(), k)
     assert rel_fro(bf16_to_np(out), ref) < 2 * gemm_rel_tol(h)
+    assert rel_fro(bf16_to_np(out_tails), ref) < 2 * gemm_rel_tol(h)
 
 
 @pytest.mark.parametrize("layout,f32_reduce,limit", [("e2m1", False, None), ("b200", True, None),
