@@ -29,8 +29,8 @@
 //   warp  5     pair TMEM allocation; UMMA issuer in the even CTA (the whole
 //               warp runs the loop so its operands stay warp-uniform, one
 //               elected lane issues: a UMMA takes ~100 cycles to issue)
-//   warp  6     TMA: this CTA's half of the token rows (L2-resident)
-//   warps 8-23  decode, two groups of 8 on alternate stages
+//   warps 6-7   TMA: this CTA's half of the token rows (L2-resident)
+//   warps 8-23  decode, groups of warps taking the stages in turn
 //
 // A pipeline stage holds one 64-k step of both operands (the decoded A and
 // this CTA's token rows) behind one "full" barrier in the even CTA, so the
@@ -58,9 +58,20 @@ constexpr int NUM_THREADS = 768;
 constexpr int EPI_WARPS = 4;
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
-constexpr int TOKEN_WARP = 6;
+constexpr int TOKEN_WARP = 6;   // token copies of even index in a stage's list
+constexpr int TOKEN_WARP2 = 7;  // and of odd index
 constexpr int DEC_WARP0 = 8;
-constexpr int NUM_DEC_WARPS = 8;  // per group; two groups
+#ifndef DWM_PAIR_DEC_GROUPS
+#define DWM_PAIR_DEC_GROUPS 2
+#endif
+#ifndef DWM_PAIR_DEC_SYNC
+#define DWM_PAIR_DEC_SYNC 0
+#endif
+constexpr int DEC_WARPS = 16;                       // decode warps per CTA
+constexpr int DEC_GROUPS = DWM_PAIR_DEC_GROUPS;      // groups taking stages in turn
+constexpr int NUM_DEC_WARPS = DEC_WARPS / DEC_GROUPS;  // per group
+constexpr int BLOCKS_PER_WARP = 8 / NUM_DEC_WARPS;     // 16-column code blocks per warp
+static_assert(DEC_GROUPS == 2 || DEC_GROUPS == 4, "2 or 4 decode groups");
 constexpr int MAX_GROUPS = 1024;
 constexpr int TMEM_COLS = 512;    // two 256-column accumulator buffers
 constexpr int ACC_COLS = 256;
@@ -100,7 +111,7 @@ struct Layout {
   static constexpr int OFF_BAR = OFF_S + CS * S_STAGE;
   static constexpr int NUM_BARS = 2 * CS + 2 * S + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int OFF_ROWS = OFF_MISC + 32;
+  static constexpr int OFF_ROWS = OFF_MISC + 64;
   static constexpr int OFF_TILES = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int OFF_EPI = (OFF_TILES + (MAX_GROUPS + 1) * 4 + 15) & ~15;
   static constexpr int BYTES = OFF_EPI + EPI_WARPS * EPI_WARP_BYTES;
@@ -143,20 +154,32 @@ __device__ __forceinline__ int group_tiles(int rows, int bt, int tail_min) {
   return rows / bt + (rows % bt >= tail_min ? 1 : 0);
 }
 
+// A group whose tiles exceed 256 rows (WIDE kernel, equal-size tiles): two
+// UMMAs per k-step.
+__device__ __forceinline__ bool wide_group(int rows, const Args& a) {
+  if (a.max_rows <= BT || a.tail_min > 0 || rows <= BT) return false;
+  const int nt = (rows + a.max_rows - 1) / a.max_rows;
+  return (rows + nt - 1) / nt > BT;
+}
+
+// tile_prefix entries: first tile index (low kTileBits) | local group above.
+constexpr int kTileBits = 21;
+constexpr int kTileMask = (1 << kTileBits) - 1;
+
 __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const int* tile_prefix,
                                          const Args& a) {
-  int lo = 0, hi = a.n_local;  // tile_prefix[lo] <= idx < tile_prefix[hi]
+  int lo = 0, hi = a.n_local;  // first tile of position lo <= idx < that of position hi
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (tile_prefix[mid] <= idx) lo = mid; else hi = mid;
+    if ((tile_prefix[mid] & kTileMask) <= idx) lo = mid; else hi = mid;
   }
   Tile t;
-  t.g = lo;
-  const int local = idx - tile_prefix[lo];
+  t.g = tile_prefix[lo] >> kTileBits;
+  const int local = idx - (tile_prefix[lo] & kTileMask);
   const int t_idx = local / a.n_tiles;
   t.n_idx = local - t_idx * a.n_tiles;
-  const int gs_start = row_start[a.group_offset + lo];
-  const int gs_rows = row_start[a.group_offset + lo + 1] - gs_start;
+  const int gs_start = row_start[a.group_offset + t.g];
+  const int gs_rows = row_start[a.group_offset + t.g + 1] - gs_start;
   const int bt = a.max_rows;
   if (a.tail_min > 0) {
     t.row0 = gs_start + t_idx * bt;
@@ -173,8 +196,9 @@ __device__ __forceinline__ Tile get_tile(int idx, const int* row_start, const in
 
 // The two 256-column TMEM accumulator slots. A tile of up to 256 rows takes
 // the next slot and the one after alternates; a WIDE tile of more rows takes
-// both (rows 0-255 in the next slot, the rest in the other) and leaves the
-// pointer where it was, since the epilogue drains that slot first. The UMMA
+// both (rows 0-255 in the next slot sa, the rest in the other, sb). Its
+// epilogue drains sb first (at most 256 rows, often a few chunks) and the
+// next tile starts in sb, so it waits for that short drain only. The UMMA
 // issuer and the epilogue walk the same tile sequence with a ring each; par
 // bit s is the phase parity of slot s's next fill.
 struct AccRing {
@@ -187,7 +211,12 @@ struct AccRing {
     pa = (par >> sa) & 1u;
     pb = (par >> sb) & 1u;
     par ^= 1u << sa;
-    if (both) par ^= 1u << sb; else nxt ^= 1;
+    if (both) {
+      par ^= 1u << sb;
+      nxt = sb;
+    } else {
+      nxt ^= 1;
+    }
   }
 };
 
@@ -199,13 +228,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 }
 
 // A decode group's wait for its next stage (codes landed, stage released by
-// the pair's UMMAs): the group's first warp polls, the other seven park on
-// named barrier 1 + grp. The outcome is double-buffered by step parity.
+// the pair's UMMAs). DWM_PAIR_DEC_SYNC 0 (default): every warp polls for
+// itself, so the group's warps drift apart within a stage (10% faster on
+// 256-row tiles); 1: the group's first warp polls, the others park on named
+// barrier 1 + grp, and the outcome is double-buffered by the group's step
+// parity (3% faster on tiles of 16-32 rows).
 __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint64_t* full,
                                            uint32_t full_ph, uint64_t* empty, uint32_t empty_ph,
                                            volatile int* abort_flag, volatile int* go,
                                            int* status) {
-  volatile int* slot = go + grp * 2 + ((step >> 1) & 1);
+  if (DWM_PAIR_DEC_SYNC == 0) {
+    bool got = mbar_wait(full, full_ph, abort_flag, status);
+    got = got && mbar_wait(empty, empty_ph, abort_flag, status);
+    return __all_sync(0xffffffffu, got);
+  }
+  volatile int* slot = go + grp * 2 + ((step / DEC_GROUPS) & 1);
   if (dw == 0) {
     bool got = mbar_wait(full, full_ph, abort_flag, status);
     got = got && mbar_wait(empty, empty_ph, abort_flag, status);
@@ -219,6 +256,8 @@ __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint6
 template <int SD, bool WIDE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_pair_kernel(const __grid_constant__ CUtensorMap tm_lhs,
+                    const __grid_constant__ CUtensorMap tm_lhs_32,
+                    const __grid_constant__ CUtensorMap tm_lhs_64,
                     const __grid_constant__ CUtensorMap tm_lhs_half,
                     const __grid_constant__ CUtensorMap tm_codes,
                     const __grid_constant__ CUtensorMap tm_scales, const Args a) {
@@ -237,7 +276,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain_bar = acc_empty + 2;  // each CTA: every UMMA complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  volatile int* group_go = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 16);  // [2][2]
+  volatile int* group_go = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 16);  // [4][2]
   int* row_start = reinterpret_cast<int*>(smem + L::OFF_ROWS);
   int* tile_prefix = reinterpret_cast<int*>(smem + L::OFF_TILES);
 
@@ -253,9 +292,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&cs_empty[i], NUM_DEC_WARPS);
     }
     for (int i = 0; i < S; ++i) {
-      // Decode warps of both CTAs, plus the even CTA's expect_tx for the
-      // token bytes of both halves.
-      mbar_init(&full[i], 2 * NUM_DEC_WARPS + 1);
+      // Decode warps of both CTAs, the even CTA's expect_tx for the token
+      // bytes of both halves, and TOKEN_WARP2 of both CTAs.
+      mbar_init(&full[i], 2 * NUM_DEC_WARPS + 3);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -268,6 +307,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   if (warp == PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tm_lhs);
+    tma_prefetch_desc(&tm_lhs_32);
+    tma_prefetch_desc(&tm_lhs_64);
     tma_prefetch_desc(&tm_lhs_half);
     tma_prefetch_desc(&tm_codes);
     tma_prefetch_desc(&tm_scales);
@@ -306,15 +347,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (run > a.m) report(a.status, DWM_DEV_BAD_INDEX);
     }
     __syncwarp();
+    // Local groups in schedule order: those with a tile above 256 rows (two
+    // UMMAs per k-step, the costliest tiles) first, so that the round-robin
+    // assignment of tiles to clusters spreads them evenly. tile_prefix[i] =
+    // first tile of the i-th group in that order | its group << kTileBits.
     const int NL = a.n_local;
     const int per2 = (NL + 31) / 32;
-    int tsum = 0;
+    auto rows_of = [&](int g) {
+      return row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
+    };
+    int nwide = 0;
     for (int i = 0; i < per2; ++i) {
       const int g = lane * per2 + i;
-      if (g < NL) {
-        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        tsum += group_tiles(rows, a.max_rows, a.tail_min) * a.n_tiles;
-      }
+      if (g < NL && wide_group(rows_of(g), a)) ++nwide;
+    }
+    int wincl = nwide;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wincl, o);
+      if (lane >= o) wincl += y;
+    }
+    const int wide_total = __shfl_sync(0xffffffffu, wincl, 31);
+    int wpos = wincl - nwide;                           // next wide position
+    int npos = wide_total + lane * per2 - (wincl - nwide);  // next narrow position
+    for (int i = 0; i < per2; ++i) {
+      const int g = lane * per2 + i;
+      if (g < NL) tile_prefix[wide_group(rows_of(g), a) ? wpos++ : npos++] = g;
+    }
+    __syncwarp();
+    int tsum = 0;
+    for (int i = 0; i < per2; ++i) {
+      const int pos = lane * per2 + i;
+      if (pos < NL) tsum += group_tiles(rows_of(tile_prefix[pos]), a.max_rows, a.tail_min) * a.n_tiles;
     }
     int tincl = tsum;
 #pragma unroll
@@ -324,11 +388,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     int trun = tincl - tsum;
     for (int i = 0; i < per2; ++i) {
-      const int g = lane * per2 + i;
-      if (g < NL) {
-        tile_prefix[g] = trun;
-        const int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        trun += group_tiles(rows, a.max_rows, a.tail_min) * a.n_tiles;
+      const int pos = lane * per2 + i;
+      if (pos < NL) {
+        const int g = tile_prefix[pos];
+        tile_prefix[pos] = trun | (g << kTileBits);
+        trun += group_tiles(rows_of(g), a.max_rows, a.tail_min) * a.n_tiles;
       }
     }
     if (lane == 31) tile_prefix[NL] = trun;
@@ -382,17 +446,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
       const uint32_t ta = tq + (uint32_t)(sa * ACC_COLS), tb = tq + (uint32_t)(sb * ACC_COLS);
-      // Chunk c of 16 token rows: rows 0-255 in slot sa, the rest in sb.
+      // Chunk c of 16 token rows: rows 0-255 in slot sa, the rest in sb. A
+      // two-slot tile drains chunks 16.. (slot sb) first: step ci takes
+      // chunk chunk_of(ci), and sb is free once its chunks are in registers.
+      const int nchunks = (t.rows + 15) >> 4;
+      const int n_sb = both ? nchunks - 16 : 0;
+      auto chunk_of = [&](int ci) { return ci < n_sb ? 16 + ci : ci - n_sb; };
       auto chunk_addr = [&](int c) { return (c < 16 ? ta : tb) + (uint32_t)((c & 15) * 16); };
-      // Slot sa of a two-slot tile is free once its 16 chunks are in registers.
-      auto release_first = [&](int c) {
-        if (both && c == 15) {
+      auto release_first = [&](int ci) {
+        if (ci == n_sb - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(sa * 8));
+          if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(sb * 8));
         }
       };
-      const int nchunks = (t.rows + 15) >> 4;
       if (act) {
         // Lanes 0-15 hold the gate, lanes 16-31 the up column of features
         // fcol + (lane & 15); lane < 16 forms the even tokens of a chunk,
@@ -400,11 +467,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int64_t fcol = (int64_t)t.n_idx * 128 + rank * 64 + q * 16;
         const int row_bytes = 16 * es;  // one staged token row: 16 features
         const int vpr = row_bytes / 16;
-        for (int c = 0; c < nchunks; ++c) {
+        for (int ci = 0; ci < nchunks; ++ci) {
+          const int c = chunk_of(ci);
           uint32_t r[16];
           tmem_ld16(chunk_addr(c), r);
           tmem_ld_wait();
-          release_first(c);
+          release_first(ci);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float even = __uint_as_float(r[2 * e]) * acc_scale;
@@ -439,11 +507,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int64_t ccol = (int64_t)t.n_idx * 256 + rank * 128 + q * 32;
         const int row_bytes = 32 * es;  // one staged token row: 32 columns
         const int vpr = row_bytes / 16;
-        for (int c = 0; c < nchunks; ++c) {
+        for (int ci = 0; ci < nchunks; ++ci) {
+          const int c = chunk_of(ci);
           uint32_t r[16];
           tmem_ld16(chunk_addr(c), r);
           tmem_ld_wait();
-          release_first(c);
+          release_first(ci);
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const float v = __uint_as_float(r[e]) * acc_scale;
@@ -479,7 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)((both ? sb : sa) * 8));
+      if (lane == 0) mbar_arrive_remote(acc_empty_0 + (uint32_t)(sa * 8));
     }
   } else if (warp == PRODUCER_WARP) {
     // ---------------- TMA producer: codes + scales (HBM stream) ----------------
@@ -513,13 +582,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int s = 0; s < CS; ++s)
         if (cs_armed & (1u << s)) mbar_wait(&cs_full[s], (cs_par >> s) & 1, nullptr, a.status);
     }
-  } else if (warp == TOKEN_WARP) {
-    // ---------------- TMA producer: this CTA's token rows ----------------
+  } else if (warp == TOKEN_WARP || warp == TOKEN_WARP2) {
+    // ---------------- TMA producers: this CTA's token rows ----------------
     // A tile's N rows are UMMA 1's first min(N, 256) and (WIDE) UMMA 2's rest;
     // this CTA loads its half of each part, the second 16 KiB after the
-    // first. A full half (128 rows) is one box; a partial one nb boxes of 16
-    // rows.
+    // first. A full half (128 rows) is one copy, a partial one of nb boxes of
+    // 16 rows at most three (64 + 32 + 16 rows). A copy costs its issuing
+    // thread about 300 cycles, so two warps split a stage's copies (even and
+    // odd positions in the list); TOKEN_WARP also arms the stage's bytes.
+    // TOKEN_WARP2 arrives on every stage, with copies or without: a waiter
+    // that no barrier waits for could fall a whole phase behind its stage's
+    // barrier and then wait on a parity that has already passed.
     if (lane == 0) {
+      const int which = warp - TOKEN_WARP;
       const uint64_t pol_keep = policy_evict_last();
       int st = 0;
       uint32_t ph = 0, armed = 0, par = 0;
@@ -548,27 +623,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          if (rank == 0)
+          if (rank == 0 && which == 0)
             mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * (nb1 + nb2) * T_BOX_BYTES));
           armed |= 1u << st;
           par = (par & ~(1u << st)) | (ph << st);
           const uint32_t bar0 = full_0 + (uint32_t)(st * 8);
           uint8_t* tdst = smem + L::OFF_STAGE + st * L::STG + A_STAGE;
+          int ci = 0;  // position of the next copy in the stage's list
+          auto copy = [&](uint8_t* dst, const CUtensorMap* map, int row) {
+            if ((ci++ & 1) == which) tma_load_2d_pair(dst, map, bar0, kk * BK, row, pol_keep);
+          };
           auto load_part = [&](uint8_t* dst, int nb, int rbase) {
             if (nb == HALF / T_BOX_ROWS) {
-              tma_load_2d_pair(dst, &tm_lhs_half, bar0, kk * BK, rbase, pol_keep);
-            } else {
-              for (int bx = 0; bx < nb; ++bx)
-                tma_load_2d_pair(dst + bx * T_BOX_BYTES, &tm_lhs, bar0, kk * BK,
-                                 rbase + bx * T_BOX_ROWS, pol_keep);
+              copy(dst, &tm_lhs_half, rbase);
+              return;
             }
+            int bx = 0;
+            if (nb & 4) {
+              copy(dst, &tm_lhs_64, rbase);
+              bx += 4;
+            }
+            if (nb & 2) {
+              copy(dst + bx * T_BOX_BYTES, &tm_lhs_32, rbase + bx * T_BOX_ROWS);
+              bx += 2;
+            }
+            if (nb & 1) copy(dst + bx * T_BOX_BYTES, &tm_lhs, rbase + bx * T_BOX_ROWS);
           };
           load_part(tdst, nb1, rbase1);
           if (WIDE && nb2 > 0) load_part(tdst + T_STAGE, nb2, rbase2);
+          if (which == 1) mbar_arrive_remote(bar0);
           if (++st == S) { st = 0; ph ^= 1; }
         }
       }
-      // Every stage this CTA filled is released by the pair's UMMAs (so its
+      // Every stage this warp filled is released by the pair's UMMAs (so its
       // copies have landed) before the CTA can exit.
       for (int i = 0; i < S; ++i)
         if (armed & (1u << i)) mbar_wait(&empty[i], (par >> i) & 1, nullptr, a.status);
@@ -638,27 +725,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) mbar_wait(drain_bar, 0, nullptr, a.status);
   } else if (warp >= DEC_WARP0) {
     // ---------------- decode ----------------
-    // Two groups of 8 warps take alternate stages. Warp dw decodes code
-    // block dw (16 weight columns) of the stage: lane l decodes word l of
-    // each of its 4 k-blocks (columns gid, gid+8 of the block, k pairs t,
-    // t+4) into A rows p*16 + gid and + 8, where the row block p puts gate
-    // block j next to up block j with SwiGLU.
+    // DEC_GROUPS groups of NUM_DEC_WARPS warps take the stages in turn. Warp
+    // dw of a group decodes code blocks dw + NUM_DEC_WARPS * i (16 weight
+    // columns each) of its stage: lane l decodes word l of each of a block's
+    // 4 k-blocks (columns gid, gid+8 of the block, k pairs t, t+4) into A
+    // rows p*16 + gid and + 8, where the row block p puts gate block j next to
+    // up block j with SwiGLU.
     const int grp = (warp - DEC_WARP0) / NUM_DEC_WARPS;
     const int dw = (warp - DEC_WARP0) % NUM_DEC_WARPS;
     constexpr int es = ScaleTraits<SD>::bytes;
     constexpr int DELTA = decode_delta<SD>();
-    const int b = dw;
-    const int p = act ? 2 * (b & 3) + (b >> 2) : b;
     const int gid = lane >> 2, tig = lane & 3;
     const DecodeRegs dregs = DecodeRegs::make();  // decode constants held in registers
-    const int r0 = 16 * p + gid;  // A rows r0 and r0 + 8
-    const int row_a_off = (r0 >> 3) * 1024 + (r0 & 7) * 128;
-    const int row_b_off = ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
     uint32_t step = 0;
     bool ok = true;
     for (int idx = cl; idx < total && ok; idx += ncl) {
       for (int kk = 0; kk < KT; ++kk, ++step) {
-        if ((int)(step & 1) != grp) continue;
+        if ((int)(step % DEC_GROUPS) != grp) continue;
         const int cs = (int)(step % CS);
         const uint32_t cs_ph = (step / CS) & 1;
         const int st = (int)(step % S);
@@ -668,55 +751,65 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
         const uint8_t* sstage = smem + L::OFF_S + cs * L::S_STAGE;
         uint8_t* astage = smem + L::OFF_STAGE + st * L::STG;
-        // The four lanes of a quad (same gid) need the same four scales: k32
-        // half h, column gid + 8c. Lane tig converts scale (h, c) = (tig >> 1,
-        // tig & 1) and the quad exchanges the multipliers.
-        uint32_t m1s, m2s;
-        const bool two = col_mult<SD, DELTA>(
-            sstage + ((tig >> 1) * ROWS + 16 * b + gid + 8 * (tig & 1)) * es, m1s, m2s);
-        const bool two_any = __any_sync(0xffffffffu, two);
-        uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int bi = 0; bi < BLOCKS_PER_WARP; ++bi) {
+          const int b = dw + NUM_DEC_WARPS * bi;
+          const int p = act ? 2 * (b & 3) + (b >> 2) : b;
+          const int r0 = 16 * p + gid;  // A rows r0 and r0 + 8
+          const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
+          // The codes' loads and table lookups first: they do not wait for
+          // the scale multipliers, whose loads and shuffles then overlap them.
+          uint32_t tv[4][4];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int src = (lane & ~3) + 2 * h + c;
-            if (two_any) {  // both multiplies: 2^(126 - delta), then the scale
-              m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
-              m2[h][c] = __shfl_sync(0xffffffffu, m2s, src);
-            } else {
-              m1[h][c] = __shfl_sync(0xffffffffu, m1s, src);
-              m2[h][c] = 0u;
+          for (int kb = 0; kb < 4; ++kb)
+            tvals_b200(*reinterpret_cast<const uint32_t*>(cstage + kb * 128 + lane * 4), dregs,
+                       tv[kb]);
+          // The four lanes of a quad (same gid) need the same four scales:
+          // k32 half h, column gid + 8c. Lane tig converts scale (h, c) =
+          // (tig >> 1, tig & 1) and the quad exchanges the multipliers.
+          uint32_t m1s, m2s;
+          const bool two = col_mult<SD, DELTA>(
+              sstage + ((tig >> 1) * ROWS + 16 * b + gid + 8 * (tig & 1)) * es, m1s, m2s);
+          const bool two_any = __any_sync(0xffffffffu, two);
+          uint32_t m1[2][2], m2[2][2];  // [k32 half][column gid / gid+8]
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int src = (lane & ~3) + 2 * h + c;
+              if (two_any) {  // both multiplies: 2^(126 - delta), then the scale
+                m1[h][c] = pow2_126_minus_delta_x2<DELTA>();
+                m2[h][c] = __shfl_sync(0xffffffffu, m2s, src);
+              } else {
+                m1[h][c] = __shfl_sync(0xffffffffu, m1s, src);
+                m2[h][c] = 0u;
+              }
             }
-          }
-        uint8_t* row_a = astage + row_a_off;
-        uint8_t* row_b = astage + row_b_off;
+          uint8_t* row_a = astage + (r0 >> 3) * 1024 + (r0 & 7) * 128;
+          uint8_t* row_b = astage + ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(cstage + kb * 128 + lane * 4);
-          uint32_t tv[4];
-          tvals_b200(w, dregs, tv);
-          const int h = kb >> 1;
-          uint32_t v0 = hmul2_bf16(tv[0], m1[h][0]);
-          uint32_t v1 = hmul2_bf16(tv[1], m1[h][1]);
-          uint32_t v2 = hmul2_bf16(tv[2], m1[h][0]);
-          uint32_t v3 = hmul2_bf16(tv[3], m1[h][1]);
-          if (two_any) {
-            v0 = hmul2_bf16(v0, m2[h][0]);
-            v1 = hmul2_bf16(v1, m2[h][1]);
-            v2 = hmul2_bf16(v2, m2[h][0]);
-            v3 = hmul2_bf16(v3, m2[h][1]);
+          for (int kb = 0; kb < 4; ++kb) {
+            const int h = kb >> 1;
+            uint32_t v0 = hmul2_bf16(tv[kb][0], m1[h][0]);
+            uint32_t v1 = hmul2_bf16(tv[kb][1], m1[h][1]);
+            uint32_t v2 = hmul2_bf16(tv[kb][2], m1[h][0]);
+            uint32_t v3 = hmul2_bf16(tv[kb][3], m1[h][1]);
+            if (two_any) {
+              v0 = hmul2_bf16(v0, m2[h][0]);
+              v1 = hmul2_bf16(v1, m2[h][1]);
+              v2 = hmul2_bf16(v2, m2[h][0]);
+              v3 = hmul2_bf16(v3, m2[h][1]);
+            }
+            // k pair (16 kb + 2 tig) sits in 16-byte chunk 2 kb, k pair
+            // (16 kb + 2 tig + 8) in chunk 2 kb + 1, both at byte 4 tig.
+            const int c0 = 2 * kb, c1 = 2 * kb + 1;
+            *reinterpret_cast<uint32_t*>(row_a + ((c0 ^ (r0 & 7)) << 4) + 4 * tig) = v0;
+            *reinterpret_cast<uint32_t*>(row_b + ((c0 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v1;
+            *reinterpret_cast<uint32_t*>(row_a + ((c1 ^ (r0 & 7)) << 4) + 4 * tig) = v2;
+            *reinterpret_cast<uint32_t*>(row_b + ((c1 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v3;
           }
-          // k pair (16 kb + 2 tig) sits in 16-byte chunk 2 kb, k pair
-          // (16 kb + 2 tig + 8) in chunk 2 kb + 1, both at byte 4 tig.
-          const int c0 = 2 * kb, c1 = 2 * kb + 1;
-          *reinterpret_cast<uint32_t*>(row_a + ((c0 ^ (r0 & 7)) << 4) + 4 * tig) = v0;
-          *reinterpret_cast<uint32_t*>(row_b + ((c0 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v1;
-          *reinterpret_cast<uint32_t*>(row_a + ((c1 ^ (r0 & 7)) << 4) + 4 * tig) = v2;
-          *reinterpret_cast<uint32_t*>(row_b + ((c1 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v3;
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -780,10 +873,19 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   using L = Layout<SD, WIDE>;
   constexpr int es = ScaleTraits<SD>::bytes;
   const bool act_on = act != DWM_ACT_NONE;
-  CUtensorMap tm_lhs, tm_lhs_half, tm_codes, tm_scales;
+  // Tile indices fit the low kTileBits of a tile_prefix entry.
+  DWM_CHECK_ARG((int64_t)(m / BT + n_local + 1) * (n / 256) < (int64_t)kTileMask,
+                "m=%d rows over n=%d columns exceed the pair kernel's tile count", m, n);
+  CUtensorMap tm_lhs, tm_lhs_32, tm_lhs_64, tm_lhs_half, tm_codes, tm_scales;
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
                           (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tm_lhs_32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
+                      (uint64_t)m, (uint64_t)k * 2, BK, 2 * T_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tm_lhs_64, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
+                      (uint64_t)m, (uint64_t)k * 2, BK, 4 * T_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_tmap_2d(&tm_lhs_half, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
                       (uint64_t)m, (uint64_t)k * 2, BK, HALF, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -843,7 +945,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3(2 * (unsigned)max_pairs<SD, WIDE>(cfg));
-  return check_cuda(cudaLaunchKernelEx(&cfg, gmm_pair_kernel<SD, WIDE>, tm_lhs, tm_lhs_half, tm_codes,
+  return check_cuda(cudaLaunchKernelEx(&cfg, gmm_pair_kernel<SD, WIDE>, tm_lhs, tm_lhs_32, tm_lhs_64, tm_lhs_half, tm_codes,
                                        tm_scales, a),
                     "gmm_pair launch");
 }

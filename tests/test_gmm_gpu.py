@@ -278,6 +278,32 @@ def test_pair_kernel_matches_single_cta(dw, sd):
     assert np.all(w[:1] == 0) and np.all(w[660:] == 0)
 
 
+def test_pair_kernel_many_short_tiles(dw):
+    """Many short pair tiles per cluster (128 groups of 17-48 rows, 32 k-steps
+    each): every role of the pipeline keeps pace with every stage barrier's
+    phases (a waiter that falls a phase behind would time out), three
+    launches in a row, with the single-CTA kernel's bits."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    rng = np.random.default_rng(33)
+    sizes = rng.integers(17, 49, 128)
+    m = int(sizes.sum())
+    lhs, packed, scales, gs = _case(34, m, 2048, 1024, len(sizes), gs=sizes)
+    b200 = ops.fp4_to_b200_out(torch.from_numpy(packed).cuda())
+    sc = torch.from_numpy(scales).cuda()
+    x = np_to_bf16(lhs)
+    g = torch.from_numpy(gs).cuda()
+    ref = torch.empty((m, 1024), dtype=torch.bfloat16, device="cuda")
+    ops.gmm_fp4_out(x, b200, sc, g, ref, layout="b200", variant=1)
+    for variant in (7, 9):
+        for _ in range(3):
+            o = torch.full((m, 1024), float("nan"), dtype=torch.bfloat16, device="cuda")
+            ops.gmm_fp4_out(x, b200, sc, g, o, layout="b200", variant=variant)
+            torch.cuda.synchronize()
+            L.raise_on_device_error()
+            assert torch.equal(o.view(torch.int16), ref.view(torch.int16)), variant
+
+
 @pytest.mark.parametrize("gs,k,act,limit,sd,out_dt", [
     ([1, 0, 2, 3, 5, 8, 0, 7], 192, None, None, "u8", "bf16"),        # <= 8 rows: one n8 tile
     ([9, 16, 11, 0, 14, 3, 12, 15], 256, None, None, "u8", "f32"),    # 9-16 rows: two n8 tiles
