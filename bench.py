@@ -695,6 +695,7 @@ def link_peak(dev, world, rank, ctx, mib=256, iters=5):
     import torch
     import torch.distributed as dist
     n = mib * 2**20
+    cn = min(n, ctx.capacity * ctx.hidden * 2)  # the peer copy stays inside the receive buffer
     src = torch.empty(n, dtype=torch.uint8, device=dev).fill_(1)
     dst = torch.empty(n, dtype=torch.uint8, device=dev)
     nxt, prv = (rank + 1) % world, (rank - 1) % world
@@ -722,7 +723,7 @@ def link_peak(dev, world, rank, ctx, mib=256, iters=5):
         torch.cuda.synchronize(dev)
         e0, e1 = events()
         e0.record()
-        ctx.link_probe(nxt, n)
+        ctx.link_probe(nxt, cn)
         e1.record()
         torch.cuda.synchronize(dev)
         if i >= 2:
@@ -730,12 +731,12 @@ def link_peak(dev, world, rank, ctx, mib=256, iters=5):
     dist.barrier()
     ms, cms = max_over_ranks([statistics.median(ts), statistics.median(cts)], world, dev)
     nccl_gbps = n / (ms * 1e-3) / 1e9
-    copy_gbps = n / (cms * 1e-3) / 1e9
+    copy_gbps = cn / (cms * 1e-3) / 1e9
     return {"GBps": round(max(nccl_gbps, copy_gbps), 1), "nccl_sendrecv_GBps": round(nccl_gbps, 1),
             "peer_copy_GBps": round(copy_gbps, 1),
-            "how": f"ring of {mib} MiB per rank each way: NCCL send/recv and a copy-engine copy "
-                   "into the peer's mapped buffer, median of 5, max over ranks; GBps = the "
-                   "larger"}
+            "how": f"ring of {mib} MiB per rank each way with NCCL send/recv, and a "
+                   f"copy-engine copy of {cn // 2**20} MiB into the peer's mapped receive "
+                   "buffer, median of 5, max over ranks; GBps = the larger"}
 
 
 def zipf_logits(ids, dev):
