@@ -269,11 +269,11 @@ def emulated_dispatch(ctxs: list[EPContext], hiddens, ids):
     return [(c.recv, c.recv_group_sizes) for c in ctxs]
 
 
-def emulated_combine(ctxs: list[EPContext], ys, weights, outs=None):
+def emulated_combine(ctxs: list[EPContext], ys, weights, outs=None, rank_order: bool = False):
     outs = outs or [None] * len(ctxs)
     for c, y, w in zip(ctxs, ys, weights):
         c.combine(y, w, None, phases=L.EP_PUSH)
-    return [c.combine(y, w, o, phases=L.EP_REDUCE)
+    return [c.combine(y, w, o, phases=L.EP_REDUCE, rank_order=rank_order)
             for c, y, w, o in zip(ctxs, ys, weights, outs)]
 
 
@@ -411,7 +411,7 @@ class EPMoELayer:
                  scoring_fn: str = "sigmoid", renormalize: bool = True,
                  act_limit: float | None = None, f32_reduce: bool = False,
                  expected_rows: float | None = None, overlap: bool = False,
-                 gemm_variant: int | None = None):
+                 gemm_variant: int | None = None, rank_order: bool = False):
         if weights.num_experts != ctx.local_experts:
             raise ValueError(f"weights hold {weights.num_experts} experts, the context "
                              f"{ctx.local_experts} per rank")
@@ -445,6 +445,12 @@ class EPMoELayer:
             elif int(gemm_variant) not in (1, 7, 9):
                 raise ValueError("the overlapped exchange runs on variant 1, 7 or 9")
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
+        # rank_order: the combine sums in the reference GMM_EP order (per-rank
+        # masked f32 partials, then ranks in order) instead of k order.
+        self.rank_order = bool(rank_order)
+        if self.rank_order and self.overlap:
+            raise ValueError("the rank-order combine pulls the peers' rows; the overlapped "
+                             "exchange pushes them")
 
     kernels_per_forward = 5  # route, dispatch, 2 gmm, combine
 
@@ -481,7 +487,7 @@ class EPMoELayer:
             return self.ctx.combine(self.y, w16, out, phases=self._COMBINE_OVERLAP)
         self.ctx.dispatch(hidden, ids)
         self._experts()
-        return self.ctx.combine(self.y, w16, out)
+        return self.ctx.combine(self.y, w16, out, rank_order=self.rank_order)
 
     __call__ = forward
 
@@ -511,4 +517,4 @@ class EPMoELayer:
         for ly in layers:
             ly._experts()
         return emulated_combine([ly.ctx for ly in layers], [ly.y for ly in layers],
-                                [r[1] for r in routed], outs)
+                                [r[1] for r in routed], outs, rank_order=layers[0].rank_order)

@@ -380,6 +380,54 @@ def test_ep_layer_matches_single_device_layer(ep, layout, t):
             c.close()
 
 
+def test_ep_layer_rank_order_combine(ep):
+    """EPMoELayer(rank_order=True) sums each token's expert outputs in the
+    reference GMM_EP order: its output has the bits of
+    oracle.ep_combine_rankorder on the layer's own expert outputs, routing and
+    weights, and stays within the GEMM tolerance of the k-order layer."""
+    import dw_tpu_b200 as dw
+    from dw_tpu_b200 import _lib as L
+    from dw_tpu_b200 import synthetic
+    from tests.gpu_util import gemm_rel_tol, rel_fro
+    world, e, h, i, k, t = 4, 16, 512, 256, 4, 24
+    w = synthetic.moe_weights(e, h, i, seed=41, device="cuda")
+    for name in ("s13", "s2"):
+        setattr(w, name, synthetic.random_e8m0(getattr(w, name).shape, 42, "cuda", lo=118,
+                                               hi=121))
+    w = w.to_b200()
+    le = e // world
+    ctx_r = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    ctx_k = ep.create_local_contexts(world, max_tokens=t, hidden=h, topk=k, num_experts=e)
+    try:
+        def shard(r):
+            return dw.FP4MoEWeights(w.w13[r * le:(r + 1) * le], w.s13[r * le:(r + 1) * le],
+                                    w.w2[r * le:(r + 1) * le], w.s2[r * le:(r + 1) * le], "b200")
+        lro = [ep.EPMoELayer(shard(r), ctx_r[r], k, rank_order=True) for r in range(world)]
+        lko = [ep.EPMoELayer(shard(r), ctx_k[r], k) for r in range(world)]
+        xs, lgs = [], []
+        for r in range(world):
+            x, router = synthetic.layer_inputs(t, h, e, seed=60 + r)
+            xs.append(x.cuda())
+            lgs.append((x.float() @ router.float()).to(torch.bfloat16).cuda())
+        a = ep.EPMoELayer.forward_emulated(lro, xs, lgs)
+        b = ep.EPMoELayer.forward_emulated(lko, xs, lgs)
+        torch.cuda.synchronize()
+        L.raise_on_device_error()
+        ids = [ly.ids[:t].cpu().numpy() for ly in lro]
+        wts = [ly.w16[:t].float().cpu().numpy() for ly in lro]
+        ref = O.ep_dispatch([bf16_to_np(x.cpu()) for x in xs], ids, e)
+        ys = [bf16_to_np(ly.y[:int(g[1].sum())].cpu()) for ly, g in zip(lro, ref)]
+        want = O.ep_combine_rankorder(ys, [g[2] for g in ref], wts, e, ids)
+        for r in range(world):
+            assert np.array_equal(bf16_to_np(a[r]), want[r]), r
+            assert rel_fro(bf16_to_np(a[r]), bf16_to_np(b[r])) < gemm_rel_tol(i), r
+        with pytest.raises(ValueError):
+            ep.EPMoELayer(shard(0), ctx_r[0], k, rank_order=True, overlap=True)
+    finally:
+        for c in ctx_r + ctx_k:
+            c.close()
+
+
 def test_ep_layer_full_size_matches_single_device(ep):
     """The cfg1 architecture (H=4096, I=2048, 256 FP4 experts, top-8 sigmoid)
     as an EP layer of 8 emulated ranks with 32 tokens each: every rank's output
