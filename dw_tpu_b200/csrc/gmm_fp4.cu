@@ -1033,9 +1033,11 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // kPairTailMin rows, the decode kernel for shorter remainders, 9 = 7 with
 // tiles of up to 512 rows (two UMMAs per k-step over one decoded stage).
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 16 rows, variant 8 from 128 rows and variant 9 from 224
+// average at most 16 rows, variant 7 from 96 rows and variant 9 from 224
 // (prefill; most groups then exceed 256 rows or come close), else the
-// single-CTA tcgen05 kernel with 128-row tiles.
+// single-CTA tcgen05 kernel with 128-row tiles. Variant 8 is not chosen
+// automatically: since the pair kernel loads a partial token half in at most
+// three copies, equal tiles (7) match it below 224 rows and 9 beats it above.
 static int run(const void* lhs, const void* codes, int codes_format, const void* scales,
                int scale_dtype, const int32_t* group_sizes, int num_groups, int m, int k, int n,
                int group_offset, int num_local_groups, int act, float act_limit, int out_dtype,
@@ -1053,7 +1055,7 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     variant = codes_format != DWM_FP4_B200 ? 1
               : avg <= 16                  ? 2
               : avg >= 224                 ? 9
-              : avg >= 128                 ? 8
+              : avg >= 96                  ? 7
                                            : 1;
   if (variant >= 2 && variant <= 4)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,

@@ -394,8 +394,8 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
         return 4  # mma.sync kernel, 16-row token tiles (one task per expert)
     if expected_rows >= 224:
         return 9  # tcgen05 on CTA pairs, tiles of up to 512 rows
-    if expected_rows >= 128:
-        return 8  # tcgen05 on CTA pairs, short group remainders on the mma.sync kernel
+    if expected_rows >= 96:
+        return 7  # tcgen05 on CTA pairs, tiles of up to 256 rows
     return 1      # tcgen05 kernel, one CTA
 
 
@@ -441,7 +441,7 @@ class EPMoELayer:
             raise ValueError("the overlapped exchange takes B200-layout weights")
         if self.overlap:  # the tcgen05 kernels carry the exchange hooks
             if gemm_variant is None:
-                self.variant = 9 if expected_rows >= 224 else 7 if expected_rows >= 128 else 1
+                self.variant = 9 if expected_rows >= 224 else 7 if expected_rows >= 96 else 1
             elif int(gemm_variant) not in (1, 7, 9):
                 raise ValueError("the overlapped exchange runs on variant 1, 7 or 9")
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16

@@ -98,7 +98,7 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
 
 /* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4),
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
- * automatic choice for groups averaging 17-127 rows),
+ * automatic choice for groups averaging 17-95 rows),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8-row token tiles up to 6 rows per group on average, 16-row tiles
  * above), 3 / 4 = the same with 8 / 16-row token tiles (2: the automatic
@@ -106,11 +106,11 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
  * double-buffered accumulators, a group above 256 rows in tiles of equal
- * size; 8 = the same kernel for each group's full 256-row tiles (and a last
+ * size (the automatic choice for B200 codes whose groups average 96-223
+ * rows); 8 = the same kernel for each group's full 256-row tiles (and a last
  * tile of 96 rows or more), the mma.sync kernel for a shorter remainder,
  * which then costs one weight stream per 16 rows instead of a whole tile's
- * decode (the automatic choice for B200 codes whose groups average 128-223
- * rows); 9 = 7 with tiles of up to 512 token rows: two UMMAs per k-step
+ * decode; 9 = 7 with tiles of up to 512 token rows: two UMMAs per k-step
  * (N = 256 and the rest) into both 256-column TMEM accumulator slots over
  * one decoded stage, so a group of 257-512 rows costs one tile's decode;
  * tiles of up to 256 rows keep the two slots double-buffered (the automatic

@@ -70,7 +70,8 @@ def test_gemm_variant_choice():
     assert gemm_variant("b200", 8) == 4
     assert gemm_variant("b200", 16) == 4
     assert gemm_variant("b200", 64) == 1
-    assert gemm_variant("b200", 128) == 8
+    assert gemm_variant("b200", 96) == 7
+    assert gemm_variant("b200", 128) == 7
     assert gemm_variant("b200", 256) == 9
 
 
