@@ -1033,7 +1033,10 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // kPairTailMin rows, the decode kernel for shorter remainders, 9 = 7 with
 // tiles of up to 512 rows (two UMMAs per k-step over one decoded stage).
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 16 rows, variant 7 from 96 rows and variant 9 from 224
+// average at most 16 rows (8 or 16-row tiles) or 32 (32-row tiles, variant
+// 5: its four MMAs per decoded fragment run at about 290 TFLOP/s, so it
+// beats the tcgen05 kernels only while a group fits one tile), variant 7 from
+// 96 rows and variant 9 from 224
 // (prefill; most groups then exceed 256 rows or come close), else the
 // single-CTA tcgen05 kernel with 128-row tiles. Variant 8 is not chosen
 // automatically: since the pair kernel loads a partial token half in at most
@@ -1054,13 +1057,15 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   if (variant == 0)
     variant = codes_format != DWM_FP4_B200 ? 1
               : avg <= 16                  ? 2
+              : avg <= 32                  ? 5
               : avg >= 224                 ? 9
               : avg >= 96                  ? 7
                                            : 1;
-  if (variant >= 2 && variant <= 4)
+  if (variant >= 2 && variant <= 5)
     return launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                       group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
-                      variant == 3 ? 1 : variant == 4 ? 2 : (avg <= 6 ? 1 : 2), s);
+                      variant == 3 ? 1 : variant == 4 ? 2 : variant == 5 ? 4 : (avg <= 6 ? 1 : 2),
+                      s);
   if (variant == 7)
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
@@ -1140,12 +1145,12 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 9 && variant != 5 && variant != 6,
-                "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-4 (mma.sync decode "
+  DWM_CHECK_ARG(variant >= 0 && variant <= 9 && variant != 6,
+                "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-5 (mma.sync decode "
                 "kernel), 7 (tcgen05 on CTA pairs), 8 (CTA pairs + decode-kernel tails) or 9 "
                 "(CTA pairs, 512-row tiles)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
-                "variants 1-4 and 7-9 need the B200 layout");
+                "variants 1-5 and 7-9 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

@@ -95,6 +95,17 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #ifndef DWM_GMV_K128
 #define DWM_GMV_K128 1
 #endif
+// 32-row tasks (four n8 token tiles, variant 5): k per stage, ring depth and
+// warps per CTA. Their token tile (32 rows) outweighs the codes of a stage.
+#ifndef DWM_GMV_KS4
+#define DWM_GMV_KS4 64
+#endif
+#ifndef DWM_GMV_STAGES4
+#define DWM_GMV_STAGES4 2
+#endif
+#ifndef DWM_GMV_WARPS4
+#define DWM_GMV_WARPS4 16
+#endif
 // Sleep (ns) of a waiting warp between mbarrier polls (leaving issue slots to
 // the warps that have data); 0 = poll.
 #ifndef DWM_GMV_BACKOFF
@@ -112,11 +123,16 @@ struct Cfg {
   // KS. Rows KS/2 + 4 words apart put the 8 rows of a B-fragment load in 8
   // different bank quads.
   static constexpr int TOK_ROW = 2 * KS + 16;
-  static constexpr bool POST = SD == DWM_U8 && DWM_GMV_POST;  // E8M0: scale f32 partials
+  // E8M0: scale the f32 partials of each k32 block. Not for 32-row tasks:
+  // there the partials would cost 2 * NT multiply-adds per code word and 64
+  // registers, against 4 exact bf16 multiplies of the decoded weights.
+  static constexpr bool POST = SD == DWM_U8 && DWM_GMV_POST && NT <= 2;
   static constexpr int DELTA = (SD == DWM_U8 && !POST) ? kDelta : 0;  // weight-side bias
   static constexpr int es = ScaleTraits<SD>::bytes;
-  static constexpr int S =
-      KS == 128 ? DWM_GMV_STAGES1_K128 : (NT == 1 ? DWM_GMV_STAGES1 : DWM_GMV_STAGES2);
+  static constexpr int S = NT == 4      ? DWM_GMV_STAGES4
+                           : KS == 128  ? DWM_GMV_STAGES1_K128
+                           : NT == 1    ? DWM_GMV_STAGES1
+                                        : DWM_GMV_STAGES2;
   static constexpr bool RAW = DWM_GMV_RAW_TVALS != 0;
   // Largest E8M0 code of the post-MMA path: the k-block factor
   // 2^(c-1-kTokExp) (raw decode) or 2^(c-127) (normalised) must be a finite f32.
@@ -126,8 +142,9 @@ struct Cfg {
   static constexpr int SC_ROW = 64 * es;
   static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
-  static constexpr int WARPS = (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
-                                                     : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
+  static constexpr int WARPS = NT == 4 ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 12)
+                             : (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
+                                                      : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
   static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
@@ -667,8 +684,8 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
 
 // Decode-regime grouped GEMM on the B200 layout (called by the dwm_gmm_fp4
 // dispatcher after argument validation: k % 64 == 0, n % 256 == 0, 16-byte
-// aligned pointers). nt: 1 or 2 n8 token tiles per task (8 or 16 token rows;
-// every weight is decoded once per task).
+// aligned pointers). nt: 1, 2 or 4 n8 token tiles per task (8, 16 or 32
+// token rows; every weight is decoded once per task).
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
@@ -707,6 +724,13 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
     if (scale_dtype == DWM_BF16)
       return gmv::launch_impl<DWM_BF16, 2, 128>(lhs, codes, scales, a, stream);
     return gmv::launch_impl<DWM_F32, 2, 128>(lhs, codes, scales, a, stream);
+  }
+  if (nt == 4) {
+    if (scale_dtype == DWM_U8)
+      return gmv::launch_impl<DWM_U8, 4, DWM_GMV_KS4>(lhs, codes, scales, a, stream);
+    if (scale_dtype == DWM_BF16)
+      return gmv::launch_impl<DWM_BF16, 4, DWM_GMV_KS4>(lhs, codes, scales, a, stream);
+    return gmv::launch_impl<DWM_F32, 4, DWM_GMV_KS4>(lhs, codes, scales, a, stream);
   }
   if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 2);
   if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 2);

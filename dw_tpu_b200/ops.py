@@ -58,10 +58,10 @@ def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
     """out <- grouped matmul of lhs with the FP4 weights (see dwm_gmm_fp4).
     ``layout`` is "e2m1" (raw [g, k, n/2]) or "b200" (``fp4_to_b200_out``);
     ``variant`` 0 picks the kernel; 1 forces the tcgen05 kernel on one CTA,
-    2-4 the mma.sync decode kernel (auto / 8 / 16-row token tiles), 7 the
+    2-5 the mma.sync decode kernel (auto / 8 / 16 / 32-row token tiles), 7 the
     tcgen05 kernel on CTA pairs and 8 the pair kernel for each group's full
     256-row tiles with short remainders on the decode kernel, 9 the pair
-    kernel with tiles of up to 512 rows; 1-4 and 7-9 need the B200
+    kernel with tiles of up to 512 rows; 1-5 and 7-9 need the B200
     layout."""
     L.require_cuda(lhs, codes, scales, group_sizes, out)
     if lhs.dtype != torch.bfloat16 or lhs.dim() != 2:

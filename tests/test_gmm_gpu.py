@@ -317,6 +317,24 @@ def test_pair_kernel_many_short_tiles(dw):
 ])
 def test_gmm_decode_regime_b200(dw, gs, k, act, limit, sd, out_dt):
     """Decode-sized groups on the B200 layout take the mma.sync kernel."""
+    _decode_case(dw, gs, k, act, limit, sd, out_dt, 0)
+
+
+@pytest.mark.parametrize("gs,k,act,limit,sd,out_dt", [
+    ([17, 32, 0, 25, 40, 1, 33, 31], 256, None, None, "u8", "bf16"),
+    ([20, 64, 18, 0, 35, 30, 29, 24], 128, "swiglu", None, "u8", "bf16"),   # 64 rows: two tasks
+    ([26, 19, 31, 8, 0, 40, 22, 17], 448, None, None, "u8_wide", "f32"),    # codes 0 and > 132
+    ([32, 17, 25, 30, 21, 0, 28, 19], 320, "swiglu", 7.0, "bf16", "bf16"),
+    ([23, 29, 18, 32, 27, 0, 20, 31], 192, None, None, "f32", "bf16"),
+])
+def test_gmm_32row_tiles(dw, gs, k, act, limit, sd, out_dt):
+    """Variant 5: the mma.sync decode kernel with 32-row token tiles (four n8
+    tiles per decoded weight fragment, weights scaled in bf16 before the
+    MMA) on groups of 17-64 rows, every scale type, against the oracle."""
+    _decode_case(dw, gs, k, act, limit, sd, out_dt, 5)
+
+
+def _decode_case(dw, gs, k, act, limit, sd, out_dt, variant):
     from dw_tpu_b200 import ops
     from dw_tpu_b200 import _lib as L
     m = sum(gs) + 5
@@ -338,7 +356,7 @@ def test_gmm_decode_regime_b200(dw, gs, k, act, limit, sd, out_dt):
     n_out = n // 2 if act else n
     out = torch.full((m, n_out), 3.0, dtype=dt, device="cuda")
     ops.gmm_fp4_out(np_to_bf16(lhs), b200, sc.cuda(), torch.from_numpy(gs).cuda(), out, act=a,
-                    act_limit=limit or 0.0, zero_init=True, layout="b200")
+                    act_limit=limit or 0.0, zero_init=True, layout="b200", variant=variant)
     torch.cuda.synchronize()
     L.raise_on_device_error()
     r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind, limit=limit, out_dtype=out_dt)
