@@ -210,11 +210,20 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 // with work (the epilogue, above all). The outcome is double-buffered by the
 // group's step parity, so the first warp can publish the next step's value
 // while a slow warp still reads this one.
+// DWM_GMM_DEC_SYNC 0 instead lets every warp poll for itself.
+#ifndef DWM_GMM_DEC_SYNC
+#define DWM_GMM_DEC_SYNC 1
+#endif
 template <int SLEEP>
 __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint64_t* full,
                                            uint32_t full_ph, uint64_t* empty, uint32_t empty_ph,
                                            volatile int* abort_flag, volatile int* go,
                                            int* status) {
+  if (DWM_GMM_DEC_SYNC == 0) {
+    bool got = mbar_wait<SLEEP>(full, full_ph, abort_flag, status);
+    got = got && mbar_wait<SLEEP>(empty, empty_ph, abort_flag, status);
+    return __all_sync(0xffffffffu, got);
+  }
   volatile int* slot = go + grp * 2 + ((step >> 1) & 1);
   if (dw == 0) {
     bool got = mbar_wait<SLEEP>(full, full_ph, abort_flag, status);
@@ -229,6 +238,9 @@ __device__ __forceinline__ bool group_wait(int grp, int dw, uint32_t step, uint6
 template <int SD, int VAR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
+                   const __grid_constant__ CUtensorMap tm_lhs_32,
+                   const __grid_constant__ CUtensorMap tm_lhs_64,
+                   const __grid_constant__ CUtensorMap tm_lhs_128,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
   using L = Smem<SD>;
@@ -283,6 +295,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   if (warp == PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tm_lhs);
+    tma_prefetch_desc(&tm_lhs_32);
+    tma_prefetch_desc(&tm_lhs_64);
+    tma_prefetch_desc(&tm_lhs_128);
     tma_prefetch_desc(&tm_codes);
     tma_prefetch_desc(&tm_scales);
   }
@@ -545,10 +560,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ts_armed |= 1u << ts;
           ts_par = (ts_par & ~(1u << ts)) | (ts_ph << ts);
           uint8_t* tdst = smem + L::OFF_T + ts * T_STAGE;
-          for (int kl = 0; kl < kn; ++kl)
-            for (int b = 0; b < nb; ++b)
-              tma_load_2d(tdst + (kl * nbp + b) * T_BOX_BYTES, &tm_lhs, &tk_full[ts],
-                          (k0 + kl) * BK, t.row0 + b * T_BOX_ROWS, pol_keep);
+          // A k-step's nb boxes of 16 rows in at most three copies (one of
+          // 128 rows, else 64 + 32 + 16): each copy costs the issuing thread
+          // about as much as a full box. The boxes land where nb single boxes
+          // would.
+          for (int kl = 0; kl < kn; ++kl) {
+            uint8_t* kdst = tdst + kl * nbp * T_BOX_BYTES;
+            const int kx = (k0 + kl) * BK;
+            if (nb == 8) {
+              tma_load_2d(kdst, &tm_lhs_128, &tk_full[ts], kx, t.row0, pol_keep);
+              continue;
+            }
+            int b = 0;
+            if (nb & 4) {
+              tma_load_2d(kdst, &tm_lhs_64, &tk_full[ts], kx, t.row0, pol_keep);
+              b += 4;
+            }
+            if (nb & 2) {
+              tma_load_2d(kdst + b * T_BOX_BYTES, &tm_lhs_32, &tk_full[ts], kx,
+                          t.row0 + b * T_BOX_ROWS, pol_keep);
+              b += 2;
+            }
+            if (nb & 1)
+              tma_load_2d(kdst + b * T_BOX_BYTES, &tm_lhs, &tk_full[ts], kx,
+                          t.row0 + b * T_BOX_ROWS, pol_keep);
+          }
           if (++ts == TS) { ts = 0; ts_ph ^= 1; }
         }
       }
@@ -945,10 +981,13 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
            float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream,
            const EpHooks* hooks = nullptr) {
   using L = Smem<SD>;
-  CUtensorMap tm_lhs, tm_codes, tm_scales;
-  int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
-                          (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tm_lhs, tm_lhs_32, tm_lhs_64, tm_lhs_128, tm_codes, tm_scales;
+  CUtensorMap* lhs_maps[4] = {&tm_lhs, &tm_lhs_32, &tm_lhs_64, &tm_lhs_128};
+  int rc = 0;
+  for (int i = 0; i < 4 && !rc; ++i)  // boxes of 16, 32, 64 and 128 token rows
+    rc = encode_tmap_2d(lhs_maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)k,
+                        (uint64_t)m, (uint64_t)k * 2, BK, T_BOX_ROWS << i,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (VAR == kMN)
     rc = encode_tmap_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)n / 2,
@@ -983,8 +1022,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.n_tiles = n / (NSUB * BW);
   a.status = status_ptr();
   a.hk = hooks ? *hooks : EpHooks{};
-  gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(tm_lhs, tm_codes,
-                                                                         tm_scales, a);
+  gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(
+      tm_lhs, tm_lhs_32, tm_lhs_64, tm_lhs_128, tm_codes, tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmm_fp4 launch");
 }
 
