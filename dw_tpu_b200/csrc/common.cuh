@@ -302,6 +302,19 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
 __device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// One thread signalling every peer: a system-scope fence followed by relaxed
+// writes forms a release pattern per write (the fence orders this thread's
+// earlier accesses, and what it has observed, before each write), at the
+// cost of one system-scope flush (~1.6 us on B200) instead of one per peer.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+__device__ __forceinline__ void red_relaxed_sys_add(uint64_t* p, uint64_t v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
   uint32_t old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)

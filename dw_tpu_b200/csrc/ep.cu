@@ -341,18 +341,21 @@ __global__ void __launch_bounds__(XFER_THREADS)
   // The last CTA to finish: reset the tickets, advance the epoch, signal the
   // peers once, and wait for all of them. Ordering: every CTA's row stores
   // precede (bar.sync, then an acq_rel ticket at gpu scope) the last CTA's
-  // ticket, which precedes its release at system scope, which the peers'
-  // acquire observes; causality order is transitive across the two scopes,
-  // so one system-scope release per rank covers all CTAs' stores.
+  // ticket, which precedes its system-scope fence and the relaxed adds after
+  // it (a release pattern per peer), which the peers' acquire observes;
+  // causality order is transitive across the two scopes, so one fence covers
+  // all CTAs' stores and every peer.
   if (tid == 0) {
     s_last = atom_add_acq_rel_gpu(&P.ctl[CTL_DONE], 1u) == gridDim.x - 1;
     if (s_last) {
       P.ctl[CTL_DONE] = 0;
       P.ctl[CTL_FIRST] = 0;
       if (counts) P.ctl[CTL_EPOCH] = epoch;
-      if (rows)
+      if (rows) {
+        fence_acq_rel_sys();
         for (int p = 0; p < P.world; ++p)
-          red_release_sys_add(reinterpret_cast<uint64_t*>(P.peer[p] + P.L.arrive), 1);
+          red_relaxed_sys_add(reinterpret_cast<uint64_t*>(P.peer[p] + P.L.arrive), 1);
+      }
       if (ph & DWM_EP_WAIT)
         wait_count(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.arrive),
                    (uint64_t)epoch * P.world, P.wait_ns, status);
@@ -395,11 +398,13 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
         !wait_counter_ge(reinterpret_cast<const uint64_t*>(P.peer[P.rank] + P.L.delivered),
                          (uint64_t)(P.ctl[CTL_PUSH_STEPS] + 1) * P.world, P.wait_ns, status))
       s_ok = 0;
-    // The outputs were written by earlier kernels on this stream: a release
-    // store at system scope publishes them.
-    if ((ph & DWM_EP_PUSH) && atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u)
+    // The outputs were written by earlier kernels on this stream: one
+    // system-scope fence, then a relaxed flag store per peer, publishes them.
+    if ((ph & DWM_EP_PUSH) && atomicAdd(&P.ctl[CTL_FIRST], 1u) == 0u) {
+      fence_acq_rel_sys();
       for (int p = 0; p < P.world; ++p)
-        st_release_sys(reinterpret_cast<uint32_t*>(P.peer[p] + P.L.ready) + P.rank, P.ctl[CTL_EPOCH]);
+        st_relaxed_sys(reinterpret_cast<uint32_t*>(P.peer[p] + P.L.ready) + P.rank, P.ctl[CTL_EPOCH]);
+    }
   }
   __syncthreads();
   if (ph & DWM_EP_REDUCE) {

@@ -819,10 +819,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (a.hk.push_tags != nullptr && threadIdx.x == 0) {
     // Every row this CTA stored precedes (bar.sync, then an acq_rel ticket
     // at gpu scope) the last CTA's ticket, which precedes its system-scope
-    // release to every rank: one release covers all CTAs.
+    // fence and relaxed add to every rank: one fence covers all CTAs and
+    // every rank.
     if (atom_add_acq_rel_gpu(a.hk.ticket, 1u) == gridDim.x - 1) {
       *a.hk.ticket = 0;
-      for (int p = 0; p < a.hk.world; ++p) red_release_sys_add(a.hk.push_done[p], 1);
+      fence_acq_rel_sys();
+      for (int p = 0; p < a.hk.world; ++p) red_relaxed_sys_add(a.hk.push_done[p], 1);
     }
   }
   if (warp == MMA_WARP) {
