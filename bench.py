@@ -86,7 +86,9 @@ def parse():
     p.add_argument("--tokens", type=int, default=T_RANK)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--variant", type=int, default=0)
-    p.add_argument("--groups", choices=["uniform", "multinomial"], default="uniform")
+    p.add_argument("--groups", choices=["uniform", "multinomial", "zipf"], default="uniform")
+    p.add_argument("--decode-sweep", action="store_true",
+                   help="run the cfg4 decode sweep at any N > 1 (by default at N = 8 only)")
     return p.parse_args()
 
 
@@ -871,12 +873,12 @@ def ep_extras(args, local, dev, world, rank):
             "overlap_speedup": round(serial["ms_per_step"] / over["ms_per_step"], 3),
             "overlapped_bitwise_equal_serial_same_kernel": differ == 0.0}
         # ---- cfg4: the decode sweep on 8 GPUs, Zipf(1.2) ----
-        if world == 8:
+        if world == 8 or (world > 1 and args.decode_sweep):
             cases = [ep_layer_case(ctx, local, dev, world, rank, t, "zipf", args.seed,
                                    link_gbps, compact=True)[0]
                      for t in (2, 16, 64, 128, 256, 512)]
             out["decode_sweep"] = {"workload": "cfg4: T_rank in {1,8,32,64,128,256}x2, "
-                                               "Zipf(1.2) routing, 8 GPUs", "cases": cases}
+                                               f"Zipf(1.2) routing, {world} GPUs", "cases": cases}
     finally:
         ctx.close()
     return out
@@ -992,6 +994,9 @@ def run_case(a):
         if a.groups == "uniform":
             gs_np = np.full(e, rows // e, np.int32)
             gs_np[: rows - int(gs_np.sum())] += 1
+        elif a.groups == "zipf":  # the experts of top-k Zipf(1.2) routing (cfg2/cfg4)
+            ids_np, _ = synthetic.route_ids(t, e, TOPK, seed=a.seed, dist="zipf")
+            gs_np = np.bincount(ids_np.ravel(), minlength=e).astype(np.int32)
         else:
             gs_np = np.random.default_rng(a.seed).multinomial(rows, [1.0 / e] * e).astype(
                 np.int32)

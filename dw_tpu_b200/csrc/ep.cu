@@ -809,7 +809,7 @@ int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int 
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min, int wide);
+                    int tail_min, int wide, int grp_lo);
 int launch_gmm_single_ep(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                          const int32_t* group_sizes, int num_groups, int m, int k, int n,
                          int act, float limit, int out_dtype, void* out, const EpHooks* hooks,
@@ -868,7 +868,7 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
                                 dst, &hk, s);
   return launch_gmm_pair(lhs, codes, scales, scale_dtype, recv_group_sizes, c->local_experts,
                          (int)c->cap, k, n, 0, c->local_experts, act, act_limit, out_dtype, 0, dst,
-                         &hk, s, 0, variant == 9 ? 1 : 0);
+                         &hk, s, 0, variant == 9 ? 1 : 0, 0);
 }
 
 extern "C" int dwm_ep_link_probe(dwm_ep* c, int peer, int64_t bytes, void* stream) {

@@ -36,12 +36,12 @@ namespace dwm {
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream, int tail_min = 0);
+               cudaStream_t stream, int tail_min = 0, int grp_lo = 0, int grp_hi = 1 << 30);
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min, int wide);
+                    int tail_min, int wide, int grp_lo = 0);
 
 namespace gmm {
 
@@ -51,6 +51,12 @@ using namespace fp4;
 // least this many rows (a whole tile's decode costs about as much as the
 // decode kernel's six 16-row weight streams).
 constexpr int kPairTailMin = 96;
+// Variant 10's size classes: groups of up to kSplitRows16 rows on the decode
+// kernel's 16-row tiles, up to kSplitRows32 on its 32-row tiles, up to
+// kSplitRows96 on the single-CTA tcgen05 kernel, larger ones on CTA pairs.
+constexpr int kSplitRows16 = 16;
+constexpr int kSplitRows32 = 32;
+constexpr int kSplitRows96 = 95;  // 33-95 rows: the single-CTA tcgen05 kernel
 
 enum Variant { kMN = 0, kKS = 1 };
 
@@ -158,9 +164,15 @@ struct Args {
   void* out;
   int ldo;      // output row length (n, or n/2 with SwiGLU)
   int n_tiles;  // column tiles per group
+  int grp_lo, grp_hi;  // only groups of grp_lo < rows <= grp_hi (variant 10's size classes)
   int* status;
   EpHooks hk;   // expert-parallel gating / push (all null for a plain GEMM)
 };
+
+// Tiles of a group of `rows` rows in this launch.
+__device__ __forceinline__ int group_tile_count(int rows, const Args& a) {
+  return rows > a.grp_lo && rows <= a.grp_hi ? ((rows + BT - 1) / BT) * a.n_tiles : 0;
+}
 
 // SMEM slot p of an 8-column group holds column perm8(p) (kMN).
 __device__ __forceinline__ int perm8(int p) { return (p >> 1) + ((p & 1) << 2); }
@@ -342,7 +354,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int g = lane * per2 + i;
       if (g < NL) {
         int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        tsum += ((rows + BT - 1) / BT) * a.n_tiles;
+        tsum += group_tile_count(rows, a);
       }
     }
     int tincl = tsum;
@@ -357,7 +369,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (g < NL) {
         tile_prefix[g] = trun;
         int rows = row_start[a.group_offset + g + 1] - row_start[a.group_offset + g];
-        trun += ((rows + BT - 1) / BT) * a.n_tiles;
+        trun += group_tile_count(rows, a);
       }
     }
     if (lane == 31) tile_prefix[NL] = trun;
@@ -981,7 +993,7 @@ template <int SD, int VAR>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, cudaStream_t stream,
-           const EpHooks* hooks = nullptr) {
+           const EpHooks* hooks = nullptr, int grp_lo = 0, int grp_hi = 1 << 30) {
   using L = Smem<SD>;
   CUtensorMap tm_lhs, tm_lhs_32, tm_lhs_64, tm_lhs_128, tm_codes, tm_scales;
   CUtensorMap* lhs_maps[4] = {&tm_lhs, &tm_lhs_32, &tm_lhs_64, &tm_lhs_128};
@@ -1022,6 +1034,8 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.out = out;
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.n_tiles = n / (NSUB * BW);
+  a.grp_lo = grp_lo;
+  a.grp_hi = grp_hi;
   a.status = status_ptr();
   a.hk = hooks ? *hooks : EpHooks{};
   gmm_fp4_kernel<SD, VAR><<<num_sms(), NUM_THREADS, L::ALLOC, stream>>>(
@@ -1074,10 +1088,11 @@ static int validate(const void* lhs, const void* codes, int codes_format, const 
 // kPairTailMin rows, the decode kernel for shorter remainders, 9 = 7 with
 // tiles of up to 512 rows (two UMMAs per k-step over one decoded stage).
 // The automatic choice for the B200 layout: mma.sync when the local groups
-// average at most 16 rows (8 or 16-row tiles) or 32 (32-row tiles, variant
-// 5: its four MMAs per decoded fragment run at about 290 TFLOP/s, so it
-// beats the tcgen05 kernels only while a group fits one tile), variant 7 from
-// 96 rows and variant 9 from 224
+// average at most 16 rows (8 or 16-row tiles), variant 10 (each group on the
+// kernel for its size) at 17-48, where groups straddle the classes (the
+// 32-row decode tiles run their four MMAs per decoded fragment at about 290
+// TFLOP/s, so they beat the tcgen05 kernels only while a group fits one
+// tile), variant 7 from 96 rows and variant 9 from 224
 // (prefill; most groups then exceed 256 rows or come close), else the
 // single-CTA tcgen05 kernel with 128-row tiles. Variant 8 is not chosen
 // automatically: since the pair kernel loads a partial token half in at most
@@ -1098,7 +1113,7 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
   if (variant == 0)
     variant = codes_format != DWM_FP4_B200 ? 1
               : avg <= 16                  ? 2
-              : avg <= 32                  ? 5
+              : avg <= 48                  ? 10
               : avg >= 224                 ? 9
               : avg >= 96                  ? 7
                                            : 1;
@@ -1115,6 +1130,39 @@ static int run(const void* lhs, const void* codes, int codes_format, const void*
     return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
                            group_offset, num_local_groups, act, act_limit, out_dtype, zero_init,
                            out, nullptr, s, 0, 1);
+  if (variant == 10) {
+    // Each group on the kernel for its size: up to 16 rows on the decode
+    // kernel's 16-row tiles, 17-32 on its 32-row tiles (one weight stream
+    // each), 33-95 on the single-CTA tcgen05 kernel, larger groups on CTA
+    // pairs with tiles of up to 512 rows. For skewed routing, where a group
+    // of a few rows would otherwise cost the pair kernel a whole tile's
+    // decode. The launches write disjoint rows; the first zeroes the rows
+    // outside the local groups. A launch that finds no group of its class
+    // costs a few microseconds.
+    int rc = launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                        group_offset, num_local_groups, act, act_limit, out_dtype, zero_init, out,
+                        2, s, 0, 0, kSplitRows16);
+    if (rc) return rc;
+    rc = launch_gmv(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                    group_offset, num_local_groups, act, act_limit, out_dtype, 0, out, 4, s, 0,
+                    kSplitRows16, kSplitRows32);
+    if (rc) return rc;
+#define DWM_GMM_CLASS(SD)                                                                   \
+  rc = launch<SD, kKS>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset,  \
+                       num_local_groups, act, act_limit, out_dtype, 0, out, s, nullptr,     \
+                       kSplitRows32, kSplitRows96)
+    if (scale_dtype == DWM_U8)
+      DWM_GMM_CLASS(DWM_U8);
+    else if (scale_dtype == DWM_BF16)
+      DWM_GMM_CLASS(DWM_BF16);
+    else
+      DWM_GMM_CLASS(DWM_F32);
+#undef DWM_GMM_CLASS
+    if (rc) return rc;
+    return launch_gmm_pair(lhs, codes, scales, scale_dtype, group_sizes, num_groups, m, k, n,
+                           group_offset, num_local_groups, act, act_limit, out_dtype, 0, out,
+                           nullptr, s, 0, 1, kSplitRows96);
+  }
   if (variant == 8) {
     // Full 256-row tiles (and remainders of kPairTailMin rows or more) on CTA
     // pairs, shorter remainders on the decode kernel: a remainder of r rows
@@ -1186,12 +1234,12 @@ extern "C" int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes
                                    int n, int group_offset, int num_local_groups, int act,
                                    float act_limit, int out_dtype, int zero_init, void* out,
                                    int variant, void* stream) {
-  DWM_CHECK_ARG(variant >= 0 && variant <= 9 && variant != 6,
+  DWM_CHECK_ARG(variant >= 0 && variant <= 10 && variant != 6,
                 "variant must be 0 (auto), 1 (tcgen05, one CTA), 2-5 (mma.sync decode "
-                "kernel), 7 (tcgen05 on CTA pairs), 8 (CTA pairs + decode-kernel tails) or 9 "
-                "(CTA pairs, 512-row tiles)");
+                "kernel), 7 (tcgen05 on CTA pairs), 8 (CTA pairs + decode-kernel tails), 9 "
+                "(CTA pairs, 512-row tiles) or 10 (each group on the kernel for its size)");
   DWM_CHECK_ARG(variant == 0 || codes_format == DWM_FP4_B200,
-                "variants 1-5 and 7-9 need the B200 layout");
+                "variants 1-5 and 7-10 need the B200 layout");
   int rc = gmm::validate(lhs, codes, codes_format, scales, scale_dtype, group_sizes, num_groups,
                          m, k, n, group_offset, num_local_groups, act, out_dtype, out);
   if (rc) return rc;

@@ -136,6 +136,7 @@ struct Args {
   int tail_min; // 0: a group's rows in tiles of equal size; > 0: tiles of 256 rows and
                 // a last tile only if at least tail_min rows remain (fewer are left to
                 // the decode kernel, which streams the weights once per 16 rows)
+  int grp_lo;   // only groups of more than grp_lo rows (variant 10's size classes)
   int* status;
   EpHooks hk;   // expert-parallel gating / push (all null for a plain GEMM)
 };
@@ -149,7 +150,8 @@ struct Tile {
 
 // Row tiles of a group of `rows` rows, tiles of at most bt rows (see
 // Args::tail_min).
-__device__ __forceinline__ int group_tiles(int rows, int bt, int tail_min) {
+__device__ __forceinline__ int group_tiles(int rows, int bt, int tail_min, int grp_lo) {
+  if (rows <= grp_lo) return 0;
   if (tail_min <= 0) return (rows + bt - 1) / bt;
   return rows / bt + (rows % bt >= tail_min ? 1 : 0);
 }
@@ -378,7 +380,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int tsum = 0;
     for (int i = 0; i < per2; ++i) {
       const int pos = lane * per2 + i;
-      if (pos < NL) tsum += group_tiles(rows_of(tile_prefix[pos]), a.max_rows, a.tail_min) * a.n_tiles;
+      if (pos < NL) tsum += group_tiles(rows_of(tile_prefix[pos]), a.max_rows, a.tail_min, a.grp_lo) * a.n_tiles;
     }
     int tincl = tsum;
 #pragma unroll
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (pos < NL) {
         const int g = tile_prefix[pos];
         tile_prefix[pos] = trun | (g << kTileBits);
-        trun += group_tiles(rows_of(g), a.max_rows, a.tail_min) * a.n_tiles;
+        trun += group_tiles(rows_of(g), a.max_rows, a.tail_min, a.grp_lo) * a.n_tiles;
       }
     }
     if (lane == 31) tile_prefix[NL] = trun;
@@ -871,7 +873,7 @@ template <int SD, bool WIDE>
 int launch(const void* lhs, const void* codes, const void* scales, const int32_t* group_sizes,
            int num_groups, int m, int k, int n, int group_offset, int n_local, int act,
            float limit, int out_dtype, int zero_init, void* out, const EpHooks* hooks,
-           int tail_min, cudaStream_t stream) {
+           int tail_min, int grp_lo, cudaStream_t stream) {
   using L = Layout<SD, WIDE>;
   constexpr int es = ScaleTraits<SD>::bytes;
   const bool act_on = act != DWM_ACT_NONE;
@@ -932,6 +934,7 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
   a.ldo = act_on ? n / 2 : n;
   a.n_tiles = n / 256;
   a.tail_min = tail_min;
+  a.grp_lo = grp_lo;
   a.max_rows = WIDE ? 2 * BT : BT;
   a.status = status_ptr();
   a.hk = hooks ? *hooks : EpHooks{};
@@ -957,16 +960,17 @@ int launch(const void* lhs, const void* codes, const void* scales, const int32_t
 // Entry from the grouped-matmul dispatcher (gmm_fp4.cu): B200-layout weights,
 // n a multiple of 256, k of 64; the caller has validated the arguments.
 // hooks: expert-parallel gating / push (dwm_ep_gmm_fp4), or nullptr;
-// tail_min: Args::tail_min; wide: tiles of up to 512 token rows (Layout).
+// tail_min: Args::tail_min; wide: tiles of up to 512 token rows (Layout);
+// grp_lo: Args::grp_lo.
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
-                    int tail_min, int wide) {
+                    int tail_min, int wide, int grp_lo) {
 #define DWM_PAIR_LAUNCH(SD, W)                                                               \
   gmm_pair::launch<SD, W>(lhs, codes, scales, group_sizes, num_groups, m, k, n, group_offset, \
                           n_local, act, limit, out_dtype, zero_init, out, hooks, tail_min,   \
-                          stream)
+                          grp_lo, stream)
   if (scale_dtype == DWM_U8) return wide ? DWM_PAIR_LAUNCH(DWM_U8, true) : DWM_PAIR_LAUNCH(DWM_U8, false);
   if (scale_dtype == DWM_BF16)
     return wide ? DWM_PAIR_LAUNCH(DWM_BF16, true) : DWM_PAIR_LAUNCH(DWM_BF16, false);

@@ -169,12 +169,19 @@ struct Args {
   int quads;  // tasks per row chunk: n / 64
   int tail_min;  // 0: all rows; > 0: only the rows past a group's last full 256-row tile,
                  // and only if fewer than tail_min (the CTA-pair kernel takes the rest)
+  int grp_lo, grp_hi;  // only groups of grp_lo < rows <= grp_hi (variant 10's size classes)
   int* status;
 };
 
 // The rows [w0, w0 + wn) of a group starting at row gs0 with gsn rows that
-// this launch computes (see Args::tail_min).
-__device__ __forceinline__ void row_window(int gs0, int gsn, int tail_min, int& w0, int& wn) {
+// this launch computes (see Args::tail_min, grp_lo and grp_hi).
+__device__ __forceinline__ void row_window(int gs0, int gsn, const Args& a, int& w0, int& wn) {
+  const int tail_min = a.tail_min;
+  if (gsn <= a.grp_lo || gsn > a.grp_hi) {
+    w0 = gs0;
+    wn = 0;
+    return;
+  }
   if (tail_min <= 0) {
     w0 = gs0;
     wn = gsn;
@@ -226,8 +233,7 @@ __device__ __forceinline__ Task get_task(int idx, const int* row_start, const in
   t.quad = local - chunk * a.quads;
   int gs0, gsn;
   row_window(row_start[a.group_offset + lo],
-             row_start[a.group_offset + lo + 1] - row_start[a.group_offset + lo], a.tail_min,
-             gs0, gsn);
+             row_start[a.group_offset + lo + 1] - row_start[a.group_offset + lo], a, gs0, gsn);
   t.row0 = gs0 + chunk * 8 * NT;
   t.rows = min(8 * NT, gsn - chunk * 8 * NT);
   return t;
@@ -316,8 +322,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
       if (g < NL) {
         int w0, rows;
         row_window(row_start[a.group_offset + g],
-                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a.tail_min,
-                   w0, rows);
+                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a, w0,
+                   rows);
         tsum += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
       }
     }
@@ -334,8 +340,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
         task_prefix[g] = trun;
         int w0, rows;
         row_window(row_start[a.group_offset + g],
-                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a.tail_min,
-                   w0, rows);
+                   row_start[a.group_offset + g + 1] - row_start[a.group_offset + g], a, w0,
+                   rows);
         trun += ((rows + 8 * NT - 1) / (8 * NT)) * a.quads;
       }
     }
@@ -689,7 +695,7 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream, int tail_min) {
+               cudaStream_t stream, int tail_min, int grp_lo, int grp_hi) {
   gmv::Args a;
   a.group_sizes = group_sizes;
   a.num_groups = num_groups;
@@ -706,6 +712,8 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.ldo = act == DWM_ACT_NONE ? n : n / 2;
   a.quads = n / 64;
   a.tail_min = tail_min;
+  a.grp_lo = grp_lo;
+  a.grp_hi = grp_hi;
   a.status = status_ptr();
 #define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
   if (nt <= 1 && k % 128 == 0 && DWM_GMV_K128) {

@@ -392,8 +392,8 @@ def gemm_variant(layout: str, expected_rows: float) -> int:
         return 3  # mma.sync kernel, 8-row token tiles
     if expected_rows <= 16:
         return 4  # mma.sync kernel, 16-row token tiles (one task per expert)
-    if expected_rows <= 32:
-        return 5  # mma.sync kernel, 32-row token tiles
+    if expected_rows <= 48:
+        return 10  # each group on the kernel for its size (decode kernel up to 32 rows)
     if expected_rows >= 224:
         return 9  # tcgen05 on CTA pairs, tiles of up to 512 rows
     if expected_rows >= 96:

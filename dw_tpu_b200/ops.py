@@ -61,8 +61,8 @@ def gmm_fp4_out(lhs, codes, scales, group_sizes, out, *, group_offset=0,
     2-5 the mma.sync decode kernel (auto / 8 / 16 / 32-row token tiles), 7 the
     tcgen05 kernel on CTA pairs and 8 the pair kernel for each group's full
     256-row tiles with short remainders on the decode kernel, 9 the pair
-    kernel with tiles of up to 512 rows; 1-5 and 7-9 need the B200
-    layout."""
+    kernel with tiles of up to 512 rows, 10 each group on the kernel for its
+    size; 1-5 and 7-10 need the B200 layout."""
     L.require_cuda(lhs, codes, scales, group_sizes, out)
     if lhs.dtype != torch.bfloat16 or lhs.dim() != 2:
         raise ValueError("lhs must be a 2-D bf16 tensor")

@@ -98,14 +98,13 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
 
 /* dwm_gmm_fp4 with the kernel variant fixed: 0 = automatic (as dwm_gmm_fp4),
  * 1 = tcgen05 MMA on weights decoded into shared memory (128-row tiles; the
- * automatic choice for groups averaging 33-95 rows),
+ * automatic choice for groups averaging 49-95 rows),
  * 2 = mma.sync on weights decoded straight into registers (decode-sized
  * groups; 8-row token tiles up to 6 rows per group on average, 16-row tiles
  * above), 3 / 4 = the same with 8 / 16-row token tiles (2: the automatic
  * choice for B200 codes whose groups average at most 16 rows), 5 = the same
  * with 32-row token tiles (four n8 tiles per decoded weight fragment; E8M0
- * scales multiplied into the decoded weights in bf16 before the MMA; the
- * automatic choice for groups averaging 17-32 rows),
+ * scales multiplied into the decoded weights in bf16 before the MMA),
  * 7 = tcgen05 on CTA pairs: M = 256 UMMAs (cta_group::2) over two SMs, each
  * decoding half of the weight columns, up to 256 token rows per tile and
  * double-buffered accumulators, a group above 256 rows in tiles of equal
@@ -117,11 +116,15 @@ int dwm_gmm_fp4(const void* lhs, const void* codes, int codes_format, const void
  * (N = 256 and the rest) into both 256-column TMEM accumulator slots over
  * one decoded stage, so a group of 257-512 rows costs one tile's decode;
  * tiles of up to 256 rows keep the two slots double-buffered (the automatic
- * choice for B200 codes whose groups average 224 rows or more). 1-5 and 7-9
- * need DWM_FP4_B200 codes; 6 is not assigned. Every variant decodes
+ * choice for B200 codes whose groups average 224 rows or more); 10 = each
+ * group on the kernel for its size, in four launches over disjoint rows:
+ * 1-16 rows on the mma.sync kernel's 16-row tiles, 17-32 on its 32-row tiles,
+ * 33-95 on variant 1's kernel, larger groups on variant 9's (the automatic
+ * choice for groups averaging 17-48 rows; for skewed routing at any size).
+ * 1-5 and 7-10 need DWM_FP4_B200 codes; 6 is not assigned. Every variant decodes
  * the same bf16 weights and accumulates in f32; results differ between
  * variants only by f32 summation order (1, 7 and 9 give identical bits; 8
- * gives them on every group's first 256 rows). Same reference interface as
+ * gives them on every group's first 256 rows, 10 on groups above 32 rows). Same reference interface as
  * dwm_gmm_fp4 (TK:107-153). */
 int dwm_gmm_fp4_variant(const void* lhs, const void* codes, int codes_format, const void* scales,
                         int scale_dtype, const int32_t* group_sizes, int num_groups, int m,

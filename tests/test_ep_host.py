@@ -69,7 +69,7 @@ def test_gemm_variant_choice():
     assert gemm_variant("b200", 2) == 3
     assert gemm_variant("b200", 8) == 4
     assert gemm_variant("b200", 16) == 4
-    assert gemm_variant("b200", 32) == 5
+    assert gemm_variant("b200", 32) == 10
     assert gemm_variant("b200", 64) == 1
     assert gemm_variant("b200", 96) == 7
     assert gemm_variant("b200", 128) == 7

@@ -412,6 +412,35 @@ def test_gmm_prefill_tiles(dw, layout):
             assert np.all(got[~v] == 0), variant
 
 
+@pytest.mark.parametrize("act", [None, "swiglu"])
+def test_gmm_size_classes(dw, act):
+    """Variant 10: each group on the kernel for its size (1-16 rows on the
+    decode kernel's 16-row tiles, 17-32 on its 32-row tiles, larger groups on
+    CTA pairs with 512-row tiles), on a skewed mix of groups, with
+    zero_init, against the oracle."""
+    from dw_tpu_b200 import ops
+    from dw_tpu_b200 import _lib as L
+    gs = [1, 5, 16, 0, 17, 32, 33, 64, 300, 2, 520, 8]
+    m = sum(gs) + 9
+    lhs, packed, scales, gs = _case(17, m, 256, 512, len(gs), gs=gs, lo=118, hi=132)
+    codes = dw.fp4_weight_to_codes(torch.from_numpy(packed).cuda())
+    sc = torch.from_numpy(scales).cuda()
+    g = torch.from_numpy(gs).cuda()
+    kind = act
+    a = L.ACT_SWIGLU if act else L.ACT_NONE
+    n_out = 256 if act else 512
+    r, v = O.gmm_ref(lhs, packed, scales, gs, act=kind)
+    r32, _ = O.gmm_f32(lhs, packed, scales, gs, act=kind)
+    out = torch.full((m, n_out), 5.0, dtype=torch.bfloat16, device="cuda")
+    ops.gmm_fp4_out(np_to_bf16(lhs), codes, sc, g, out, act=a, zero_init=True, layout="b200",
+                    variant=10)
+    torch.cuda.synchronize()
+    L.raise_on_device_error()
+    got = bf16_to_np(out)
+    assert_gemm_close(got, r, r32, 256, rows=v)
+    assert np.all(got[~v] == 0)
+
+
 def test_gmm_deterministic(dw):
     lhs, packed, scales, gs = _case(7, 300, 256, 512, 4)
     a = _run_gmm(dw, lhs, packed, scales, gs)
