@@ -106,19 +106,30 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #ifndef DWM_GMV_WARPS4
 #define DWM_GMV_WARPS4 16
 #endif
+// 1: 128-k launches whose 64-column tasks would give a warp fewer than three
+// run half-width tasks (QB = 2); 0 (default): always 64 columns. Measured
+// slower at the per-rank shapes of 4 and 8 GPUs (32 experts x 512 rows: gmm1
+// 0.187 against 0.163 ms; 64 experts: 0.239 against 0.213): a half-width
+// stage carries the same fixed cost for half the words.
+#ifndef DWM_GMV_HALF_TASKS
+#define DWM_GMV_HALF_TASKS 0
+#endif
 // Sleep (ns) of a waiting warp between mbarrier polls (leaving issue slots to
 // the warps that have data); 0 = poll.
 #ifndef DWM_GMV_BACKOFF
 #define DWM_GMV_BACKOFF 0
 #endif
 
-// KS: k per ring stage (64 or 128).
-template <int SD, int NT, int KS>
+// KS: k per ring stage (64 or 128). QB: 16-column code blocks per task, 4 (64
+// weight columns: 32 output features with SwiGLU) or 2 (half that: twice the
+// tasks, for launches with too few tasks to fill every warp a few times).
+template <int SD, int NT, int KS, int QB = 4>
 struct Cfg {
   static constexpr int KSTAGE = KS;
   static constexpr int KS16 = KS / 16, KS32 = KS / 32;
-  // [2 halves][2 column blocks][KS16 k16 blocks][32 words], one TMA copy.
-  static constexpr int CODE_BYTES = 4 * KS16 * 128;
+  // [QB column blocks (gate ones first with SwiGLU)][KS16 k16 blocks][32
+  // words], one TMA copy.
+  static constexpr int CODE_BYTES = QB * KS16 * 128;
   // A token row in shared memory: KS + 8 k of bf16, of which the stage uses
   // KS. Rows KS/2 + 4 words apart put the 8 rows of a B-fragment load in 8
   // different bank quads.
@@ -138,8 +149,8 @@ struct Cfg {
   // 2^(c-1-kTokExp) (raw decode) or 2^(c-127) (normalised) must be a finite f32.
   static constexpr uint32_t POST_MAX = POST ? (RAW ? 128u + kTokExp : 254u) : 128u + kDelta;
   static constexpr int TOK = 8 * NT * TOK_ROW;  // token tile: rows of KS + 8 k (KS used)
-  // Scales of a stage: [KS32 k32 rows][2 tiles][32 columns], one TMA copy.
-  static constexpr int SC_ROW = 64 * es;
+  // Scales of a stage: [KS32 k32 rows][2 tiles][8 * QB columns], one TMA copy.
+  static constexpr int SC_ROW = 16 * QB * es;
   static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
   static constexpr int WARPS = NT == 4 ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 12)
@@ -150,7 +161,7 @@ struct Cfg {
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int BYTES = OFF_TASKS + (MAX_GROUPS + 1) * 4;
   static constexpr int ALLOC = BYTES + 128;  // slack for 128-byte alignment (TMA destinations)
-  static constexpr uint32_t TX = TOK + CODE_BYTES + 2 * KS32 * 32 * es;
+  static constexpr uint32_t TX = TOK + CODE_BYTES + SC;
   static_assert(ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory");
   static_assert(TOK % 128 == 0 && CODE_BYTES % 128 == 0 && SC % 128 == 0 && KS32 % 2 == 0,
                 "TMA destinations need 128-byte alignment");
@@ -166,7 +177,7 @@ struct Args {
   int zero_init;
   void* out;
   int ldo;
-  int quads;  // tasks per row chunk: n / 64
+  int quads;  // tasks per row chunk: n / (16 * QB)
   int tail_min;  // 0: all rows; > 0: only the rows past a group's last full 256-row tile,
                  // and only if fewer than tail_min (the CTA-pair kernel takes the rest)
   int grp_lo, grp_hi;  // only groups of grp_lo < rows <= grp_hi (variant 10's size classes)
@@ -239,24 +250,26 @@ __device__ __forceinline__ Task get_task(int idx, const int* row_start, const in
   return t;
 }
 
-// First column block of each of the task's two block pairs: adjacent 64
-// columns, or the gate and up halves for SwiGLU.
+// First column block of each of the task's two halves of QB/2 blocks:
+// adjacent columns, or the gate and up halves for SwiGLU.
+template <int QB>
 __device__ __forceinline__ void task_blocks(const Task& t, const Args& a, int& cb0, int& cb1) {
+  constexpr int HB = QB / 2;
   if (a.act == DWM_ACT_NONE) {
-    cb0 = 4 * t.quad;
-    cb1 = cb0 + 2;
+    cb0 = QB * t.quad;
+    cb1 = cb0 + HB;
   } else {
-    cb0 = 2 * t.quad;
-    cb1 = a.n / 32 + 2 * t.quad;
+    cb0 = HB * t.quad;
+    cb1 = a.n / 32 + HB * t.quad;
   }
 }
 
-template <int SD, int NT, int KS>
-__global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
+template <int SD, int NT, int KS, int QB>
+__global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
     gmv_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_scales, const Args a) {
-  using C = Cfg<SD, NT, KS>;
+  using C = Cfg<SD, NT, KS, QB>;
   constexpr int S = C::S;
   constexpr int es = C::es;
   constexpr int KSTAGE = C::KSTAGE, CODE_BYTES = C::CODE_BYTES, TOK_ROW = C::TOK_ROW;
@@ -392,10 +405,17 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     const bool act = a.act != DWM_ACT_NONE;
     y_tok = t.row0;
     c_g = t.g;
-    c_a = act ? t.quad : 0;
-    c_b = act ? 0 : t.quad;
-    s_x = act ? 32 * t.quad : 0;
-    s_y = act ? 0 : 2 * t.quad;
+    if constexpr (QB == 4) {
+      c_a = act ? t.quad : 0;
+      c_b = act ? 0 : t.quad;
+      s_x = act ? 32 * t.quad : 0;
+      s_y = act ? 0 : 2 * t.quad;
+    } else {  // the maps of launch_impl for QB = 2
+      c_a = t.quad;
+      c_b = 0;
+      s_x = act ? 16 * t.quad : 0;
+      s_y = act ? 0 : t.quad;
+    }
     y_s = t.g * (a.k / 32);
   };
   uint32_t issued = 0;  // stages issued so far (ring sequence)
@@ -428,11 +448,11 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
   for (int idx = first; idx < total && ok; idx += wstride) {
     const Task t = get_task<NT>(idx, row_start, task_prefix, a);
     int cb0, cb1;
-    task_blocks(t, a, cb0, cb1);
+    task_blocks<QB>(t, a, cb0, cb1);
 
-    float acc[4][NT][4];
+    float acc[QB][NT][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < QB; ++i)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -459,15 +479,15 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
 #pragma unroll
         for (int h = 0; h < C::KS32; ++h) {  // 32-deep k block inside the stage
           // Scales of the lane's columns: block i, column gid (+8 for hc =
-          // 1); tile i/2 holds 2 rows (k32 blocks) of 32 columns.
-          uint32_t wm[4][2];
-          float post[4][2];
+          // 1); a k32 row holds the task's 16 * QB columns, block i's at
+          // 16 i.
+          uint32_t wm[QB][2];
+          float post[QB][2];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < QB; ++i)
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
-              const uint8_t* p =
-                  sc + h * C::SC_ROW + ((i >> 1) * 32 + (i & 1) * 16 + gid + 8 * hc) * es;
+              const uint8_t* p = sc + h * C::SC_ROW + (i * 16 + gid + 8 * hc) * es;
               uint32_t c;
               if constexpr (SD == DWM_U8)
                 c = *p;
@@ -488,7 +508,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
                                      : __uint_as_float(c << 23);  // 2^(c-127)
               }
             }
-          float part[4][NT][4];
+          float part[QB][NT][4];
 #pragma unroll
           for (int kk2 = 0; kk2 < 2; ++kk2) {
             const int kk = 2 * h + kk2;  // k16 block inside the stage
@@ -509,7 +529,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
               b[nt][1] = b1;
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < QB; ++i) {
               const uint32_t w =
                   *reinterpret_cast<const uint32_t*>(code + i * (C::KS16 * 128) + kk * 128 + lane * 4);
               uint32_t af[4];
@@ -545,7 +565,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
           }
           if constexpr (!PRE && C::POST) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < QB; ++i)
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -555,12 +575,12 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
         }
       };
       if constexpr (SD == DWM_U8) {
-        // One check per stage for the whole warp: each lane tests KS32 / 2 of
-        // the stage's KS32 x 16 scale words; the fast path needs every code in
+        // One check per stage for the whole warp: each lane tests SC / 128 of
+        // the stage's SC / 4 scale words; the fast path needs every code in
         // [1, POST_MAX].
         uint32_t bad = 0;
 #pragma unroll
-        for (int q = 0; q < C::KS32 / 2; ++q) {
+        for (int q = 0; q < C::SC / 128; ++q) {
           const uint32_t v = *reinterpret_cast<const uint32_t*>(sc + (q * 32 + lane) * 4);
           const uint32_t zero_byte = (v - 0x01010101u) & ~v & 0x80808080u;
           uint32_t high_byte;
@@ -588,7 +608,9 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
     // Epilogue: c0,c1 = (column gid, tokens 2t, 2t+1), c2,c3 = (column gid+8, ...);
     // kAccScale removes the weight-side 2^-delta exactly.
     constexpr float kAccScale = (float)(1 << C::DELTA);
-    const int colbase[4] = {16 * cb0, 16 * cb0 + 16, 16 * cb1, 16 * cb1 + 16};
+    int colbase[QB];
+#pragma unroll
+    for (int i = 0; i < QB; ++i) colbase[i] = 16 * (i < QB / 2 ? cb0 + i : cb1 + i - QB / 2);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -598,7 +620,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
         const int64_t row = t.row0 + r;
         if (a.act == DWM_ACT_NONE) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < QB; ++i) {
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
               const float v = acc[i][nt][hc * 2 + e] * kAccScale;
@@ -611,11 +633,11 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
+          for (int i = 0; i < QB / 2; ++i) {
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
               float g = acc[i][nt][hc * 2 + e] * kAccScale;
-              float u = acc[i + 2][nt][hc * 2 + e] * kAccScale;
+              float u = acc[i + QB / 2][nt][hc * 2 + e] * kAccScale;
               if (a.act == DWM_ACT_SWIGLU_CLAMP) {
                 g = fminf(g, a.limit);
                 u = fminf(fmaxf(u, -a.limit), a.limit);
@@ -639,10 +661,11 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS>::WARPS * 32, 1)
   }
 }
 
-template <int SD, int NT, int KS>
-int launch_impl(const void* lhs, const void* codes, const void* scales, const Args& a,
+template <int SD, int NT, int KS, int QB = 4>
+int launch_impl(const void* lhs, const void* codes, const void* scales, Args a,
                 cudaStream_t stream) {
-  using C = Cfg<SD, NT, KS>;
+  using C = Cfg<SD, NT, KS, QB>;
+  a.quads = a.n / (16 * QB);
   CUtensorMap tm_lhs, tm_codes, tm_scales;
   // lhs [m, k] bf16: box of KS + 8 k (KS used) x 8*NT rows, rows TOK_ROW bytes apart.
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)a.k,
@@ -657,11 +680,23 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
   const bool act = a.act != DWM_ACT_NONE;
   const uint64_t R = (uint64_t)(a.k / 16) * 128;
   const uint64_t cw = (uint64_t)(a.k / 16) * 32, q64 = (uint64_t)a.n / 64, G = a.n_local;
-  {
+  if (QB == 4) {
     const uint64_t dims[5] = {cw, 2, act ? q64 : 2, act ? 2 : q64, G};
     const uint64_t strides[4] = {R, 2 * R, act ? (uint64_t)(a.n / 32) * R : 4 * R,
                                  (uint64_t)(a.n / 16) * R};
     const uint32_t box[5] = {(uint32_t)(C::KS16 * 32), 2, act ? 1u : 2u, act ? 2u : 1u, 1};
+    rc = encode_tmap_nd(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 5, codes, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    // Two blocks per task, coordinates (word, 0, task, 0, group): with SwiGLU
+    // gate block `task` and its up block n/32 later, else blocks 2 task and
+    // 2 task + 1. Dimensions of one are placeholders.
+    const uint64_t q32 = (uint64_t)a.n / 32;
+    const uint64_t dims[5] = {cw, act ? 1u : 2u, q32, act ? 2u : 1u, G};
+    const uint64_t strides[4] = {R, act ? R : 2 * R, act ? q32 * R : q32 * 2 * R,
+                                 (uint64_t)(a.n / 16) * R};
+    const uint32_t box[5] = {(uint32_t)(C::KS16 * 32), act ? 1u : 2u, 1, act ? 2u : 1u, 1};
     rc = encode_tmap_nd(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 5, codes, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -670,18 +705,21 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, const Ar
   // k32 rows; the tiles are the gate and up halves (n/2 apart) with SwiGLU,
   // else two adjacent 32-column groups.
   {
+    // QB = 2: 16 columns x (gate, up) with SwiGLU, else one 32-column group.
     constexpr uint64_t es = ScaleTraits<SD>::bytes;
     const uint64_t dims[3] = {act ? (uint64_t)a.n / 2 : 32, act ? 2 : (uint64_t)a.n / 32,
                               G * (a.k / 32)};
     const uint64_t strides[2] = {act ? (uint64_t)a.n / 2 * es : 32 * es, (uint64_t)a.n * es};
-    const uint32_t box[3] = {32, 2, (uint32_t)C::KS32};
+    const uint32_t box[3] = {act ? (uint32_t)(8 * QB) : 32u, act ? 2u : (uint32_t)(QB / 2),
+                             (uint32_t)C::KS32};
     rc = encode_tmap_nd(&tm_scales, ScaleTraits<SD>::tma, 3, scales, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  rc = set_smem_limit(reinterpret_cast<const void*>(gmv_fp4_kernel<SD, NT, KS>), C::ALLOC, "gmv smem attribute");
+  rc = set_smem_limit(reinterpret_cast<const void*>(gmv_fp4_kernel<SD, NT, KS, QB>), C::ALLOC,
+                      "gmv smem attribute");
   if (rc) return rc;
-  gmv_fp4_kernel<SD, NT, KS><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(
+  gmv_fp4_kernel<SD, NT, KS, QB><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(
       tm_lhs, tm_codes, tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmv_fp4 launch");
 }
@@ -716,11 +754,21 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.grp_hi = grp_hi;
   a.status = status_ptr();
 #define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
+  // Half-width tasks (QB = 2) when 64-column tasks, one per local group and
+  // column quad, would not give every warp of the grid three.
+  auto half_tasks = [&](int warps) {
+    return DWM_GMV_HALF_TASKS && (int64_t)n_local * (n / 64) < 3LL * num_sms() * warps;
+  };
+#define DWM_GMV_K128_BY_QB(SD, NT)                                                       \
+  do {                                                                                    \
+    if (half_tasks(gmv::Cfg<SD, NT, 128, 2>::WARPS))                                      \
+      return gmv::launch_impl<SD, NT, 128, 2>(lhs, codes, scales, a, stream);             \
+    return gmv::launch_impl<SD, NT, 128, 4>(lhs, codes, scales, a, stream);               \
+  } while (0)
   if (nt <= 1 && k % 128 == 0 && DWM_GMV_K128) {
-    if (scale_dtype == DWM_U8) return gmv::launch_impl<DWM_U8, 1, 128>(lhs, codes, scales, a, stream);
-    if (scale_dtype == DWM_BF16)
-      return gmv::launch_impl<DWM_BF16, 1, 128>(lhs, codes, scales, a, stream);
-    return gmv::launch_impl<DWM_F32, 1, 128>(lhs, codes, scales, a, stream);
+    if (scale_dtype == DWM_U8) DWM_GMV_K128_BY_QB(DWM_U8, 1);
+    if (scale_dtype == DWM_BF16) DWM_GMV_K128_BY_QB(DWM_BF16, 1);
+    DWM_GMV_K128_BY_QB(DWM_F32, 1);
   }
   if (nt <= 1) {
     if (scale_dtype == DWM_U8) DWM_GMV(DWM_U8, 1);
@@ -728,10 +776,9 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
     DWM_GMV(DWM_F32, 1);
   }
   if (nt == 2 && DWM_GMV_K128_NT2 && k % 128 == 0) {
-    if (scale_dtype == DWM_U8) return gmv::launch_impl<DWM_U8, 2, 128>(lhs, codes, scales, a, stream);
-    if (scale_dtype == DWM_BF16)
-      return gmv::launch_impl<DWM_BF16, 2, 128>(lhs, codes, scales, a, stream);
-    return gmv::launch_impl<DWM_F32, 2, 128>(lhs, codes, scales, a, stream);
+    if (scale_dtype == DWM_U8) DWM_GMV_K128_BY_QB(DWM_U8, 2);
+    if (scale_dtype == DWM_BF16) DWM_GMV_K128_BY_QB(DWM_BF16, 2);
+    DWM_GMV_K128_BY_QB(DWM_F32, 2);
   }
   if (nt == 4) {
     if (scale_dtype == DWM_U8)
@@ -744,6 +791,7 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   if (scale_dtype == DWM_BF16) DWM_GMV(DWM_BF16, 2);
   DWM_GMV(DWM_F32, 2);
 #undef DWM_GMV
+#undef DWM_GMV_K128_BY_QB
 }
 
 }  // namespace dwm
