@@ -904,6 +904,8 @@ def ep_layer_case(ctx, local, dev, world, rank, t, routing, seed, link_gbps, com
         ids_np, _ = synthetic.route_ids(t, E, TOPK, seed=2000 + 7 * t + rank, dist="zipf")
         logits = zipf_logits(ids_np, dev)
     expected = t * TOPK / E * world
+    if gemm_variant is None and routing == "zipf" and expected > 16 and not overlap:
+        gemm_variant = 10  # skewed groups: each on the kernel for its size
     layer = ep_mod.EPMoELayer(local, ctx, TOPK, expected_rows=expected, overlap=overlap,
                               gemm_variant=gemm_variant)
     out = torch.empty((t, H), dtype=torch.bfloat16, device=dev)
