@@ -114,6 +114,10 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #ifndef DWM_GMV_HALF_TASKS
 #define DWM_GMV_HALF_TASKS 0
 #endif
+// 1: 128-k launches with few tasks split each task's k range over a warp pair.
+#ifndef DWM_GMV_SPLIT
+#define DWM_GMV_SPLIT 1
+#endif
 // Sleep (ns) of a waiting warp between mbarrier polls (leaving issue slots to
 // the warps that have data); 0 = poll.
 #ifndef DWM_GMV_BACKOFF
@@ -153,11 +157,16 @@ struct Cfg {
   static constexpr int SC_ROW = 16 * QB * es;
   static constexpr int SC = KS32 * SC_ROW;
   static constexpr int WARP_BYTES = (S * (TOK + CODE_BYTES + SC) + 127) & ~127;
+  // Split-K warp pairs: 128-k stages, and a token slot that holds a warp's
+  // f32 partials (QB * NT quads of registers per lane).
+  static constexpr bool SPLIT_OK = KS == 128 && QB * NT * 32 * 16 <= TOK;
   static constexpr int WARPS = NT == 4 ? (SD != DWM_F32 ? DWM_GMV_WARPS4 : 12)
                              : (NT == 2 && KS == 128) ? (SD != DWM_F32 ? DWM_GMV_WARPS2_K128 : 10)
                                                       : (SD != DWM_F32 ? DWM_GMV_WARPS1 : 12);
   static constexpr int OFF_BAR = WARPS * WARP_BYTES;
-  static constexpr int OFF_ROWS = OFF_BAR + WARPS * S * 8;
+  // Split-K exchange barriers: [WARPS / 2 pairs][ready, consumed].
+  static constexpr int OFF_XBAR = OFF_BAR + WARPS * S * 8;
+  static constexpr int OFF_ROWS = OFF_XBAR + WARPS * 8;
   static constexpr int OFF_TASKS = OFF_ROWS + (MAX_GROUPS + 1) * 4;
   static constexpr int BYTES = OFF_TASKS + (MAX_GROUPS + 1) * 4;
   static constexpr int ALLOC = BYTES + 128;  // slack for 128-byte alignment (TMA destinations)
@@ -181,6 +190,7 @@ struct Args {
   int tail_min;  // 0: all rows; > 0: only the rows past a group's last full 256-row tile,
                  // and only if fewer than tail_min (the CTA-pair kernel takes the rest)
   int grp_lo, grp_hi;  // only groups of grp_lo < rows <= grp_hi (variant 10's size classes)
+  int ksplit;  // 1, or 2: warp pairs split each task's k range (split-K in the CTA)
   int* status;
 };
 
@@ -264,7 +274,7 @@ __device__ __forceinline__ void task_blocks(const Task& t, const Args& a, int& c
   }
 }
 
-template <int SD, int NT, int KS, int QB>
+template <int SD, int NT, int KS, int QB, bool SPLIT>
 __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
     gmv_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
@@ -285,9 +295,21 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
   uint8_t* code_s = tok_s + S * C::TOK;           // [S][CODE_BYTES]
   uint8_t* sc_s = code_s + S * CODE_BYTES;        // [S][SC]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR) + warp * S;
+  // Split-K: warps 2p and 2p+1 take the same tasks, the first half of k and
+  // the second; the second hands its f32 partials to the first through
+  // shared memory (its just-consumed token slot) behind two mbarriers, and
+  // the first adds them (own + partner, a fixed order) and stores.
+  static_assert(!SPLIT || C::SPLIT_OK, "split-K needs 128-k stages and room for the partials");
+  constexpr int ks = SPLIT ? 2 : 1;  // a.ksplit
+  const int kh = SPLIT ? (warp & 1) : 0;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + C::OFF_XBAR) + 2 * (warp >> 1);
 
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    if (SPLIT && kh == 0) {
+      mbar_init(&xbar[0], 1);  // partials ready (the second warp)
+      mbar_init(&xbar[1], 1);  // partials read (the first warp)
+    }
     fence_mbar_init();
   }
   if (threadIdx.x == 32) {
@@ -378,6 +400,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
 
   const int gid = lane >> 2, tig = lane & 3;
   const int NSTAGE = a.k / KSTAGE;
+  const int NST = NSTAGE / ks;  // stages of this warp's part of a task
   const DecodeRegs dregs = DecodeRegs::make();
   // Register-held constants of the post-MMA path: the zero quad of the
   // partials' first MMA and the tokens' 2^kTokExp pre-scale.
@@ -386,15 +409,15 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
   const uint32_t tok_scale = pin(kBf16x2_TokScale);
   // 2^(c-1-delta) for E8M0 code c, both bf16 halves: c * 0x00800080 + bias.
   const uint32_t wm_bias = pin((126u - C::DELTA) * 0x00800080u);
-  const int wstride = gridDim.x * C::WARPS;
-  // Warps numbered SM-minor: the last, partial round of tasks lands on one
-  // warp per SM (which then runs with the SM nearly to itself) instead of
-  // on every warp of a few SMs.
-  const int first = warp * gridDim.x + blockIdx.x;
+  const int wstride = gridDim.x * (C::WARPS / ks);
+  // Warps (pairs with split-K) numbered SM-minor: the last, partial round of
+  // tasks lands on one warp per SM (which then runs with the SM nearly to
+  // itself) instead of on every warp of a few SMs.
+  const int first = (SPLIT ? warp >> 1 : warp) * gridDim.x + blockIdx.x;
 
   // ---- producer state (lane 0): the next (task, stage) to fetch ----
   uint64_t pol_stream = 0, pol_keep = 0;
-  int iss_idx = first, iss_st = 0;
+  int iss_idx = first, iss_st = 0, iss_end = NST;
   // Per-task TMA coordinates: token row, the group and the two quad
   // coordinates of the code map (the map's dimensions differ with the
   // activation; the task's quad goes into one of them), the scale map's two
@@ -417,6 +440,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
       s_y = act ? 0 : t.quad;
     }
     y_s = t.g * (a.k / 32);
+    iss_st = kh * NST;
+    iss_end = iss_st + NST;
   };
   uint32_t issued = 0;  // stages issued so far (ring sequence)
   auto issue_one = [&]() {
@@ -429,8 +454,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
     tma_load_3d(sc_s + slot * C::SC, &tm_scales, bar, s_x, s_y, y_s + C::KS32 * iss_st,
                 pol_stream);
     ++issued;
-    if (++iss_st == NSTAGE) {
-      iss_st = 0;
+    if (++iss_st == iss_end) {
       iss_idx += wstride;
       if (iss_idx < total) set_task(iss_idx);
     }
@@ -445,7 +469,8 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
 
   uint32_t seq = 0;  // stages consumed
   bool ok = true;
-  for (int idx = first; idx < total && ok; idx += wstride) {
+  uint32_t tcount = 0;  // tasks done (the exchange barriers' phase)
+  for (int idx = first; idx < total && ok; idx += wstride, ++tcount) {
     const Task t = get_task<NT>(idx, row_start, task_prefix, a);
     int cb0, cb1;
     task_blocks<QB>(t, a, cb0, cb1);
@@ -458,7 +483,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.0f;
 
-    for (int st = 0; st < NSTAGE; ++st, ++seq) {
+    for (int st = 0; st < NST; ++st, ++seq) {
       const int slot = (int)(seq % S);
       const bool got =
           mbar_wait<DWM_GMV_BACKOFF>(&bars[slot], (seq / S) & 1, nullptr, a.status);
@@ -600,10 +625,56 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
         stage(std::true_type{});
       }
       __syncwarp();  // every lane is done with this slot
-      if (lane == 0 && iss_idx < total) issue_one();
+      // The second warp of a split pair keeps its last slot for the hand-over.
+      const bool keep = SPLIT && kh == 1 && st == NST - 1;
+      if (!keep && lane == 0 && iss_idx < total) issue_one();
       __syncwarp();
     }
     if (!ok) break;
+    if constexpr (SPLIT) {
+      // Hand-over area: the second warp's slot of its last stage (both warps
+      // of the pair have consumed the same number of stages).
+      const int xslot = (int)((seq - 1) % S);
+      float4* xb = reinterpret_cast<float4*>(smem + (warp | 1) * C::WARP_BYTES + xslot * C::TOK);
+      const uint32_t xph = tcount & 1;
+      if (kh == 1) {
+#pragma unroll
+        for (int i = 0; i < QB; ++i)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            xb[(i * NT + nt) * 32 + lane] =
+                make_float4(acc[i][nt][0], acc[i][nt][1], acc[i][nt][2], acc[i][nt][3]);
+        fence_proxy_async_smem();  // before this warp's next TMA into the slot
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xbar[0]);
+        const bool got = mbar_wait<DWM_GMV_BACKOFF>(&xbar[1], xph, nullptr, a.status);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0 && iss_idx < total) issue_one();
+        __syncwarp();
+        continue;  // the first warp stores the task
+      }
+      const bool got = mbar_wait<DWM_GMV_BACKOFF>(&xbar[0], xph, nullptr, a.status);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int i = 0; i < QB; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 v = xb[(i * NT + nt) * 32 + lane];
+          acc[i][nt][0] += v.x;
+          acc[i][nt][1] += v.y;
+          acc[i][nt][2] += v.z;
+          acc[i][nt][3] += v.w;
+        }
+      fence_proxy_async_smem();  // these reads before the partner's TMA into the slot
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[1]);
+    }
 
     // Epilogue: c0,c1 = (column gid, tokens 2t, 2t+1), c2,c3 = (column gid+8, ...);
     // kAccScale removes the weight-side 2^-delta exactly.
@@ -666,6 +737,13 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, Args a,
                 cudaStream_t stream) {
   using C = Cfg<SD, NT, KS, QB>;
   a.quads = a.n / (16 * QB);
+  // Split-K warp pairs when the launch has too few tasks to give every warp
+  // several (the last, partial round of tasks then dominates): each task's
+  // two halves run concurrently, so a round costs half a task.
+  a.ksplit = (DWM_GMV_SPLIT && C::SPLIT_OK && (a.k / KS) % 2 == 0 && C::WARPS % 2 == 0 &&
+              (int64_t)a.n_local * a.quads < 4LL * num_sms() * C::WARPS)
+                 ? 2
+                 : 1;
   CUtensorMap tm_lhs, tm_codes, tm_scales;
   // lhs [m, k] bf16: box of KS + 8 k (KS used) x 8*NT rows, rows TOK_ROW bytes apart.
   int rc = encode_tmap_2d(&tm_lhs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lhs, (uint64_t)a.k,
@@ -716,11 +794,12 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, Args a,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  rc = set_smem_limit(reinterpret_cast<const void*>(gmv_fp4_kernel<SD, NT, KS, QB>), C::ALLOC,
-                      "gmv smem attribute");
+  auto kernel = gmv_fp4_kernel<SD, NT, KS, QB, false>;
+  if constexpr (C::SPLIT_OK)
+    if (a.ksplit == 2) kernel = gmv_fp4_kernel<SD, NT, KS, QB, true>;
+  rc = set_smem_limit(reinterpret_cast<const void*>(kernel), C::ALLOC, "gmv smem attribute");
   if (rc) return rc;
-  gmv_fp4_kernel<SD, NT, KS, QB><<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(
-      tm_lhs, tm_codes, tm_scales, a);
+  kernel<<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(tm_lhs, tm_codes, tm_scales, a);
   return check_cuda(cudaGetLastError(), "gmv_fp4 launch");
 }
 
@@ -752,6 +831,7 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.tail_min = tail_min;
   a.grp_lo = grp_lo;
   a.grp_hi = grp_hi;
+  a.ksplit = 1;
   a.status = status_ptr();
 #define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
   // Half-width tasks (QB = 2) when 64-column tasks, one per local group and
