@@ -114,9 +114,13 @@ constexpr uint32_t kBf16x2_2p126 = 253u * 0x00800080u;                          
 #ifndef DWM_GMV_HALF_TASKS
 #define DWM_GMV_HALF_TASKS 0
 #endif
-// 1: 128-k launches with few tasks split each task's k range over a warp pair.
+// 1: 128-k launches with few tasks split each task's k range over a warp pair
+// (3-5% faster at the per-rank shapes of 4 and 8 GPUs); 0 (default): every
+// task sums its whole k range in one warp, so the expert-parallel layer keeps
+// the single-device layer's bits at every rank count (split-K sums the two
+// halves of k separately: within 1 bf16 ulp, not bit-equal).
 #ifndef DWM_GMV_SPLIT
-#define DWM_GMV_SPLIT 1
+#define DWM_GMV_SPLIT 0
 #endif
 // Sleep (ns) of a waiting warp between mbarrier polls (leaving issue slots to
 // the warps that have data); 0 = poll.
