@@ -87,6 +87,9 @@ def parse():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--variant", type=int, default=0)
     p.add_argument("--groups", choices=["uniform", "multinomial", "zipf"], default="uniform")
+    p.add_argument("--overlap", action="store_true",
+                   help="N > 1: the cfg1 step with the overlapped exchange (gated gmm1, "
+                        "pushing gmm2)")
     p.add_argument("--decode-sweep", action="store_true",
                    help="run the cfg4 decode sweep at any N > 1 (by default at N = 8 only)")
     return p.parse_args()
@@ -322,12 +325,14 @@ def max_over_ranks(vals, world, dev):
 
 class GmmTimer:
     """Records CUDA events around every dw_moe gmm_fp4 launch (on the current
-    stream) while active, tagged gmm1 (SwiGLU) or gmm2."""
+    stream) while active, tagged gmm1 (SwiGLU) or gmm2; with `ctx`, also
+    around the overlapped exchange's grouped matmuls (EPContext.gmm)."""
 
-    def __init__(self):
+    def __init__(self, ctx=None):
         from dw_tpu_b200 import ops
         self.ops = ops
         self.orig = ops.gmm_fp4_out
+        self.ctx = ctx
         self.ev = []
 
     def __enter__(self):
@@ -343,10 +348,24 @@ class GmmTimer:
             self.ev.append((e0, e1, kw.get("act", L.ACT_NONE) != L.ACT_NONE))
             return r
         self.ops.gmm_fp4_out = timed
+        if self.ctx is not None:
+            orig_gmm = self.ctx.gmm
+
+            def timed_ep(*a, **kw):
+                e0, e1 = events()
+                s = torch.cuda.current_stream()
+                e0.record(s)
+                r = orig_gmm(*a, **kw)
+                e1.record(s)
+                self.ev.append((e0, e1, kw.get("mode") == L.EP_GEMM_GATED))
+                return r
+            self.ctx.gmm = timed_ep
         return self
 
     def __exit__(self, *exc):
         self.ops.gmm_fp4_out = self.orig
+        if self.ctx is not None:
+            del self.ctx.gmm  # back to the class method
 
     def ms(self):
         g1 = [a.elapsed_time(b) for a, b, act in self.ev if act]
@@ -393,7 +412,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         from dw_tpu_b200 import ep as ep_mod
         ctx = ep_mod.create_context(max_tokens=T_RANK, hidden=H, topk=TOPK, num_experts=E)
-        layer = ep_mod.EPMoELayer(local, ctx, TOPK)
+        layer = ep_mod.EPMoELayer(local, ctx, TOPK, overlap=args.overlap)
     else:
         layer = dw.MoELayer(local, TOPK, T_RANK)
     out = torch.empty((T_RANK, H), dtype=torch.bfloat16, device=dev)
@@ -424,7 +443,7 @@ def run_ours(args, rank, world, local_rank):
             return run
         ctx.dispatch, ctx.combine = timed(orig_d, "dispatch"), timed(orig_c, "combine")
     start, end = events()
-    with GmmTimer() as gt, ClockSampler(local_rank) as clk:
+    with GmmTimer(ctx) as gt, ClockSampler(local_rank) as clk:
         barrier()
         torch.cuda.synchronize(dev)
         torch.cuda._sleep(PREROLL_CYCLES)  # the steps queue up: the events time the device
@@ -1071,7 +1090,8 @@ def main():
         "ms_per_step": round(res["ms"] / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; FP4 weights and E8M0 scales as BASELINE config 0/1)",
-        "config": config_of(world),
+        "config": dict(config_of(world), **({"exchange": "one-shot, overlapped with the GEMMs"}
+                                             if world > 1 and args.overlap else {})),
         "e2e": {"value": round(tokens / (res["e2e_ms"] * 1e-3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
         "roofline": res["roofline"],

@@ -810,6 +810,10 @@ int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int 
                     int group_offset, int n_local, int act, float limit, int out_dtype,
                     int zero_init, void* out, const EpHooks* hooks, cudaStream_t stream,
                     int tail_min, int wide, int grp_lo);
+int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
+               const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
+               int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
+               cudaStream_t stream, int tail_min, int grp_lo, int grp_hi, const EpHooks* hooks);
 int launch_gmm_single_ep(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                          const int32_t* group_sizes, int num_groups, int m, int k, int n,
                          int act, float limit, int out_dtype, void* out, const EpHooks* hooks,
@@ -824,9 +828,11 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
   int rc = check_ctx(c);
   if (rc) return rc;
   DWM_CHECK_ARG(mode == DWM_EP_GEMM_GATED || mode == DWM_EP_GEMM_PUSH, "mode=%d", mode);
-  DWM_CHECK_ARG(variant == 1 || variant == 7 || variant == 9,
-                "the EP grouped matmul runs on the tcgen05 kernels: variant 1 (one CTA), 7 "
-                "(CTA pairs) or 9 (CTA pairs, 512-row tiles)");
+  DWM_CHECK_ARG(variant == 1 || variant == 3 || variant == 4 || variant == 5 || variant == 7 ||
+                    variant == 9,
+                "the EP grouped matmul runs variant 1 (tcgen05, one CTA), 3 / 4 / 5 (mma.sync "
+                "decode kernel, 8 / 16 / 32-row tiles), 7 (CTA pairs) or 9 (CTA pairs, 512-row "
+                "tiles)");
   DWM_CHECK_ARG(codes_format == DWM_FP4_B200, "the EP grouped matmul takes the B200 layout");
   DWM_CHECK_ARG(scale_dtype == DWM_U8 || scale_dtype == DWM_BF16 || scale_dtype == DWM_F32,
                 "scale dtype must be u8 (e8m0), bf16 or f32");
@@ -862,6 +868,10 @@ extern "C" int dwm_ep_gmm_fp4(dwm_ep* c, const void* lhs, const void* codes, int
     dst = c->base + c->L.outb;  // not written: every row goes to its token's owner
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (variant >= 3 && variant <= 5)
+    return launch_gmv(lhs, codes, scales, scale_dtype, recv_group_sizes, c->local_experts,
+                      (int)c->cap, k, n, 0, c->local_experts, act, act_limit, out_dtype, 0, dst,
+                      variant == 3 ? 1 : variant == 4 ? 2 : 4, s, 0, 0, 1 << 30, &hk);
   if (variant == 1)
     return launch_gmm_single_ep(lhs, codes, scales, scale_dtype, recv_group_sizes,
                                 c->local_experts, (int)c->cap, k, n, act, act_limit, out_dtype,

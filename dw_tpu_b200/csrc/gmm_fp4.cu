@@ -36,7 +36,8 @@ namespace dwm {
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream, int tail_min = 0, int grp_lo = 0, int grp_hi = 1 << 30);
+               cudaStream_t stream, int tail_min = 0, int grp_lo = 0, int grp_hi = 1 << 30,
+               const EpHooks* hooks = nullptr);
 int launch_gmm_pair(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                     const int32_t* group_sizes, int num_groups, int m, int k, int n,
                     int group_offset, int n_local, int act, float limit, int out_dtype,

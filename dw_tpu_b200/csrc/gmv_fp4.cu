@@ -196,6 +196,7 @@ struct Args {
   int grp_lo, grp_hi;  // only groups of grp_lo < rows <= grp_hi (variant 10's size classes)
   int ksplit;  // 1, or 2: warp pairs split each task's k range (split-K in the CTA)
   int* status;
+  EpHooks hk;  // expert-parallel gating / push (all null for a plain GEMM)
 };
 
 // The rows [w0, w0 + wn) of a group starting at row gs0 with gsn rows that
@@ -427,9 +428,18 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
   // activation; the task's quad goes into one of them), the scale map's two
   // column coordinates and the task's first scale row.
   int y_tok = 0, c_g = 0, c_a = 0, c_b = 0, s_x = 0, s_y = 0, y_s = 0;
+  int gated = -1;  // expert-parallel gating: last local expert seen complete
   auto set_task = [&](int idx) {
     const Task t = get_task<NT>(idx, row_start, task_prefix, a);
     const bool act = a.act != DWM_ACT_NONE;
+    if (a.hk.gate_arrive != nullptr && t.g != gated) {
+      // Every source rank's rows of this expert have been stored here (and
+      // made visible) before TMA reads them. A wait that runs out reports a
+      // timeout; the stages then load whatever has arrived.
+      wait_counter_ge(a.hk.gate_arrive + t.g, a.hk.gate_target[t.g], a.hk.wait_ns, a.status);
+      fence_proxy_async_all();
+      gated = t.g;
+    }
     y_tok = t.row0;
     c_g = t.g;
     if constexpr (QB == 4) {
@@ -694,16 +704,26 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
         if (r >= t.rows) continue;
         const int64_t row = t.row0 + r;
         if (a.act == DWM_ACT_NONE) {
+          // Expert parallel: straight into the token owner's buffer, at the
+          // row of its (token, k) pair (over NVLink for a peer).
+          void* obase = a.out;
+          int64_t orow = row;
+          if (a.hk.push_tags != nullptr) {
+            const int tag = a.hk.push_tags[row];
+            if (tag < 0) continue;
+            obase = a.hk.push_base[tag >> kEpTagBits];
+            orow = tag & ((1 << kEpTagBits) - 1);
+          }
 #pragma unroll
           for (int i = 0; i < QB; ++i) {
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
               const float v = acc[i][nt][hc * 2 + e] * kAccScale;
-              const int64_t off = row * a.ldo + colbase[i] + gid + 8 * hc;
+              const int64_t off = orow * a.ldo + colbase[i] + gid + 8 * hc;
               if (a.out_f32)
-                reinterpret_cast<float*>(a.out)[off] = v;
+                reinterpret_cast<float*>(obase)[off] = v;
               else
-                reinterpret_cast<uint16_t*>(a.out)[off] = (uint16_t)f32_to_bf16_bits(v);
+                reinterpret_cast<uint16_t*>(obase)[off] = (uint16_t)f32_to_bf16_bits(v);
             }
           }
         } else {
@@ -733,6 +753,17 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
   if (!ok && lane == 0) {
     for (uint32_t q = seq; q < issued; ++q)
       mbar_wait(&bars[q % S], (q / S) & 1, nullptr, a.status);
+  }
+  if (a.hk.push_tags != nullptr) {
+    // Every row this CTA stored precedes (bar.sync, then an acq_rel ticket at
+    // gpu scope) the last CTA's ticket, which precedes its system-scope fence
+    // and relaxed add to every rank: one fence covers all CTAs and ranks.
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(a.hk.ticket, 1u) == gridDim.x - 1) {
+      *a.hk.ticket = 0;
+      fence_acq_rel_sys();
+      for (int p = 0; p < a.hk.world; ++p) red_relaxed_sys_add(a.hk.push_done[p], 1);
+    }
   }
 }
 
@@ -812,11 +843,12 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, Args a,
 // Decode-regime grouped GEMM on the B200 layout (called by the dwm_gmm_fp4
 // dispatcher after argument validation: k % 64 == 0, n % 256 == 0, 16-byte
 // aligned pointers). nt: 1, 2 or 4 n8 token tiles per task (8, 16 or 32
-// token rows; every weight is decoded once per task).
+// token rows; every weight is decoded once per task). hooks: expert-parallel
+// gating / push (dwm_ep_gmm_fp4), or nullptr.
 int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale_dtype,
                const int32_t* group_sizes, int num_groups, int m, int k, int n, int group_offset,
                int n_local, int act, float limit, int out_dtype, int zero_init, void* out, int nt,
-               cudaStream_t stream, int tail_min, int grp_lo, int grp_hi) {
+               cudaStream_t stream, int tail_min, int grp_lo, int grp_hi, const EpHooks* hooks) {
   gmv::Args a;
   a.group_sizes = group_sizes;
   a.num_groups = num_groups;
@@ -837,6 +869,7 @@ int launch_gmv(const void* lhs, const void* codes, const void* scales, int scale
   a.grp_hi = grp_hi;
   a.ksplit = 1;
   a.status = status_ptr();
+  a.hk = hooks ? *hooks : EpHooks{};
 #define DWM_GMV(SD, NT) return gmv::launch_impl<SD, NT, 64>(lhs, codes, scales, a, stream)
   // Half-width tasks (QB = 2) when 64-column tasks, one per local group and
   // column quad, would not give every warp of the grid three.

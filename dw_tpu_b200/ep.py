@@ -171,8 +171,9 @@ class EPContext:
         reads the receive buffer (lhs = ``recv``) expert by expert as the rows
         arrive and writes ``out``; EP_GEMM_PUSH stores every output row into
         its token owner's buffer (``out`` unused). ``variant`` 1 runs the
-        one-CTA tcgen05 kernel, 7 the CTA-pair kernel, 9 the CTA-pair kernel
-        with tiles of up to 512 rows."""
+        one-CTA tcgen05 kernel, 3 / 4 / 5 the mma.sync decode kernel with 8 /
+        16 / 32-row tiles, 7 the CTA-pair kernel, 9 the CTA-pair kernel with
+        tiles of up to 512 rows."""
         L.require_cuda(lhs, codes, scales)
         sc = scales.view(torch.uint8) if scales.element_size() == 1 else scales
         g, n, k2 = codes.shape
@@ -383,6 +384,20 @@ def reduce_scatter_local(x: torch.Tensor, group=None,
 # The EP layer
 # ---------------------------------------------------------------------------
 
+def overlap_variant(expected_rows: float) -> int:
+    """Kernel of the overlapped exchange (one that carries its hooks) for a
+    local expert receiving ``expected_rows`` rows on average."""
+    if expected_rows >= 224:
+        return 9  # tcgen05 on CTA pairs, tiles of up to 512 rows
+    if expected_rows >= 96:
+        return 7  # tcgen05 on CTA pairs
+    if expected_rows > 32:
+        return 1  # tcgen05, one CTA
+    if expected_rows > 16:
+        return 5  # mma.sync decode kernel, 32-row tiles
+    return 4 if expected_rows > 6 else 3  # mma.sync decode kernel, 16 / 8-row tiles
+
+
 def gemm_variant(layout: str, expected_rows: float) -> int:
     """Kernel choice for a local expert receiving ``expected_rows`` rows on
     average (the receive buffer's row count is a capacity, not a size)."""
@@ -441,11 +456,11 @@ class EPMoELayer:
         self.overlap = bool(overlap)
         if self.overlap and weights.layout != "b200":
             raise ValueError("the overlapped exchange takes B200-layout weights")
-        if self.overlap:  # the tcgen05 kernels carry the exchange hooks
+        if self.overlap:  # the kernels that carry the exchange hooks
             if gemm_variant is None:
-                self.variant = 9 if expected_rows >= 224 else 7 if expected_rows >= 96 else 1
-            elif int(gemm_variant) not in (1, 7, 9):
-                raise ValueError("the overlapped exchange runs on variant 1, 7 or 9")
+                self.variant = overlap_variant(expected_rows)
+            elif int(gemm_variant) not in (1, 3, 4, 5, 7, 9):
+                raise ValueError("the overlapped exchange runs on variant 1, 3, 4, 5, 7 or 9")
         self.y_dtype = torch.float32 if f32_reduce else torch.bfloat16
         # rank_order: the combine sums in the reference GMM_EP order (per-rank
         # masked f32 partials, then ranks in order) instead of k order.

@@ -357,8 +357,9 @@ int dwm_ep_combine_shared(dwm_ep* ctx, const void* y, int y_dtype, const void* t
                           int w_dtype, const void* shared, int shared_dtype, float routed_scale,
                           int mid_dtype, void* out, int out_dtype, int phases, void* stream);
 /* The overlapped form of the exchange (prefill): the grouped matmuls run on a
- * tcgen05 kernel (`variant` 1, one CTA, 7, CTA pairs, or 9, CTA pairs with
- * 512-row tiles, as in dwm_gmm_fp4_variant) with the exchange folded in,
+ * kernel of `variant` 1 (tcgen05, one CTA), 3 / 4 / 5 (mma.sync decode
+ * kernel, 8 / 16 / 32-row tiles), 7 (CTA pairs) or 9 (CTA pairs, 512-row
+ * tiles), as in dwm_gmm_fp4_variant, with the exchange folded in,
  * instead of the dispatch waiting for every row and the combine pulling every
  * output after the GEMMs.
  *   dwm_ep_dispatch(..., DWM_EP_COUNTS | DWM_EP_ROWS | DWM_EP_GATED): stores

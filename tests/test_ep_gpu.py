@@ -470,13 +470,15 @@ def test_ep_layer_full_size_matches_single_device(ep):
 
 
 @pytest.mark.parametrize("f32_reduce,t,variant", [(False, 128, 9), (True, 128, 9),
-                                                  (False, 96, 7), (False, 32, 1)])
+                                                  (False, 96, 7), (False, 32, 1), (False, 16, 5),
+                                                  (True, 8, 4), (False, 2, 3)])
 def test_ep_overlapped_layer_matches_serial_bitwise(ep, f32_reduce, t, variant):
     """The overlapped exchange (rows gated per expert into gmm1, gmm2 pushing
     its rows to the token owners, local combine) gives the serial EP layer's
     bits, three steps in a row, on 4 emulated ranks with prefill-sized groups
     (~256 rows per expert: the CTA-pair kernel with 512-row tiles; ~192: the
-    CTA-pair kernel; ~64: the one-CTA kernel)."""
+    CTA-pair kernel; ~64: the one-CTA kernel) and decode-sized ones (~32, 16
+    and 4 rows: the mma.sync decode kernel with 32, 16 and 8-row tiles)."""
     import dw_tpu_b200 as dw
     from dw_tpu_b200 import _lib as L
     from dw_tpu_b200 import synthetic

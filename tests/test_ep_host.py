@@ -74,6 +74,8 @@ def test_gemm_variant_choice():
     assert gemm_variant("b200", 96) == 7
     assert gemm_variant("b200", 128) == 7
     assert gemm_variant("b200", 256) == 9
+    from dw_tpu_b200.ep import overlap_variant
+    assert [overlap_variant(r) for r in (4, 16, 32, 64, 128, 256)] == [3, 4, 5, 1, 7, 9]
 
 
 def _free_port():
