@@ -279,7 +279,7 @@ __device__ __forceinline__ void task_blocks(const Task& t, const Args& a, int& c
   }
 }
 
-template <int SD, int NT, int KS, int QB, bool SPLIT>
+template <int SD, int NT, int KS, int QB, bool SPLIT, bool EP>
 __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
     gmv_fp4_kernel(const __grid_constant__ CUtensorMap tm_lhs,
                    const __grid_constant__ CUtensorMap tm_codes,
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
   auto set_task = [&](int idx) {
     const Task t = get_task<NT>(idx, row_start, task_prefix, a);
     const bool act = a.act != DWM_ACT_NONE;
-    if (a.hk.gate_arrive != nullptr && t.g != gated) {
+    if (EP && a.hk.gate_arrive != nullptr && t.g != gated) {
       // Every source rank's rows of this expert have been stored here (and
       // made visible) before TMA reads them. A wait that runs out reports a
       // timeout; the stages then load whatever has arrived.
@@ -708,7 +708,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
           // row of its (token, k) pair (over NVLink for a peer).
           void* obase = a.out;
           int64_t orow = row;
-          if (a.hk.push_tags != nullptr) {
+          if (EP && a.hk.push_tags != nullptr) {
             const int tag = a.hk.push_tags[row];
             if (tag < 0) continue;
             obase = a.hk.push_base[tag >> kEpTagBits];
@@ -754,7 +754,7 @@ __global__ void __launch_bounds__(Cfg<SD, NT, KS, QB>::WARPS * 32, 1)
     for (uint32_t q = seq; q < issued; ++q)
       mbar_wait(&bars[q % S], (q / S) & 1, nullptr, a.status);
   }
-  if (a.hk.push_tags != nullptr) {
+  if (EP && a.hk.push_tags != nullptr) {
     // Every row this CTA stored precedes (bar.sync, then an acq_rel ticket at
     // gpu scope) the last CTA's ticket, which precedes its system-scope fence
     // and relaxed add to every rank: one fence covers all CTAs and ranks.
@@ -829,9 +829,14 @@ int launch_impl(const void* lhs, const void* codes, const void* scales, Args a,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  auto kernel = gmv_fp4_kernel<SD, NT, KS, QB, false>;
+  // Expert-parallel hooks (their own instance, so the plain kernel keeps its
+  // registers), or split-K pairs, or neither.
+  const bool ep = a.hk.gate_arrive != nullptr || a.hk.push_tags != nullptr;
+  if (ep) a.ksplit = 1;
+  auto kernel = ep ? gmv_fp4_kernel<SD, NT, KS, QB, false, true>
+                   : gmv_fp4_kernel<SD, NT, KS, QB, false, false>;
   if constexpr (C::SPLIT_OK)
-    if (a.ksplit == 2) kernel = gmv_fp4_kernel<SD, NT, KS, QB, true>;
+    if (a.ksplit == 2) kernel = gmv_fp4_kernel<SD, NT, KS, QB, true, false>;
   rc = set_smem_limit(reinterpret_cast<const void*>(kernel), C::ALLOC, "gmv smem attribute");
   if (rc) return rc;
   kernel<<<num_sms(), C::WARPS * 32, C::ALLOC, stream>>>(tm_lhs, tm_codes, tm_scales, a);
