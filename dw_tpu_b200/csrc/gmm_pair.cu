@@ -225,6 +225,13 @@ struct AccRing {
 // UMMA N of a tile: rows rounded up to 32 (each CTA's half a multiple of 16).
 __device__ __forceinline__ int tile_n(int rows) { return max(32, (rows + 31) & ~31); }
 
+// A 32-bit shared store that the compiler may schedule freely among the
+// other loads and stores (no memory clobber); volatile asm keeps it before
+// the proxy fence that publishes the stage.
+__device__ __forceinline__ void sts_b32_free(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -739,6 +746,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr int DELTA = decode_delta<SD>();
     const int gid = lane >> 2, tig = lane & 3;
     const DecodeRegs dregs = DecodeRegs::make();  // decode constants held in registers
+    // The lane's offset in a row pair of A: row gid of an 8-row swizzle atom,
+    // byte 4 tig of a 16-byte chunk, and the atom's XOR phase (gid) in the
+    // chunk bits, which the chunk index is XORed into.
+    const uint32_t lane_sw = (uint32_t)(gid * 128 + (gid << 4) + 4 * tig);
     uint32_t step = 0;
     bool ok = true;
     for (int idx = cl; idx < total && ok; idx += ncl) {
@@ -759,7 +770,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int bi = 0; bi < BLOCKS_PER_WARP; ++bi) {
           const int b = dw + NUM_DEC_WARPS * bi;
           const int p = act ? 2 * (b & 3) + (b >> 2) : b;
-          const int r0 = 16 * p + gid;  // A rows r0 and r0 + 8
           const uint8_t* cstage = smem + L::OFF_C + cs * C_STAGE + b * 512;
           // The codes' loads and table lookups first: they do not wait for
           // the scale multipliers, whose loads and shuffles then overlap them.
@@ -789,8 +799,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 m2[h][c] = 0u;
               }
             }
-          uint8_t* row_a = astage + (r0 >> 3) * 1024 + (r0 & 7) * 128;
-          uint8_t* row_b = astage + ((r0 + 8) >> 3) * 1024 + ((r0 + 8) & 7) * 128;
+          // Rows r0 = 16 p + gid and r0 + 8 sit 1 KiB apart in the same
+          // swizzle phase (gid), so one XOR of the 16-byte chunk index into
+          // the lane's base address serves both (the stage is 1 KiB aligned).
+          const uint32_t row_a = smem_u32(astage) + (uint32_t)(2 * p * 1024) + lane_sw;
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
             const int h = kb >> 1;
@@ -807,10 +819,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // k pair (16 kb + 2 tig) sits in 16-byte chunk 2 kb, k pair
             // (16 kb + 2 tig + 8) in chunk 2 kb + 1, both at byte 4 tig.
             const int c0 = 2 * kb, c1 = 2 * kb + 1;
-            *reinterpret_cast<uint32_t*>(row_a + ((c0 ^ (r0 & 7)) << 4) + 4 * tig) = v0;
-            *reinterpret_cast<uint32_t*>(row_b + ((c0 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v1;
-            *reinterpret_cast<uint32_t*>(row_a + ((c1 ^ (r0 & 7)) << 4) + 4 * tig) = v2;
-            *reinterpret_cast<uint32_t*>(row_b + ((c1 ^ ((r0 + 8) & 7)) << 4) + 4 * tig) = v3;
+            const uint32_t a0 = row_a ^ (uint32_t)(c0 << 4), a1 = row_a ^ (uint32_t)(c1 << 4);
+            sts_b32_free(a0, v0);
+            sts_b32_free(a0 + 1024, v1);
+            sts_b32_free(a1, v2);
+            sts_b32_free(a1 + 1024, v3);
           }
         }
         fence_proxy_async_smem();
